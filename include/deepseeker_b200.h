@@ -1,0 +1,184 @@
+/*
+ * deepseeker_b200 -- C ABI of the B200 (sm_100a) routed-expert MoE hot path.
+ *
+ * Every entry point:
+ *   - returns an int status (DS_OK = 0); the message of the last failure on
+ *     the calling thread is available from ds_last_error_string();
+ *   - takes DEVICE pointers for tensors (caller owns every buffer) unless the
+ *     name says otherwise, plain integer sizes, and a cudaStream_t passed as
+ *     `void* stream` (NULL = legacy default stream);
+ *   - launches asynchronously on that stream and never synchronises it;
+ *   - allocates nothing: scratch comes from a caller-provided workspace whose
+ *     size a matching *_workspace_size() call reports.
+ * The library is stateless and reentrant across distinct streams.
+ *
+ * Layout conventions (all row-major, K = input features contiguous):
+ *   FP4  : packed [N, K/2] u8, two e2m1 codes per byte, LOW nibble = even
+ *          element; scales [N, K/32] u8 (ue8m0: 2^(b-127), 0xFF = NaN).
+ *   Q3   : words [N, K*3/32] u32 (builder-defined 3-bit layout, see DESIGN),
+ *          scales / biases [N, K/64] f16; w = f32(scale)*q + f32(bias).
+ *   BF16 : [N, K] bf16.
+ *   Expert banks stack E experts: [E, N, ...] with the per-expert layout above.
+ */
+#ifndef DEEPSEEKER_B200_H
+#define DEEPSEEKER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define DS_OK 0
+#define DS_EINVAL 1   /* bad shape / dtype / argument                       */
+#define DS_EALIGN 2   /* pointer not aligned as the call requires            */
+#define DS_ERANGE 3   /* index out of range (host check or device guard)     */
+#define DS_ECUDA 4    /* CUDA runtime error                                  */
+#define DS_ETIMEOUT 5 /* a bounded device-side wait gave up                  */
+#define DS_ENOTSUP 6  /* unsupported combination                            */
+
+/* ---- element types ----------------------------------------------------- */
+#define DS_F32 0
+#define DS_BF16 1
+#define DS_F16 2
+#define DS_U8 3
+
+/* ---- weight formats ---------------------------------------------------- */
+#define DS_FMT_FP4 0
+#define DS_FMT_Q3 1
+#define DS_FMT_BF16 2
+
+/* ---- routing kinds ----------------------------------------------------- */
+#define DS_ROUTE_SOFTMAX 0      /* softmax over experts, top-k, renormalised  */
+#define DS_ROUTE_SQRTSOFTPLUS 1 /* sqrt(softplus(s)), top-k of s+bias, *scale */
+#define DS_ROUTE_SCORES 2       /* input already scores s: top-k of s+bias     */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ds_last_error_string(void);
+
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int ds_version(void);
+
+/* ------------------------------------------------------------------------
+ * FP4 e2m1 dequantisation, bit-exact with the reference table.
+ * Replaces metal_fp4.metal_dequant / the three Metal kernels
+ *   (reference: src/deepseeker/metal_fp4.py:28-66, 139-155) and
+ *   mlx_weights.dequant_fp4_rowmajor (src/deepseeker/mlx_weights.py:148-166).
+ * out[e] = FP4_TABLE[nibble(e)] * scale[e / 32] in f32 (round-to-nearest,
+ * no flush-to-zero), then stored as f32 or bf16 (RNE).
+ *   packed     : n_bytes u8 (n = 2*n_bytes elements)
+ *   scales     : n_scales entries, f32 (scale_kind = DS_F32) or raw ue8m0
+ *                bytes (scale_kind = DS_U8); n_scales must be ceil(n/32)
+ *   out        : n elements of out_dtype (DS_F32 or DS_BF16)
+ * ------------------------------------------------------------------------ */
+int ds_fp4_dequant(const uint8_t* packed, int64_t n_bytes, const void* scales,
+                   int scale_kind, int64_t n_scales, void* out, int out_dtype,
+                   void* stream);
+
+/* FP8 e4m3 with one ue8m0 scale per 32x32 block -> f32.
+ * Replaces mlx_weights.dequant_fp8_block (src/deepseeker/mlx_weights.py:82-89).
+ *   packed [rows, cols] u8, scales [rows/32, cols/32] u8, out [rows, cols] f32 */
+int ds_fp8_block_dequant(const uint8_t* packed, int64_t rows, int64_t cols,
+                         const uint8_t* scales, float* out, void* stream);
+
+/* 3-bit affine (group 64) dequantisation: out = f32(scale)*q + f32(bias)
+ * (multiply, then add: two roundings).  Replaces mx.dequantize(bits=3,
+ * group_size=64) at src/deepseeker/mlx_forward.py:99-101 and
+ * tests/test_q3.py:100-105.  cols % 64 == 0.
+ *   words [rows, cols*3/32] u32, scales/biases [rows, cols/64] f16,
+ *   out [rows, cols] of out_dtype (DS_F32 or DS_BF16) */
+int ds_q3_dequant(const uint32_t* words, const uint16_t* scales,
+                  const uint16_t* biases, int64_t rows, int64_t cols,
+                  void* out, int out_dtype, void* stream);
+
+/* 3-bit affine quantiser (builder rule: per-64 min/max, scale=(max-min)/7,
+ * bias=min, both rounded to f16, q=clamp(rint((w-bias)/scale),0,7)).
+ * Replaces mx.quantize(group_size=64, bits=3) in
+ * scripts/requant_experts_3bit.py:69-83 (convert_tensor).
+ *   w [rows, cols] f32 -> words [rows, cols*3/32], scales, biases [rows, cols/64] */
+int ds_q3_quantize(const float* w, int64_t rows, int64_t cols, uint32_t* words,
+                   uint16_t* scales, uint16_t* biases, void* stream);
+
+/* FP4 quantiser for synthetic weights (builder rule: per-32 block
+ * e = ceil(log2(amax/6)) clamped to [-127,127], RNE onto the e2m1 grid with
+ * ties to the even code).  The reference consumes pre-quantised checkpoints
+ * (no counterpart); used to build resident banks for tests and benches.
+ *   w [rows, cols] f32 -> packed [rows, cols/2] u8, scales [rows, cols/32] u8 */
+int ds_fp4_quantize(const float* w, int64_t rows, int64_t cols, uint8_t* packed,
+                    uint8_t* scales, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Router: per row, choose top_k experts and their gates.
+ *   kind = DS_ROUTE_SOFTMAX: softmax over n_experts logits, top-k (ties to the
+ *          lower id), gates renormalised to sum 1;
+ *   kind = DS_ROUTE_SQRTSOFTPLUS: s = sqrt(softplus(logit)), top-k of s+bias,
+ *          gates = s/(sum s + 1e-20) * route_scale
+ *          (src/deepseeker/mlx_forward.py:62-81, sqrtsoftplus_scores/route_topk);
+ *   kind = DS_ROUTE_SCORES: as SQRTSOFTPLUS with the input already the scores
+ *          s (route_topk alone, mlx_forward.py:68-81).
+ * Slots are written in descending selection-score order.
+ *   logits [rows, n_experts] f32; bias [n_experts] f32 or NULL;
+ *   ids [rows, top_k] i32; weights [rows, top_k] f32.  n_experts <= 1024,
+ *   top_k <= 32. */
+int ds_route_topk(const float* logits, const float* bias, int64_t rows,
+                  int n_experts, int top_k, int kind, float route_scale,
+                  int32_t* ids, float* weights, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Expert banks and the fused routed-expert MoE layer.
+ * ------------------------------------------------------------------------ */
+typedef struct DsExpertBank {
+  int32_t format;     /* DS_FMT_FP4, DS_FMT_Q3 or DS_FMT_BF16                 */
+  int32_t n_experts;  /* E                                                    */
+  int32_t rows;       /* N: output features                                  */
+  int32_t cols;       /* K: input features                                   */
+  const void* data;   /* FP4 [E,N,K/2] u8 | Q3 [E,N,K*3/32] u32 | BF16 [E,N,K] */
+  const void* scales; /* FP4 [E,N,K/32] u8 | Q3 [E,N,K/64] f16 | BF16 NULL     */
+  const void* biases; /* Q3 [E,N,K/64] f16 | otherwise NULL                   */
+} DsExpertBank;
+
+typedef struct DsMoeDesc {
+  int32_t hidden;       /* H                                                  */
+  int32_t inter;        /* I (routed intermediate size)                       */
+  int32_t n_experts;    /* E                                                  */
+  int32_t top_k;        /* k                                                  */
+  DsExpertBank w1;      /* gate: N = I, K = H                                 */
+  DsExpertBank w3;      /* up  : N = I, K = H                                 */
+  DsExpertBank w2;      /* down: N = H, K = I                                 */
+  /* optional shared expert, BF16 (NULL pointers = none)                      */
+  const void* shared_w1; /* [shared_inter, H] bf16                            */
+  const void* shared_w3; /* [shared_inter, H] bf16                            */
+  const void* shared_w2; /* [H, shared_inter] bf16                            */
+  int32_t shared_inter;
+  float swiglu_limit;    /* > 0: g = min(g, L), u = clip(u, -L, L); else none */
+  int32_t route_before_down; /* 1: h *= gate before the down projection
+                                (moe_layer, mlx_forward.py:404-405);
+                                0: y *= gate after it (grouped.py:50-53)       */
+} DsMoeDesc;
+
+/* Workspace bytes ds_moe_decode needs for `tokens` rows. */
+int ds_moe_decode_workspace_size(const DsMoeDesc* desc, int64_t tokens,
+                                 size_t* bytes);
+
+/* Fused routed-expert MoE layer for decode (tokens <= 8): for every distinct
+ * routed expert e (ascending id), h = silu(min(x W1e^T, L)) * clip(x W3e^T, ±L)
+ * (f32, weights dequantised in registers), scaled by the token's gate, then
+ * out += h W2e^T; plus the shared expert (its output rounded to bf16 before
+ * the add, as the reference does); out has the dtype of x.
+ * Replaces moe_layer's expert loop + qmm + shared add
+ *   (src/deepseeker/mlx_forward.py:84-103, 388-419;
+ *    src/deepseeker/mlx_runner.py:776-781).
+ *   x [tokens, H] of x_dtype (DS_BF16, or DS_F32 for the f32 oracle config);
+ *   topk_ids [tokens, k] i32 (-1 = dropped slot); topk_w [tokens, k] f32;
+ *   out [tokens, H] of x_dtype. */
+int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens,
+                  const int32_t* topk_ids, const float* topk_w, void* out,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DEEPSEEKER_B200_H */
