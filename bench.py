@@ -207,11 +207,12 @@ def run_ours(args) -> dict:
         if ev is not None:
             ev[1].record(stream)
 
+    min_warm_s = 0.0 if args.quick else 1.0
     with ClockSampler(local) as clk:
         # warm-up: at least W steps and at least ~1 s so clocks settle and get sampled
         t0 = time.perf_counter()
         i = 0
-        while i < args.warmup or time.perf_counter() - t0 < 1.0:
+        while i < args.warmup or time.perf_counter() - t0 < min_warm_s:
             step(i % (total_steps + 64))
             i += 1
             if i % 256 == 0:
@@ -237,7 +238,7 @@ def run_ours(args) -> dict:
         # keep the GPU busy a little longer so the sampler sees the load
         t1 = time.perf_counter()
         j = 0
-        while time.perf_counter() - t1 < 0.6:
+        while time.perf_counter() - t1 < (0.0 if args.quick else 0.6):
             step(j % (total_steps + 64))
             j += 1
             if j % 256 == 0:
@@ -246,6 +247,7 @@ def run_ours(args) -> dict:
     clocks = clk.summary()
 
     # ---- e2e: public API with host buffers, every step synchronised
+    e2e_steps = 0 if args.quick else args.steps
     pin_x = torch.empty(args.steps, tokens, H, dtype=torch.bfloat16).pin_memory()
     pin_l = torch.empty(args.steps, tokens, E, dtype=torch.float32).pin_memory()
     pin_o = torch.empty(args.steps, tokens, H, dtype=torch.bfloat16).pin_memory()
@@ -262,18 +264,18 @@ def run_ours(args) -> dict:
         moe.moe_decode(dx, layers[s % L], ids, w, out=do, workspace=ws)
         pin_o[s].copy_(do, non_blocking=True)
         stream.synchronize()
-    for s in range(min(args.warmup, args.steps)):
+    for s in range(min(args.warmup, e2e_steps)):
         e2e_step(s)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for s in range(args.steps):
+    for s in range(e2e_steps):
         e2e_step(s)
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = max(e0.elapsed_time(e1), 1e-9)
 
     # per-step algorithmic bytes: distinct experts x expert bytes + shared + x/out/route traffic
     per_expert = sum(b.nbytes() // E for b in (layers[0].w1, layers[0].w3, layers[0].w2))
@@ -334,6 +336,8 @@ def main() -> int:
     ap.add_argument("--config", choices=["c2", "c3"], default="c2")
     ap.add_argument("--layers", type=int, default=8, help="distinct resident layers rotated (L2-cold)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="profiling runs: no time-based warm-up, no e2e / CPU-baseline legs")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
 
@@ -356,7 +360,7 @@ def main() -> int:
 
     result = run_ours(args)
     if rank == 0 and result is not None:
-        if not args.no_cpu_baseline and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        if not (args.no_cpu_baseline or args.quick) and int(os.environ.get("WORLD_SIZE", "1")) == 1:
             value, cores, sample = time_reference(steps=1000, warmup=1, budget_s=15.0)
             result["cpu_baseline"] = {"value": round(value, 4), "unit": "tokens/s", "cores": cores,
                                       "kind": "port", "sample": sample}

@@ -21,31 +21,21 @@
 //
 // Weight loads use the streaming cache hint (__ldcs): every weight byte is
 // read exactly once per layer.
-#include "ds_common.cuh"
+#include <stdlib.h>
+
+#include "moe_decode.cuh"
 
 namespace {
+
+using ds::decode::DecodeArgs;
+using ds::decode::kMaxEntries;
+using ds::decode::kMaxTokens;
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRowsPerWarp = 2;
 constexpr int kRowsPerItem = kWarps * kRowsPerWarp;  // 16
-constexpr int kMaxTokens = 8;
-constexpr int kMaxEntries = 128;                     // tokens * top_k
 constexpr int kSmemBudget = 200 * 1024;              // dynamic smem cap per CTA
-
-struct DecodeArgs {
-  DsMoeDesc d;
-  const void* x;           // [T, H] bf16 or f32 (x_f32)
-  int x_f32;               // 1: x and out are f32; 0: bf16
-  int tokens;
-  const int32_t* ids;      // [T, k]
-  const float* gates;      // [T, k]
-  void* out;               // [T, H], dtype of x
-  float* h;                // [max_slots + 1][T][h_stride]
-  int max_slots;           // routed slots reserved = min(T*k, E)
-  int h_stride;            // max(I, shared_inter), multiple of 4
-  int* err;                // device error word (bit 0: expert id out of range)
-};
 
 struct Slots {
   int count;
@@ -820,5 +810,13 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
   a.h_stride = w.h_stride;
   a.err = reinterpret_cast<int*>(static_cast<char*>(workspace) + w.err_off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Single-token FP4 layers take the pipelined tensor-core kernels; the
+  // environment variable DEEPSEEKER_DECODE_GENERIC=1 forces the generic
+  // kernels (used by the tests to cross-check the two implementations).
+  static const bool force_generic = [] {
+    const char* v = getenv("DEEPSEEKER_DECODE_GENERIC");
+    return v != nullptr && v[0] == '1';
+  }();
+  if (!force_generic && ds::decode::tc_supported(a)) return ds::decode::launch_tc(a, s);
   return desc->w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
 }

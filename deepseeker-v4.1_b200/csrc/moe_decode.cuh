@@ -1,0 +1,37 @@
+// Shared definitions of the decode MoE kernels (moe_decode.cu: generic path,
+// moe_decode_tc.cu: single-token tensor-core pipeline).
+#pragma once
+
+#include "ds_common.cuh"
+
+namespace ds {
+namespace decode {
+
+constexpr int kMaxTokens = 8;
+constexpr int kMaxEntries = 128;  // tokens * top_k
+
+// Error bits written to the workspace error word.
+constexpr int kErrExpertRange = 1;
+constexpr int kErrWaitTimeout = 2;
+
+struct DecodeArgs {
+  DsMoeDesc d;
+  const void* x;      // [T, H] bf16 or f32 (x_f32)
+  int x_f32;          // 1: x and out are f32; 0: bf16
+  int tokens;
+  const int32_t* ids; // [T, k]
+  const float* gates; // [T, k]
+  void* out;          // [T, H], dtype of x
+  float* h;           // [max_slots + 1][T][h_stride] f32
+  int max_slots;      // routed slots reserved = min(T*k, E)
+  int h_stride;       // max(I, shared_inter), multiple of 4
+  int* err;           // device error word
+};
+
+// Single-token tensor-core pipeline (moe_decode_tc.cu).  Returns true and
+// launches when the geometry is supported; false means "use the generic path".
+bool tc_supported(const DecodeArgs& a);
+int launch_tc(const DecodeArgs& a, cudaStream_t st);
+
+}  // namespace decode
+}  // namespace ds

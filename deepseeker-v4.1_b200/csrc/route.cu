@@ -1,8 +1,7 @@
 // Router: per token, select top_k experts and their gates.
 //
-// One CTA per row.  Selection is k rounds of a block-wide arg-max over the
-// row's keys held in shared memory (n_experts <= 1024, top_k <= 32), so the
-// slot order is descending key.  Tie-breaking follows each reference:
+// Selection is k rounds of a warp-wide arg-max over the row's keys
+// (n_experts <= 1024, top_k <= 32), so the slot order is descending key.  Tie-breaking follows each reference:
 //   softmax       : descending probability, ties -> lower id
 //                   (torch.argsort(-p, stable=True) restatement);
 //   sqrt-softplus : the reference takes the LAST top_k of an ascending stable
@@ -14,7 +13,6 @@
 
 namespace {
 
-constexpr int kRouteThreads = 256;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 32;
 
@@ -32,104 +30,99 @@ __device__ __forceinline__ bool beats(const KeyIdx& a, const KeyIdx& b, bool tie
   return ties_high ? (a.idx > b.idx) : (a.idx < b.idx);
 }
 
-__global__ void __launch_bounds__(kRouteThreads)
+// One warp per row: each lane holds n_experts/32 keys in registers; k rounds
+// of a shuffle arg-max pick the experts.  The kernel first lets the next
+// kernel on the stream (the MoE layer, launched with programmatic stream
+// serialisation) start its prologue; that kernel waits for this one before
+// reading the routing.
+__global__ void __launch_bounds__(32)
 route_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int n_experts,
                   int top_k, int kind, float route_scale, int32_t* __restrict__ ids,
                   float* __restrict__ weights) {
-  __shared__ float key[kMaxExperts];
-  __shared__ float val[kMaxExperts];   // softmax: exp(l - max); sqrtsoftplus: s
-  __shared__ KeyIdx warp_best[kRouteThreads / 32];
-  __shared__ float red[kRouteThreads / 32];
-  __shared__ int chosen[kMaxTopK];
-  __shared__ float total_s;
-
-  const int row = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  constexpr int kPer = kMaxExperts / 32;
+  const int row = blockIdx.x, lane = threadIdx.x;
   const float* lg = logits + (int64_t)row * n_experts;
   const bool ties_high = (kind != DS_ROUTE_SOFTMAX);
-
-  // ---- keys
-  float local_max = -INFINITY;
-  for (int e = tid; e < n_experts; e += kRouteThreads) {
-    const float l = lg[e];
-    if (kind == DS_ROUTE_SOFTMAX) {
-      key[e] = l;
-      local_max = fmaxf(local_max, l);
-    } else {
-      // softplus(l) = logaddexp(l, 0) = max(l, 0) + log1p(exp(-|l|))
-      const float s = (kind == DS_ROUTE_SCORES) ? l : sqrtf(fmaxf(l, 0.0f) + log1pf(expf(-fabsf(l))));
-      val[e] = s;
-      key[e] = s + (bias ? bias[e] : 0.0f);
+  const float qnan = __uint_as_float(0x7FC00000u);
+  float key[kPer], val[kPer];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane + 32 * j;
+    key[j] = qnan;
+    val[j] = 0.0f;
+    if (e < n_experts) {
+      const float l = lg[e];
+      if (kind == DS_ROUTE_SOFTMAX) {
+        val[j] = l;
+        mx = fmaxf(mx, l);
+      } else {
+        // softplus(l) = logaddexp(l, 0) = max(l, 0) + log1p(exp(-|l|))
+        const float sc = (kind == DS_ROUTE_SCORES) ? l : sqrtf(fmaxf(l, 0.0f) + log1pf(expf(-fabsf(l))));
+        val[j] = sc;
+        key[j] = sc + (bias ? bias[e] : 0.0f);
+      }
     }
   }
   if (kind == DS_ROUTE_SOFTMAX) {
-    for (int o = 16; o; o >>= 1) local_max = fmaxf(local_max, __shfl_xor_sync(0xffffffffu, local_max, o));
-    if (lane == 0) red[warp] = local_max;
-    __syncthreads();
-    float mx = red[0];
-    for (int w = 1; w < kRouteThreads / 32; ++w) mx = fmaxf(mx, red[w]);
-    __syncthreads();
-    float local_sum = 0.0f;
-    for (int e = tid; e < n_experts; e += kRouteThreads) {
-      const float p = expf(key[e] - mx);
-      val[e] = p;
-      local_sum += p;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      if (lane + 32 * j < n_experts) {
+        val[j] = expf(val[j] - mx);
+        sum += val[j];
+      }
     }
-    for (int o = 16; o; o >>= 1) local_sum += __shfl_xor_sync(0xffffffffu, local_sum, o);
-    if (lane == 0) red[warp] = local_sum;
-    __syncthreads();
-    if (tid == 0) {
-      float s = 0.0f;
-      for (int w = 0; w < kRouteThreads / 32; ++w) s += red[w];
-      total_s = s;
-    }
-    __syncthreads();
-    // probabilities become the selection key (ties on p -> lower id)
-    for (int e = tid; e < n_experts; e += kRouteThreads) {
-      const float p = val[e] / total_s;
-      val[e] = p;
-      key[e] = p;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      if (lane + 32 * j < n_experts) {
+        val[j] = val[j] / sum;  // probability: the selection key (ties -> lower id)
+        key[j] = val[j];
+      }
     }
   }
-  __syncthreads();
-
-  // ---- k rounds of arg-max
+  float chosen_val = 0.0f, total = 0.0f;  // lane r keeps slot r
+  int chosen_id = -1;
   for (int r = 0; r < top_k; ++r) {
     KeyIdx best{-INFINITY, -1};
-    for (int e = tid; e < n_experts; e += kRouteThreads) {
-      KeyIdx c{key[e], e};
-      if (!(c.key == c.key)) continue;  // NaN never selected
-      if (beats(c, best, ties_high)) best = c;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      KeyIdx c{key[j], lane + 32 * j};
+      if (c.key == c.key && beats(c, best, ties_high)) best = c;
     }
+#pragma unroll
     for (int o = 16; o; o >>= 1) {
       KeyIdx other{__shfl_xor_sync(0xffffffffu, best.key, o), __shfl_xor_sync(0xffffffffu, best.idx, o)};
       if (beats(other, best, ties_high)) best = other;
     }
-    if (lane == 0) warp_best[warp] = best;
-    __syncthreads();
-    if (tid == 0) {
-      KeyIdx b = warp_best[0];
-      for (int w = 1; w < kRouteThreads / 32; ++w)
-        if (beats(warp_best[w], b, ties_high)) b = warp_best[w];
-      chosen[r] = b.idx;
-      if (b.idx >= 0) key[b.idx] = __uint_as_float(0x7FC00000u);  // remove (NaN)
+    float v = 0.0f;
+    if (best.idx >= 0 && (best.idx & 31) == lane) {
+      const int j = best.idx >> 5;
+#pragma unroll
+      for (int q = 0; q < kPer; ++q)
+        if (q == j) {
+          v = val[q];
+          key[q] = qnan;  // remove
+        }
     }
-    __syncthreads();
+    v = __shfl_sync(0xffffffffu, v, best.idx >= 0 ? (best.idx & 31) : 0);
+    if (best.idx >= 0) total += v;
+    if (lane == r) {
+      chosen_id = best.idx;
+      chosen_val = best.idx >= 0 ? v : 0.0f;
+    }
   }
-
-  // ---- gates
-  if (tid == 0) {
-    float s = 0.0f;
-    for (int r = 0; r < top_k; ++r) s += (chosen[r] >= 0) ? val[chosen[r]] : 0.0f;
-    for (int r = 0; r < top_k; ++r) {
-      const int e = chosen[r];
-      float w = 0.0f;
-      if (e >= 0) {
-        w = (kind == DS_ROUTE_SOFTMAX) ? val[e] / s : (val[e] / (s + 1e-20f)) * route_scale;
-      }
-      ids[(int64_t)row * top_k + r] = e;
-      weights[(int64_t)row * top_k + r] = w;
-    }
+  if (lane < top_k) {
+    float w = 0.0f;
+    if (chosen_id >= 0)
+      w = (kind == DS_ROUTE_SOFTMAX) ? chosen_val / total : (chosen_val / (total + 1e-20f)) * route_scale;
+    ids[(int64_t)row * top_k + lane] = chosen_id;
+    weights[(int64_t)row * top_k + lane] = w;
   }
 }
 
@@ -148,7 +141,7 @@ extern "C" int ds_route_topk(const float* logits, const float* bias, int64_t row
   if (rows == 0) return DS_OK;
   DS_REQUIRE(rows <= 0x7fffffff, DS_EINVAL, "route_topk: too many rows");
   DS_REQUIRE(logits && ids && weights, DS_EINVAL, "route_topk: null pointer");
-  route_topk_kernel<<<(unsigned)rows, kRouteThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  route_topk_kernel<<<(unsigned)rows, 32, 0, static_cast<cudaStream_t>(stream)>>>(
       logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
   DS_CHECK_LAUNCH("route_topk_kernel");
   return DS_OK;

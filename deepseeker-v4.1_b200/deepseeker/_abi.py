@@ -18,7 +18,7 @@ DS_F32, DS_BF16, DS_F16, DS_U8 = range(4)
 # weight formats
 DS_FMT_FP4, DS_FMT_Q3, DS_FMT_BF16 = range(3)
 # routing kinds
-DS_ROUTE_SOFTMAX, DS_ROUTE_SQRTSOFTPLUS = 0, 1
+DS_ROUTE_SOFTMAX, DS_ROUTE_SQRTSOFTPLUS, DS_ROUTE_SCORES = 0, 1, 2
 
 
 class DsExpertBank(Structure):
