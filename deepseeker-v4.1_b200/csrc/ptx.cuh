@@ -52,12 +52,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Bounded wait: gives up after `limit_ns` of wall time and returns false.
+// The timer is read only every 1024 polls so that a waiting warp notices the
+// phase flip promptly.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) return false;
+    if ((i & 1023u) == 0u) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > limit_ns) return false;
+    }
   }
 }
 
@@ -71,6 +77,38 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Tiled tensor copies (no multicast): box described by a CUtensorMap that
+// lives in kernel parameter / constant / global memory.  The x coordinate
+// (innermost, in elements) must be 16-byte aligned; all callers use x = 0.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const void* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Byte offset of (row r, byte x of the row) inside a 3-D box [128 B][R rows]
+// [chunks] written with CU_TENSOR_MAP_SWIZZLE_128B: 128-byte line
+// (x / 128) * R + r, 16-byte chunk index XOR-ed with the line index mod 8.
+// The box must start on a 1024-byte boundary.
+__device__ __forceinline__ uint32_t swz128(int r, int x, int R) {
+  const int line = (x >> 7) * R + r;
+  return (uint32_t)(line * 128 + ((((x >> 4) & 7) ^ (line & 7)) << 4) + (x & 15));
 }
 
 // ---------------------------------------------------------------- PDL
