@@ -187,15 +187,15 @@ struct ListA {
 // word t of the 16-byte block of both rows; the codes map to the MMA k slots
 // (2t, 2t+1, 2t+8, 2t+9) of two k16 steps, and the B fragment carries the
 // activations of the same K positions (8t .. 8t+7 of the block).
-__device__ __forceinline__ void fp4_word_mma(uint32_t wg, uint32_t w8, uint4 bv, float (&d)[4]) {
+__device__ __forceinline__ void fp4_word_mma(uint32_t wg, uint32_t w8, uint4 bv, float (&d0)[4], float (&d1)[4]) {
   uint32_t hg[4], h8[4];
   e2m1x8_to_f16x2(wg, hg);
   e2m1x8_to_f16x2(w8, h8);
   const uint32_t a0[4] = {hg[0], h8[0], hg[1], h8[1]};
   const uint32_t a1[4] = {hg[2], h8[2], hg[3], h8[3]};
   const float z[4] = {0.f, 0.f, 0.f, 0.f};
-  mma_f16(d, a0, bv.x, bv.y, z);
-  mma_f16(d, a1, bv.z, bv.w, d);
+  mma_f16(d0, a0, bv.x, bv.y, z);  // two independent k16 halves: no MMA -> MMA dependency
+  mma_f16(d1, a1, bv.z, bv.w, z);
 }
 
 // ue8m0 byte i (0..3) of w -> 2^(b-127), valid for b in 1..254 (exponent field
@@ -398,16 +398,34 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_gate_up(const __grid_const
         const uint2 sg = *reinterpret_cast<const uint2*>(s1 + gq * srow + bg);
         const uint2 su = *reinterpret_cast<const uint2*>(s3 + gq * srow + bg);
         const bool exact = __any_sync(0xffffffffu, has_special_byte(sg) || has_special_byte(su));
+        // two batches of 4 blocks: all shared-memory loads of a batch are
+        // issued before its conversions and MMAs (independent chains)
 #pragma unroll
-        for (int bb = 0; bb < 8; ++bb) {
-          const uint32_t off = rowoff ^ (uint32_t)(bb << 4);
-          const uint32_t wg = *reinterpret_cast<const uint32_t*>(top + off);
-          const uint32_t w8 = *reinterpret_cast<const uint32_t*>(bot + off);
-          const uint4 xv = *reinterpret_cast<const uint4*>(x16 + (bg + bb) * 32 + t * 8);
-          float d[4];
-          fp4_word_mma(wg, w8, xv, d);
-          acc0 = fmaf(scale_at(sg, bb, exact), d[0], acc0);
-          acc2 = fmaf(scale_at(su, bb, exact), d[2], acc2);
+        for (int h4 = 0; h4 < 8; h4 += 4) {
+          uint32_t wg[4], w8[4];
+          uint4 xv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t off = rowoff ^ (uint32_t)((h4 + q) << 4);
+            wg[q] = *reinterpret_cast<const uint32_t*>(top + off);
+            w8[q] = *reinterpret_cast<const uint32_t*>(bot + off);
+            xv[q] = *reinterpret_cast<const uint4*>(x16 + (bg + h4 + q) * 32 + t * 8);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float d0[4], d1[4];
+            fp4_word_mma(wg[q], w8[q], xv[q], d0, d1);
+            float sgv, suv;
+            if (!exact) {
+              sgv = scale_fast(h4 == 0 ? sg.x : sg.y, q);
+              suv = scale_fast(h4 == 0 ? su.x : su.y, q);
+            } else {
+              sgv = scale_at(sg, h4 + q, true);
+              suv = scale_at(su, h4 + q, true);
+            }
+            acc0 = fmaf(sgv, d0[0] + d1[0], acc0);
+            acc2 = fmaf(suv, d0[2] + d1[2], acc2);
+          }
         }
       }
     }
@@ -545,11 +563,28 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_down(const __grid_constant
   __half* hh = reinterpret_cast<__half*>(smem + g.b_hh_off);   // [slot][I]
   __half* hl = reinterpret_cast<__half*>(smem + g.b_hl_off);   // [slot][I]
   __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(smem + g.b_sh_off);  // [2][Is] hi, lo
-  // h rows are h_stride apart; I is a multiple of 4, so float4 loads never
-  // straddle two slots.  Pass 1 takes the max, pass 2 (L1/L2 hits) converts.
+  // h rows are h_stride apart and I is a multiple of 4, so a float4 never
+  // straddles two slots.  Each thread keeps up to kHVec float4 of h in
+  // registers (one global round trip), the block agrees on max|h|, and the
+  // registers are converted to f16 hi/lo; larger D * I falls back to a
+  // second (L2-hit) pass.
+  constexpr int kHVec = 8;
   const int nvec = D * g.I / 4;
+  float4 hv4[kHVec];
   float m = 0.f;
-  for (int v = tid; v < nvec; v += kConsumerThreads) {
+#pragma unroll
+  for (int r = 0; r < kHVec; ++r) {
+    const int v = tid + r * kConsumerThreads;
+    hv4[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (v < nvec) {
+      const int k = 4 * v, s = k / g.I, c = k - s * g.I;
+      hv4[r] = *reinterpret_cast<const float4*>(a.h + (size_t)s * a.h_stride + c);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kHVec; ++r)
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(hv4[r].x), fabsf(hv4[r].y)), fmaxf(fabsf(hv4[r].z), fabsf(hv4[r].w))));
+  for (int v = tid + kHVec * kConsumerThreads; v < nvec; v += kConsumerThreads) {
     const int k = 4 * v, s = k / g.I, c = k - s * g.I;
     const float4 f = *reinterpret_cast<const float4*>(a.h + (size_t)s * a.h_stride + c);
     m = fmaxf(m, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
@@ -563,16 +598,28 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_down(const __grid_constant
   for (int w = 0; w < kCW; ++w) mx = fmaxf(mx, hred[w]);
   const int pe = (mx > 0.f && isfinite(mx)) ? 14 - ilogbf(mx) : 0;
   const float hsc = ldexpf(1.0f, pe), hinv = ldexpf(1.0f, -pe);
-  for (int v = tid; v < nvec; v += kConsumerThreads) {
-    const int k = 4 * v, s = k / g.I, c = k - s * g.I;
-    const float4 f = *reinterpret_cast<const float4*>(a.h + (size_t)s * a.h_stride + c);
+  auto store_hilo = [&](int k, float4 f) {
     const float fv[4] = {f.x * hsc, f.y * hsc, f.z * hsc, f.w * hsc};
+    uint32_t hi2[2], lo2[2];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const __half hi = __float2half_rn(fv[e]);
-      hh[k + e] = hi;
-      hl[k + e] = __float2half_rn(fv[e] - __half2float(hi));
+    for (int e = 0; e < 2; ++e) {
+      const __half2 hi = __floats2half2_rn(fv[2 * e], fv[2 * e + 1]);
+      const float2 hf = __half22float2(hi);
+      const __half2 lo = __floats2half2_rn(fv[2 * e] - hf.x, fv[2 * e + 1] - hf.y);
+      hi2[e] = *reinterpret_cast<const uint32_t*>(&hi);
+      lo2[e] = *reinterpret_cast<const uint32_t*>(&lo);
     }
+    *reinterpret_cast<uint2*>(hh + k) = make_uint2(hi2[0], hi2[1]);
+    *reinterpret_cast<uint2*>(hl + k) = make_uint2(lo2[0], lo2[1]);
+  };
+#pragma unroll
+  for (int r = 0; r < kHVec; ++r) {
+    const int v = tid + r * kConsumerThreads;
+    if (v < nvec) store_hilo(4 * v, hv4[r]);
+  }
+  for (int v = tid + kHVec * kConsumerThreads; v < nvec; v += kConsumerThreads) {
+    const int k = 4 * v, s = k / g.I, c = k - s * g.I;
+    store_hilo(k, *reinterpret_cast<const float4*>(a.h + (size_t)s * a.h_stride + c));
   }
   if (g.shared) {
     for (int k = tid; k < g.Is; k += kConsumerThreads) {
@@ -617,18 +664,33 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_down(const __grid_constant
           const uint2 s8v = *reinterpret_cast<const uint2*>(sc + (gq + 8) * srow + bg);
           const bool exact = __any_sync(0xffffffffu, has_special_byte(s0v) || has_special_byte(s8v));
 #pragma unroll
-          for (int bb = 0; bb < 8; ++bb) {
-            const uint32_t off = rowoff ^ (uint32_t)(bb << 4);
-            const uint32_t wg = *reinterpret_cast<const uint32_t*>(dat + off);
-            const uint32_t w8 = *reinterpret_cast<const uint32_t*>(dat + off + 8 * 128);
-            const uint4 hv = *reinterpret_cast<const uint4*>(hsrc + (bg + bb) * 32 + t * 8);
-            float d[4];
-            fp4_word_mma(wg, w8, hv, d);
-            const float s0 = scale_at(s0v, bb, exact), s8 = scale_at(s8v, bb, exact);
-            acc[0] = fmaf(s0, d[0], acc[0]);
-            acc[1] = fmaf(s0, d[1], acc[1]);
-            acc[2] = fmaf(s8, d[2], acc[2]);
-            acc[3] = fmaf(s8, d[3], acc[3]);
+          for (int h4 = 0; h4 < 8; h4 += 4) {
+            uint32_t wg[4], w8[4];
+            uint4 hv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t off = rowoff ^ (uint32_t)((h4 + q) << 4);
+              wg[q] = *reinterpret_cast<const uint32_t*>(dat + off);
+              w8[q] = *reinterpret_cast<const uint32_t*>(dat + off + 8 * 128);
+              hv[q] = *reinterpret_cast<const uint4*>(hsrc + (bg + h4 + q) * 32 + t * 8);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float d0[4], d1[4];
+              fp4_word_mma(wg[q], w8[q], hv[q], d0, d1);
+              float s0, s8;
+              if (!exact) {
+                s0 = scale_fast(h4 == 0 ? s0v.x : s0v.y, q);
+                s8 = scale_fast(h4 == 0 ? s8v.x : s8v.y, q);
+              } else {
+                s0 = scale_at(s0v, h4 + q, true);
+                s8 = scale_at(s8v, h4 + q, true);
+              }
+              acc[0] = fmaf(s0, d0[0] + d1[0], acc[0]);
+              acc[1] = fmaf(s0, d0[1] + d1[1], acc[1]);
+              acc[2] = fmaf(s8, d0[2] + d1[2], acc[2]);
+              acc[3] = fmaf(s8, d0[3] + d1[3], acc[3]);
+            }
           }
         }
       }
