@@ -23,6 +23,8 @@
 // read exactly once per layer.
 #include <stdlib.h>
 
+#include <mutex>
+
 #include "moe_decode.cuh"
 
 namespace {
@@ -818,5 +820,88 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
     return v != nullptr && v[0] == '1';
   }();
   if (!force_generic && ds::decode::tc_supported(a)) return ds::decode::launch_tc(a, s);
+  return desc->w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
+}
+
+// ============================================================== no-allocation variant
+//
+// Some callers cannot hand the library a workspace: a serving loop whose
+// device memory is carved up once at start-up by its own pool (and whose pool
+// may not be touched from the decode thread), or a host thread that runs
+// between stream-ordered allocator phases and must not trigger an
+// allocation, implicit or not.  ds_moe_decode_noalloc takes its scratch
+// from a file-scope __device__ array instead: the CUDA runtime reserves it
+// when the module is loaded, so the call itself allocates nothing on the
+// device or the host heap (tensor maps are encoded on the stack per call).
+
+namespace {
+
+// Scratch limit: 8 MiB.  A call needs 256 + (slots + 1) * tokens * stride * 4
+// bytes (slots = min(tokens * k, experts), stride = max(inter, shared_inter)):
+// one token fits for any k <= 32 with stride <= 8192, eight tokens of a top-8
+// layer fit with stride <= 4032.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device, resolved once
+// per device (the first call on a device does this setup).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  DS_CHECK_CUDA(cudaGetDevice(&dev));
+  DS_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, DS_EINVAL, "moe_decode_noalloc: device %d beyond %d", dev,
+             kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    DS_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    DS_REQUIRE(p != nullptr && ds::aligned(p, 256), DS_ECUDA, "moe_decode_noalloc: bad scratch address");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DS_OK;
+}
+
+}  // namespace
+
+extern "C" size_t ds_moe_decode_noalloc_max_scratch(void) { return kNoAllocScratchBytes; }
+
+extern "C" int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens,
+                                     const int32_t* topk_ids, const float* topk_w, void* out, void* stream) {
+  int st = validate(desc, tokens);
+  if (st != DS_OK) return st;
+  DS_REQUIRE(x && topk_ids && topk_w && out, DS_EINVAL, "moe_decode_noalloc: null pointer");
+  DS_REQUIRE(x_dtype == DS_BF16 || x_dtype == DS_F32, DS_EINVAL,
+             "moe_decode_noalloc: x_dtype must be DS_BF16 or DS_F32");
+  DS_REQUIRE(ds::aligned(x, 16) && ds::aligned(out, 4), DS_EALIGN,
+             "moe_decode_noalloc: x 16-byte and out 4-byte aligned");
+  const WsLayout w = ws_layout(desc, tokens);
+  DS_REQUIRE(w.total <= kNoAllocScratchBytes, DS_ERANGE,
+             "moe_decode_noalloc: this layer needs %zu bytes of scratch, the static limit is %zu "
+             "(use ds_moe_decode with a workspace)",
+             w.total, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if ((st = noalloc_scratch(&scratch)) != DS_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The error word is the only scratch that must start at zero (every h row
+  // the kernels read is written earlier in the same call); clear it on the
+  // stream so that it reports this call alone.
+  DS_CHECK_CUDA(cudaMemsetAsync(static_cast<char*>(scratch) + w.err_off, 0, sizeof(int), s));
+  DecodeArgs a;
+  a.d = *desc;
+  a.x = x;
+  a.x_f32 = x_dtype == DS_F32;
+  a.tokens = (int)tokens;
+  a.ids = topk_ids;
+  a.gates = topk_w;
+  a.out = out;
+  a.h = reinterpret_cast<float*>(static_cast<char*>(scratch) + w.h_off);
+  a.max_slots = w.max_slots;
+  a.h_stride = w.h_stride;
+  a.err = reinterpret_cast<int*>(static_cast<char*>(scratch) + w.err_off);
+  if (ds::decode::tc_supported(a)) return ds::decode::launch_tc_uncached(a, s);
   return desc->w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
 }

@@ -32,6 +32,9 @@ struct DecodeArgs {
 // launches when the geometry is supported; false means "use the generic path".
 bool tc_supported(const DecodeArgs& a);
 int launch_tc(const DecodeArgs& a, cudaStream_t st);
+// Same launch, tensor maps encoded on the stack for this call only (no cache,
+// so no host heap either).
+int launch_tc_uncached(const DecodeArgs& a, cudaStream_t st);
 
 }  // namespace decode
 }  // namespace ds

@@ -838,6 +838,28 @@ struct Maps {
   CUtensorMap w1d, w3d, w1s, w3s, sw1, sw3, w2d, w2s, sw2;
 };
 
+// Encode the tensor maps of a layer (pure host work, no allocation).
+int encode_maps(const DecodeArgs& a, Maps& m) {
+  const DsMoeDesc& d = a.d;
+  DS_REQUIRE(encode_fn() != nullptr, DS_ECUDA, "moe_decode: cuTensorMapEncodeTiled unavailable");
+  memset(&m, 0, sizeof(m));
+  const uint64_t E = d.n_experts, H = d.hidden, I = d.inter;
+  bool ok = map_rows_swizzled(&m.w1d, d.w1.data, E * I, H / 2, 8, H / 256) &&
+            map_rows_swizzled(&m.w3d, d.w3.data, E * I, H / 2, 8, H / 256) &&
+            map_rows_plain(&m.w1s, d.w1.scales, E * I, H / 32, 8) &&
+            map_rows_plain(&m.w3s, d.w3.scales, E * I, H / 32, 8) &&
+            map_rows_swizzled(&m.w2d, d.w2.data, E * H, I / 2, 16, I / 256) &&
+            map_rows_plain(&m.w2s, d.w2.scales, E * H, I / 32, 16);
+  if (ok && d.shared_w1) {
+    const uint64_t Is = d.shared_inter;
+    ok = map_rows_swizzled(&m.sw1, d.shared_w1, Is, H * 2, 8, 16) &&
+         map_rows_swizzled(&m.sw3, d.shared_w3, Is, H * 2, 8, 16) &&
+         map_rows_swizzled(&m.sw2, d.shared_w2, H, Is * 2, 16, 16);
+  }
+  DS_REQUIRE(ok, DS_ECUDA, "moe_decode: tensor map encoding failed");
+  return DS_OK;
+}
+
 // Encode (or fetch cached) tensor maps for a layer.  Resident banks keep
 // their addresses, so a small cache makes the per-call cost a hash lookup.
 int get_maps(const DecodeArgs& a, Maps& out) {
@@ -859,26 +881,38 @@ int get_maps(const DecodeArgs& a, Maps& out) {
     out = it->second;
     return DS_OK;
   }
-  DS_REQUIRE(encode_fn() != nullptr, DS_ECUDA, "moe_decode: cuTensorMapEncodeTiled unavailable");
   Maps m;
-  memset(&m, 0, sizeof(m));
-  const uint64_t E = d.n_experts, H = d.hidden, I = d.inter;
-  bool ok = map_rows_swizzled(&m.w1d, d.w1.data, E * I, H / 2, 8, H / 256) &&
-            map_rows_swizzled(&m.w3d, d.w3.data, E * I, H / 2, 8, H / 256) &&
-            map_rows_plain(&m.w1s, d.w1.scales, E * I, H / 32, 8) &&
-            map_rows_plain(&m.w3s, d.w3.scales, E * I, H / 32, 8) &&
-            map_rows_swizzled(&m.w2d, d.w2.data, E * H, I / 2, 16, I / 256) &&
-            map_rows_plain(&m.w2s, d.w2.scales, E * H, I / 32, 16);
-  if (ok && d.shared_w1) {
-    const uint64_t Is = d.shared_inter;
-    ok = map_rows_swizzled(&m.sw1, d.shared_w1, Is, H * 2, 8, 16) &&
-         map_rows_swizzled(&m.sw3, d.shared_w3, Is, H * 2, 8, 16) &&
-         map_rows_swizzled(&m.sw2, d.shared_w2, H, Is * 2, 16, 16);
-  }
-  DS_REQUIRE(ok, DS_ECUDA, "moe_decode: tensor map encoding failed");
+  const int rc = encode_maps(a, m);
+  if (rc != DS_OK) return rc;
   if (cache.size() > 256) cache.clear();
   cache.emplace(key, m);
   out = m;
+  return DS_OK;
+}
+
+int launch_with_maps(const DecodeArgs& a, const Maps& m, cudaStream_t st) {
+  TcParams p;
+  memset(&p, 0, sizeof(p));
+  p.w1d = m.w1d, p.w3d = m.w3d, p.w1s = m.w1s, p.w3s = m.w3s, p.sw1 = m.sw1, p.sw3 = m.sw3;
+  p.w2d = m.w2d, p.w2s = m.w2s, p.sw2 = m.sw2;
+  p.a = a;
+  p.g = make_geo(a);
+  DS_CHECK_CUDA(cudaFuncSetAttribute(moe_tc_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, p.g.a_total));
+  DS_CHECK_CUDA(cudaFuncSetAttribute(moe_tc_down, cudaFuncAttributeMaxDynamicSharedMemorySize, p.g.b_total));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(ds::sm_count());
+  cfg.dynamicSmemBytes = p.g.a_total;
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, moe_tc_gate_up, p));
+  cfg.gridDim = dim3(std::min(ds::sm_count(), p.g.H / 16));
+  cfg.dynamicSmemBytes = p.g.b_total;
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, moe_tc_down, p));
   return DS_OK;
 }
 
@@ -908,32 +942,17 @@ bool tc_supported(const DecodeArgs& a) {
 }
 
 int launch_tc(const DecodeArgs& a, cudaStream_t st) {
-  TcParams p;
-  memset(&p, 0, sizeof(p));
   Maps m;
   const int rc = get_maps(a, m);
   if (rc != DS_OK) return rc;
-  p.w1d = m.w1d, p.w3d = m.w3d, p.w1s = m.w1s, p.w3s = m.w3s, p.sw1 = m.sw1, p.sw3 = m.sw3;
-  p.w2d = m.w2d, p.w2s = m.w2s, p.sw2 = m.sw2;
-  p.a = a;
-  p.g = make_geo(a);
-  DS_CHECK_CUDA(cudaFuncSetAttribute(moe_tc_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, p.g.a_total));
-  DS_CHECK_CUDA(cudaFuncSetAttribute(moe_tc_down, cudaFuncAttributeMaxDynamicSharedMemorySize, p.g.b_total));
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(kThreads);
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cfg.gridDim = dim3(ds::sm_count());
-  cfg.dynamicSmemBytes = p.g.a_total;
-  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, moe_tc_gate_up, p));
-  cfg.gridDim = dim3(std::min(ds::sm_count(), p.g.H / 16));
-  cfg.dynamicSmemBytes = p.g.b_total;
-  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, moe_tc_down, p));
-  return DS_OK;
+  return launch_with_maps(a, m, st);
+}
+
+int launch_tc_uncached(const DecodeArgs& a, cudaStream_t st) {
+  Maps m;
+  const int rc = encode_maps(a, m);
+  if (rc != DS_OK) return rc;
+  return launch_with_maps(a, m, st);
 }
 
 }  // namespace decode

@@ -47,6 +47,9 @@ SIGNATURES: dict[str, tuple] = {
     "ds_moe_decode_workspace_size": (c_int, [POINTER(DsMoeDesc), c_int64, POINTER(c_size_t)]),
     "ds_moe_decode": (c_int, [POINTER(DsMoeDesc), c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_size_t, c_void_p]),
+    "ds_moe_decode_noalloc_max_scratch": (c_size_t, []),
+    "ds_moe_decode_noalloc": (c_int, [POINTER(DsMoeDesc), c_void_p, c_int, c_int64, c_void_p, c_void_p,
+                                      c_void_p, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -9,7 +9,8 @@
  *     `void* stream` (NULL = legacy default stream);
  *   - launches asynchronously on that stream and never synchronises it;
  *   - allocates nothing: scratch comes from a caller-provided workspace whose
- *     size a matching *_workspace_size() call reports.
+ *     size a matching *_workspace_size() call reports (ds_moe_decode_noalloc
+ *     uses a static device array instead).
  * The library is stateless and reentrant across distinct streams.
  *
  * Layout conventions (all row-major, K = input features contiguous):
@@ -176,6 +177,24 @@ int ds_moe_decode_workspace_size(const DsMoeDesc* desc, int64_t tokens,
 int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens,
                   const int32_t* topk_ids, const float* topk_w, void* out,
                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ds_moe_decode without a workspace.  No counterpart in the reference (its
+ * MLX runtime owns all scratch); added for callers that may not allocate
+ * device memory at all while decoding.  Scratch comes from a static device
+ * array of ds_moe_decode_noalloc_max_scratch() bytes (8 MiB) per device;
+ * a layer whose ds_moe_decode_workspace_size() exceeds it is rejected with
+ * DS_ERANGE.  Same arguments, kernels and results as ds_moe_decode.
+ *   - The first call on each device resolves the array's address (setup);
+ *     make it before any latency-sensitive or otherwise restricted phase.
+ *   - Each call clears the array's error word on `stream` (cudaMemsetAsync);
+ *     nothing else has to start at zero.
+ *   - All calls on one device share the array: two calls that may overlap
+ *     (different streams, or host threads without ordering) race on it and
+ *     corrupt each other's results.  Serialise them on one stream. */
+size_t ds_moe_decode_noalloc_max_scratch(void);
+int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens,
+                          const int32_t* topk_ids, const float* topk_w, void* out,
+                          void* stream);
 
 #ifdef __cplusplus
 }
