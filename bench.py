@@ -314,7 +314,9 @@ def run_ours(args) -> dict:
             "gbs_per_gpu": round(achieved, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                         "traffic": traffic, "kernel": "ds_moe_decode (moe_gate_up_kernel + moe_down_kernel)",
+                         "traffic": traffic,
+                         "kernel": "ds_moe_decode: " + ("moe_tc_gate_up + moe_tc_down" if fmt == "fp4"
+                                                        else "moe_gate_up_kernel + moe_down_kernel (q3)"),
                          "bytes_per_launch": step_bytes, "peak_kind": kind},
             "e2e": {"value": round(world * tokens * args.steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * (H * 2 + E * 4), "d2h_bytes_per_step": tokens * H * 2},
