@@ -47,6 +47,18 @@ SIGNATURES: dict[str, tuple] = {
     "ds_moe_decode_workspace_size": (c_int, [POINTER(DsMoeDesc), c_int64, POINTER(c_size_t)]),
     "ds_moe_decode": (c_int, [POINTER(DsMoeDesc), c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_size_t, c_void_p]),
+    "ds_moe_align_capacity": (c_int, [c_int64, c_int, c_int, c_int, POINTER(c_int64), POINTER(c_int64)]),
+    "ds_moe_align": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_int64, c_void_p, c_int64,
+                             c_void_p, c_void_p]),
+    "ds_grouped_scales_size": (c_int, [POINTER(DsMoeDesc), POINTER(c_size_t), POINTER(c_size_t)]),
+    "ds_grouped_prepare_scales": (c_int, [POINTER(DsMoeDesc), c_void_p, c_void_p, c_void_p]),
+    "ds_grouped_ffn_workspace_size": (c_int, [POINTER(DsMoeDesc), c_int64, POINTER(c_size_t)]),
+    "ds_grouped_ffn": (c_int, [POINTER(DsMoeDesc), c_void_p, c_void_p, c_void_p, c_int, c_int64, c_void_p,
+                               c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ds_dense_swiglu_workspace_size": (c_int, [c_int64, c_int, POINTER(c_size_t)]),
+    "ds_dense_swiglu": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64,
+                                c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_size_t,
+                                c_void_p]),
     "ds_moe_decode_noalloc_max_scratch": (c_size_t, []),
     "ds_moe_decode_noalloc": (c_int, [POINTER(DsMoeDesc), c_void_p, c_int, c_int64, c_void_p, c_void_p,
                                       c_void_p, c_void_p]),

@@ -74,3 +74,24 @@ def make_layer(fmt: str, hidden: int, inter: int, n_experts: int, seed: int, sha
         sw = [_normal(shape, std, seed * 10 + 7 + i, device).to(torch.bfloat16)
               for i, shape in enumerate(((shared_inter, hidden), (shared_inter, hidden), (hidden, shared_inter)))]
     return MoEWeights(w1, w3, w2, *sw, swiglu_limit=limit if limit is not None else 0.0)
+
+
+def zipf_routing(tokens: int, n_experts: int, top_k: int, s: float = 1.1, seed: int = 0,
+                 device: torch.device | str = "cuda") -> tuple[torch.Tensor, torch.Tensor]:
+    """Top-k routing with Zipf(s) expert popularity.
+
+    Expert rank r (1-based) has popularity r^-s; ranks map to ids through a
+    seeded permutation.  Every token draws k distinct experts without
+    replacement by Gumbel-top-k on log popularity; gates are a softmax of
+    N(0, 1) logits over the k picks.  Returns ids [T, k] int32, gates [T, k] f32.
+    """
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    rank_to_id = torch.randperm(n_experts, generator=g)
+    logp = -s * torch.log(torch.arange(1, n_experts + 1, dtype=torch.float64))
+    u = torch.rand(tokens, n_experts, generator=g, dtype=torch.float64).clamp_min(1e-300)
+    gumbel = -torch.log(-torch.log(u))
+    ranks = torch.topk(logp[None, :] + gumbel, top_k, dim=1).indices
+    ids = rank_to_id[ranks].to(torch.int32)
+    w = torch.softmax(torch.randn(tokens, top_k, generator=g), dim=1).float()
+    return ids.to(device), w.to(device)

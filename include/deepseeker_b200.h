@@ -178,6 +178,69 @@ int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tok
                   const int32_t* topk_ids, const float* topk_w, void* out,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- sort-and-pad of routed pairs by expert ---------------------------- */
+
+/* Output capacities ds_moe_align needs for topk_ids [m, k] over n_experts:
+ * sorted_cap = m*k + min(n_experts, m*k) * (block - 1), blocks_cap =
+ * sorted_cap / block. */
+int ds_moe_align_capacity(int64_t m, int k, int n_experts, int block,
+                          int64_t* sorted_cap, int64_t* blocks_cap);
+
+/* align_block_size on the device (src/deepseeker/moe_align.py:21-46):
+ * flat positions of topk_ids [m, k] (i32, device) grouped by expert in
+ * stable order, each expert's run padded with the sentinel m*k to a multiple
+ * of block, experts in id order.  Writes sorted_ids (i32), expert_ids (i32,
+ * one per block) and *n_pad (device i32, the padded length; -1 when an id is
+ * outside [0, n_experts), in which case the other outputs are undefined).
+ * n_experts <= 1024. */
+int ds_moe_align(const int32_t* topk_ids, int64_t m, int k, int n_experts, int block,
+                 int32_t* sorted_ids, int64_t sorted_cap, int32_t* expert_ids,
+                 int64_t blocks_cap, int32_t* n_pad, void* stream);
+
+/* ---- batched grouped expert FFN (FP4 banks, tcgen05) ------------------- */
+
+/* Bytes of the re-laid-out block scales the grouped kernels read: W1 and W3
+ * together (w13_bytes) and W2 (w2_bytes); same totals as the bank scales. */
+int ds_grouped_scales_size(const DsMoeDesc* desc, size_t* w13_bytes, size_t* w2_bytes);
+
+/* Re-lay the FP4 bank scales of desc (w1, w3, w2) into the tensor-core scale
+ * atoms: for every 128 weight rows and 128-wide K chunk, 512 bytes where byte
+ * (r%32)*16 + (r/32)*4 + b is the scale of row r, k-block b.  Run once per
+ * resident bank (replaces no reference function: the reference reads the
+ * checkpoint scales directly, mlx_weights.py:92-110). */
+int ds_grouped_prepare_scales(const DsMoeDesc* desc, void* w13_sf, void* w2_sf, void* stream);
+
+int ds_grouped_ffn_workspace_size(const DsMoeDesc* desc, int64_t tokens, size_t* bytes);
+
+/* Routed-expert SwiGLU FFN for a batch of tokens (prefill / MTP verify):
+ * pairs sorted by expert on the device, gate/up and down projections as
+ * tcgen05 block-scaled MMAs (FP4 weights, activations as exact e4m3 pieces),
+ * f32 accumulate, combine in top-k order.  Replaces grouped_swiglu and the
+ * moe_layer expert loop for FP4 banks (src/deepseeker/grouped.py:34-56,
+ * src/deepseeker/mlx_forward.py:388-419).  FP4 banks only, hidden and inter
+ * multiples of 128, x bf16 [tokens, hidden], no shared expert (add it
+ * separately); topk_ids [tokens, k] (-1 = dropped slot); out bf16.
+ * desc->route_before_down selects where the route weight is applied. */
+int ds_grouped_ffn(const DsMoeDesc* desc, const void* w13_sf, const void* w2_sf,
+                   const void* x, int x_dtype, int64_t tokens, const int32_t* topk_ids,
+                   const float* topk_w, void* out, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* ---- dense-weight pair FFN (grouped_swiglu / naive_swiglu with dense experts) */
+
+int ds_dense_swiglu_workspace_size(int64_t n_pairs, int hidden, size_t* bytes);
+
+/* y_p = w_p * (silu(x_r gate_e) * (x_r up_e)) down_e for every pair p = (r, e)
+ * (f32; gate/up [E, H, I], down [E, I, H]; w_p = 1 when pair_weight is NULL;
+ * swiglu_limit > 0 clamps as moe_layer does), then out[t] = sum of y_p over
+ * the pairs row_ptr[t] .. row_ptr[t+1]-1 in that order
+ * (src/deepseeker/grouped.py:34-81). */
+int ds_dense_swiglu(const float* x, int64_t tokens, int hidden, int inter, int n_experts,
+                    const float* gate, const float* up, const float* down, int64_t n_pairs,
+                    const int32_t* pair_row, const int32_t* pair_expert, const float* pair_weight,
+                    const int32_t* row_ptr, float swiglu_limit, float* out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 /* ds_moe_decode without a workspace.  No counterpart in the reference (its
  * MLX runtime owns all scratch); added for callers that may not allocate
  * device memory at all while decoding.  Scratch comes from a static device
