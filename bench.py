@@ -19,7 +19,12 @@ roofline = algorithmic bytes of the decode launch pair / its CUDA-event
 duration vs MEASURED_PEAKS.json hbm_gbs; cpu_baseline = the reference CPU
 path (oracle port) on this host's cores for a bounded sample.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2|c3]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2|c3|c4]
+
+--config c4 measures BASELINE config 4 instead: one batched grouped FFN over
+2048 tokens (256 FP4 experts, top-8 Zipf(1.1) routing) per step; value is
+TFLOP/s of algorithmic FFN FLOPs, roofline is HBM GB/s of the weights
+streamed, and a second "tensor" object gives the MMA-side fraction.
 """
 from __future__ import annotations
 
@@ -147,6 +152,58 @@ def reference_step_factory(seed: int, fmt: str = "fp4"):
     return step, ex
 
 
+C4_TOKENS = 2048
+
+
+def grouped_flops(pairs: int) -> float:
+    """Algorithmic FLOPs of the routed SwiGLU FFN over `pairs` (token, expert) pairs."""
+    return 2.0 * pairs * 3 * H * I
+
+
+def time_reference_grouped(budget_s: float) -> tuple[float, int, str]:
+    """TFLOP/s of the reference CPU path on config 4 (numpy FP4 dequant +
+    torch f32 expert matmuls, the restatement in oracle/), measured on a
+    sample of experts and extrapolated to the 256-expert batch: per-expert
+    dequant time x experts touched + per-pair matmul time x pairs."""
+    import numpy as np
+    import torch
+
+    from deepseeker import synthetic
+    from oracle import fp4 as ofp4
+    from oracle import moe as omoe
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(4)
+    ids, w = synthetic.zipf_routing(C4_TOKENS, E, K_TOP, seed=4, device="cpu")
+    x = torch.randn(C4_TOKENS, H, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).float()
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    touched = int((counts > 0).sum())
+    order = torch.argsort(counts, descending=True).tolist()
+    t_deq = t_mm = 0.0
+    n_exp = n_pairs = 0
+    t_start = time.perf_counter()
+    for e in order[::max(1, E // 16)]:   # a spread of heavy and light experts
+        mats = [(rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8),
+                 rng.integers(118, 128, size=(n, k // 32), dtype=np.uint8)) for n, k in ((I, H), (I, H), (H, I))]
+        t0 = time.perf_counter()
+        w1, w3, w2 = (torch.from_numpy(ofp4.dequant_matrix(*m)) for m in mats)
+        t1 = time.perf_counter()
+        rows, slots = torch.nonzero(ids == e, as_tuple=True)
+        h = omoe.swiglu_hidden(x[rows], w1, w3, 10.0) * w[rows, slots][:, None]
+        _ = h @ w2.T
+        t2 = time.perf_counter()
+        t_deq += t1 - t0
+        t_mm += t2 - t1
+        n_exp += 1
+        n_pairs += int(rows.numel())
+        if time.perf_counter() - t_start > budget_s:
+            break
+    total = touched * (t_deq / n_exp) + C4_TOKENS * K_TOP * (t_mm / max(n_pairs, 1))
+    value = grouped_flops(C4_TOKENS * K_TOP) / total / 1e12
+    return value, os.cpu_count() or 1, (f"{n_exp} of {touched} touched experts of config 4 ({n_pairs} pairs) timed, "
+                                       f"extrapolated to 16384 pairs; f32 CPU")
+
+
 def time_reference(steps: int, warmup: int, budget_s: float | None = None) -> tuple[float, int, str]:
     """tokens/s of the reference CPU path; returns (value, cores, sample description)."""
     step, ex = reference_step_factory(seed=1234)
@@ -168,6 +225,294 @@ def time_reference(steps: int, warmup: int, budget_s: float | None = None) -> tu
 # ------------------------------------------------------------------ our arm
 
 def run_ours(args) -> dict:
+    if args.config == "c4":
+        return run_grouped(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        return run_ep(args)
+    return run_decode(args)
+
+
+def run_ep(args) -> dict:
+    """N > 1: config 2's layer expert-parallel over the N ranks (rank g owns
+    experts [g*E/N, (g+1)*E/N) of every rotated layer, shared expert
+    replicated); every rank decodes its own --batch tokens per step (weak
+    scaling), token rows dispatched / combined with NCCL all_to_all_single."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from deepseeker import ep, moe, synthetic
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    fmt = "q3" if args.config == "c3" else "fp4"
+    El = E // world
+    L = args.layers
+    b = args.batch
+    layers = [synthetic.make_layer(fmt, H, I, El, seed=1000 + l, shared_inter=IS, std=0.02, device=dev,
+                                   expert_offset=rank * El) for l in range(L)]
+    eps = [ep.gpu_layer(layer, E, K_TOP) for layer in layers]
+    total_steps = args.warmup + args.steps
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    logits = torch.randn(total_steps + 64, b, E, generator=g, device=dev)
+    xs = torch.randn(total_steps + 64, b, H, generator=g, device=dev).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i, ev=None):
+        w, ids = moe.route_softmax_topk(logits[i], K_TOP)
+        if ev is not None:
+            ev[0].record(stream)
+        out = eps[i % L](xs[i], ids, w)
+        if ev is not None:
+            ev[1].record(stream)
+        return out
+
+    with ClockSampler(local) as clk:
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                 for _ in range(args.steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for s_ in range(args.steps):
+            step(args.warmup + s_, pairs[s_])
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        ms = start.elapsed_time(end)
+        layer_ms = statistics.mean(a.elapsed_time(c) for a, c in pairs)
+    clocks = clk.summary()
+
+    # e2e: the step's x and logits from pinned host memory, output back to the host
+    e2e_steps = 0 if args.quick else min(args.steps, 50)
+    pin_x = xs[:max(e2e_steps, 1)].cpu().pin_memory()
+    pin_l = logits[:max(e2e_steps, 1)].cpu().pin_memory()
+    pin_o = torch.empty(b, H, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty(b, H, dtype=torch.bfloat16, device=dev)
+    dl = torch.empty(b, E, dtype=torch.float32, device=dev)
+
+    def e2e_step(s_):
+        dx.copy_(pin_x[s_], non_blocking=True)
+        dl.copy_(pin_l[s_], non_blocking=True)
+        w, ids = moe.route_softmax_topk(dl, K_TOP)
+        out = eps[s_ % L](dx, ids, w)
+        pin_o.copy_(out, non_blocking=True)
+        stream.synchronize()
+    for s_ in range(min(3, e2e_steps)):
+        e2e_step(s_)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s_ in range(e2e_steps):
+        e2e_step(s_)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max(e0.elapsed_time(e1), 1e-9)
+
+    per_expert = sum(bk.nbytes() // El for bk in (layers[0].w1, layers[0].w3, layers[0].w2))
+    # bytes one rank streams per step: its share of the routed experts + the shared expert for its tokens
+    step_bytes = b * K_TOP * per_expert + 3 * IS * H * 2 * ((b + 7) // 8)
+    ms_t = torch.tensor([ms, e2e_ms, layer_ms], device=dev)
+    dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, layer_ms = (float(v) for v in ms_t.cpu())
+    result = None
+    if rank == 0:
+        pk, kind = peaks()
+        gbs = step_bytes / (layer_ms * 1e-3) / 1e9
+        result = {
+            "metric": METRIC,
+            "value": round(world * b * args.steps / (ms * 1e-3), 2),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": f"{fmt} weights, bf16 activations, f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights quantised on device; router logits N(0,1))",
+            "config": {"workload": f"BASELINE config {'2' if fmt == 'fp4' else '3'} layer, expert-parallel over "
+                                   f"{world} GPUs ({El} experts each, shared expert replicated), {b} decode "
+                                   "token(s) per GPU per step",
+                       "format": fmt, "tokens_per_step_per_gpu": b, "layers_rotated": L,
+                       "l2": f"rotating {L} resident layer shards per GPU",
+                       "parallelism": f"ep{world} (NCCL all_to_all_single dispatch + combine)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None,
+                         "kernel": "ep layer step (dispatch + local experts + combine), per GPU",
+                         "bytes_per_launch": int(step_bytes), "peak_kind": kind},
+            "e2e": {"value": round(world * b * max(e2e_steps, 1) / (e2e_ms * 1e-3), 2) if e2e_steps else None,
+                    "unit": "tokens/s", "h2d_bytes_per_step": b * (H * 2 + E * 4), "d2h_bytes_per_step": b * H * 2},
+            "gpu_launches": args.steps * (1 + 5 + 2 * ((b + 7) // 8)),
+            "clocks": clocks,
+        }
+    del eps
+    dist.barrier()
+    dist.destroy_process_group()
+    return result
+
+
+def run_grouped(args) -> dict:
+    """one batched grouped FFN over 2048 tokens, FP4 experts."""
+    import torch
+
+    from deepseeker import grouped, synthetic
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    T = C4_TOKENS
+    layer = synthetic.make_layer("fp4", H, I, E, seed=1000 * (rank + 1), shared_inter=None, std=0.02, device=dev)
+    ffn = grouped.GroupedFFN(layer, K_TOP)
+    R = 4  # distinct routings / inputs rotated
+    routes = [synthetic.zipf_routing(T, E, K_TOP, s=1.1, seed=100 * rank + r, device=dev) for r in range(R)]
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + rank)
+    xs = [torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16) for _ in range(R)]
+    outs = [torch.empty(T, H, dtype=torch.bfloat16, device=dev) for _ in range(R)]
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i, ev=None):
+        ids, w = routes[i % R]
+        if ev is not None:
+            ev[0].record(stream)
+        ffn(xs[i % R], ids, w, out=outs[i % R], route_before_down=True)
+        if ev is not None:
+            ev[1].record(stream)
+
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        i = 0
+        while i < args.warmup or time.perf_counter() - t0 < (0.0 if args.quick else 1.0):
+            step(i)
+            i += 1
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        pairs_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    for _ in range(args.steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for s_ in range(args.steps):
+            step(s_, pairs_ev[s_])
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ms = start.elapsed_time(end)
+        step_ms = statistics.mean(a.elapsed_time(b) for a, b in pairs_ev)
+        t1 = time.perf_counter()
+        j = 0
+        while time.perf_counter() - t1 < (0.0 if args.quick else 0.6):
+            step(j)
+            j += 1
+        torch.cuda.synchronize(dev)
+    clocks = clk.summary()
+
+    # e2e: x and routing from pinned host memory, output back to host, every step synchronised
+    e2e_steps = 0 if args.quick else min(args.steps, 20)
+    pin_x = [x.cpu().pin_memory() for x in xs]
+    pin_i = [r[0].cpu().pin_memory() for r in routes]
+    pin_w = [r[1].cpu().pin_memory() for r in routes]
+    pin_o = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    di = torch.empty(T, K_TOP, dtype=torch.int32, device=dev)
+    dw = torch.empty(T, K_TOP, dtype=torch.float32, device=dev)
+    do = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+
+    def e2e_step(s_):
+        dx.copy_(pin_x[s_ % R], non_blocking=True)
+        di.copy_(pin_i[s_ % R], non_blocking=True)
+        dw.copy_(pin_w[s_ % R], non_blocking=True)
+        ffn(dx, di, dw, out=do, route_before_down=True)
+        pin_o.copy_(do, non_blocking=True)
+        stream.synchronize()
+    for s_ in range(min(3, e2e_steps)):
+        e2e_step(s_)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s_ in range(e2e_steps):
+        e2e_step(s_)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max(e0.elapsed_time(e1), 1e-9)
+
+    per_expert = sum(b.nbytes() // E for b in (layer.w1, layer.w3, layer.w2))
+    touched = statistics.mean(int(torch.unique(r[0]).numel()) for r in routes)
+    step_bytes = touched * per_expert + 2 * T * H * 2
+    flops = grouped_flops(T * K_TOP)
+    ms_t = torch.tensor([ms, e2e_ms, step_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, step_ms = (float(v) for v in ms_t.cpu())
+    result = None
+    if rank == 0:
+        pk, kind = peaks()
+        tflops = world * flops * args.steps / (ms * 1e-3) / 1e12
+        gbs = step_bytes / (step_ms * 1e-3) / 1e9
+        result = {
+            "metric": METRIC,
+            "value": round(tflops, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp4-e2m1 weights x e4m3 activation pieces (bf16-exact x, ~14-bit h), f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights quantised on device; Zipf(1.1) top-8 routing)",
+            "config": {"workload": "BASELINE config 4: batched grouped expert FFN, 2048 tokens, hidden 4096, "
+                                   "256 FP4 experts inter 2048, top-8 Zipf(1.1), bf16 out",
+                       "tokens_per_step": T, "pairs_per_step": T * K_TOP, "experts_touched": touched,
+                       "l2": f"each step streams {step_bytes / 1e9:.2f} GB of expert weights (> 126 MB L2)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "tokens_per_s": round(world * T * args.steps / (ms * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": ncu_traffic("grouped_fp4_c4"),
+                         "kernel": "ds_grouped_ffn: align + xquant + gemm<gate/up> + gemm<down> + combine",
+                         "bytes_per_launch": int(step_bytes), "peak_kind": kind},
+            "tensor": {"achieved_tflops": round(flops / (step_ms * 1e-3) / 1e12, 1),
+                       "peak_tflops": 4500.0, "peak_kind": "nominal dense mxf8f6f4 rate",
+                       "frac": round(flops / (step_ms * 1e-3) / 1e12 / 4500.0, 4),
+                       "note": "activation pieces make the MMA do 2x (gate/up) and 3x (down) the algorithmic FLOPs"},
+            "e2e": {"value": round(world * flops * max(e2e_steps, 1) / (e2e_ms * 1e-3) / 1e12, 2) if e2e_steps else None,
+                    "unit": "TFLOP/s", "h2d_bytes_per_step": T * H * 2 + T * K_TOP * 8,
+                    "d2h_bytes_per_step": T * H * 2},
+            "gpu_launches": 5 * args.steps,
+            "clocks": clocks,
+        }
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_decode(args) -> dict:
     import torch
 
     from deepseeker import moe, synthetic
@@ -335,8 +680,9 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3"], default="c2")
+    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c2")
     ap.add_argument("--layers", type=int, default=8, help="distinct resident layers rotated (L2-cold)")
+    ap.add_argument("--batch", type=int, default=1, help="decode tokens per GPU per step (N > 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="profiling runs: no time-based warm-up, no e2e / CPU-baseline legs")
@@ -345,6 +691,20 @@ def main() -> int:
 
     if args.impl == "reference":
         if rank != 0:
+            return 0
+        if args.config == "c4":
+            value, cores, sample = time_reference_grouped(budget_s=20.0)
+            line = {"metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": args.gpus,
+                    "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": round(grouped_flops(C4_TOKENS * K_TOP) / (value * 1e12) * 1e3, 1),
+                    "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "impl": "reference",
+                    "dtype": "f32 (reference CPU path)", "data": "synthetic",
+                    "config": {"workload": "BASELINE config 4: batched grouped expert FFN (reference CPU path)"},
+                    "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                     "sample": sample},
+                    "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                            "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
             return 0
         # bounded per-step sample: one decode token of config 2 through the reference CPU path
         value, cores, sample = time_reference(args.steps, args.warmup)
@@ -363,9 +723,14 @@ def main() -> int:
     result = run_ours(args)
     if rank == 0 and result is not None:
         if not (args.no_cpu_baseline or args.quick) and int(os.environ.get("WORLD_SIZE", "1")) == 1:
-            value, cores, sample = time_reference(steps=1000, warmup=1, budget_s=15.0)
-            result["cpu_baseline"] = {"value": round(value, 4), "unit": "tokens/s", "cores": cores,
-                                      "kind": "port", "sample": sample}
+            if args.config == "c4":
+                value, cores, sample = time_reference_grouped(budget_s=20.0)
+                result["cpu_baseline"] = {"value": round(value, 6), "unit": "TFLOP/s", "cores": cores,
+                                          "kind": "port", "sample": sample}
+            else:
+                value, cores, sample = time_reference(steps=1000, warmup=1, budget_s=15.0)
+                result["cpu_baseline"] = {"value": round(value, 4), "unit": "tokens/s", "cores": cores,
+                                          "kind": "port", "sample": sample}
         print(json.dumps(result), flush=True)
     return 0
 

@@ -643,10 +643,11 @@ extern "C" int ds_grouped_ffn_workspace_size(const DsMoeDesc* desc, int64_t toke
 
 extern "C" int ds_grouped_ffn(const DsMoeDesc* desc, const void* w13_sf, const void* w2_sf, const void* x,
                               int x_dtype, int64_t tokens, const int32_t* topk_ids, const float* topk_w, void* out,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+                              int out_dtype, void* workspace, size_t workspace_bytes, void* stream) {
   int st = validate(desc, tokens);
   if (st != DS_OK) return st;
   DS_REQUIRE(x_dtype == DS_BF16, DS_ENOTSUP, "grouped_ffn: x must be bf16");
+  DS_REQUIRE(out_dtype == DS_BF16 || out_dtype == DS_F32, DS_EINVAL, "grouped_ffn: out_dtype must be bf16 or f32");
   DS_REQUIRE(w13_sf && w2_sf && x && topk_ids && topk_w && out && workspace, DS_EINVAL,
              "grouped_ffn: null pointer");
   DS_REQUIRE(ds::aligned(x, 16) && ds::aligned(out, 16) && ds::aligned(workspace, 256) &&
@@ -724,9 +725,13 @@ extern "C" int ds_grouped_ffn(const DsMoeDesc* desc, const void* w13_sf, const v
   gemm_kernel<DOWN><<<grid_b, kThreads, smem_bytes<DOWN>(), s>>>(p);
   DS_CHECK_LAUNCH("gemm_kernel<down>");
 
-  combine_kernel<__nv_bfloat16><<<(unsigned)tokens, 256, 0, s>>>(y, pos, topk_w, ints, ints + 2, k, H,
-                                                                  desc->route_before_down ? 0 : 1,
-                                                                  static_cast<__nv_bfloat16*>(out));
+  if (out_dtype == DS_F32)
+    combine_kernel<float><<<(unsigned)tokens, 256, 0, s>>>(y, pos, topk_w, ints, ints + 2, k, H,
+                                                            desc->route_before_down ? 0 : 1, static_cast<float*>(out));
+  else
+    combine_kernel<__nv_bfloat16><<<(unsigned)tokens, 256, 0, s>>>(y, pos, topk_w, ints, ints + 2, k, H,
+                                                                    desc->route_before_down ? 0 : 1,
+                                                                    static_cast<__nv_bfloat16*>(out));
   DS_CHECK_LAUNCH("combine_kernel");
   return DS_OK;
 }

@@ -1,0 +1,176 @@
+"""Expert-parallel MoE layer: routed experts sharded over the ranks of a
+process group, token rows exchanged with all-to-all (NCCL over NVLink on B200
+ranks; the CPU tests drive the same host logic over gloo).
+
+Rank g owns global experts [g * E_l, (g + 1) * E_l), E_l = E / G; the shared
+expert is replicated.  One layer step for the b tokens a rank holds (its
+"home" tokens):
+
+  1. dispatch: every (token, slot) pair with expert e goes to rank e // E_l.
+     Each rank sends a fixed-capacity block of b * k rows to every peer
+     (unused rows carry expert -1), so the exchange needs no host sync and is
+     one all_to_all_single of 32-bit words: the activation row followed by
+     (local expert id, route weight).
+  2. experts: the owner runs its local experts over the received rows -- route
+     weight applied before the down projection, SwiGLU clamp -- producing f32
+     rows (GPU: ds_grouped_ffn with top_k = 1, rows of expert -1 skipped).
+  3. combine: rows return with a second all_to_all_single; the home rank adds
+     each token's k contributions in slot order, then the shared expert (its
+     output rounded to the activation dtype first, as the reference does) and
+     casts to the activation dtype.
+
+A row's result does not depend on which other rows share its launch, so the
+G-rank output equals the 1-rank output bit for bit.  The layer contract is
+moe_layer's (src/deepseeker/mlx_forward.py:388-419, shared add
+src/deepseeker/mlx_runner.py:776-781); the reference itself runs on one device.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+# local_ffn(x_rows [R, H] (activation dtype), expert [R] int32 (-1 = none), gate [R] f32) -> f32 [R, H]
+LocalFFN = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+# shared_fn(x [b, H]) -> f32 [b, H], already rounded to the activation dtype
+SharedFn = Callable[[torch.Tensor], torch.Tensor]
+
+
+class ExpertParallelMoE:
+    def __init__(self, n_experts: int, top_k: int, local_ffn: LocalFFN, shared_fn: SharedFn | None = None,
+                 group: dist.ProcessGroup | None = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if n_experts % self.world:
+            raise ValueError(f"{n_experts} experts do not shard over {self.world} ranks")
+        self.n_experts = n_experts
+        self.local_experts = n_experts // self.world
+        self.first_expert = self.rank * self.local_experts
+        self.top_k = top_k
+        self.local_ffn = local_ffn
+        self.shared_fn = shared_fn
+
+    # -- packing: [rows, H] activations + (expert int32, gate f32) as int32 words
+    @staticmethod
+    def _pack(x: torch.Tensor, expert: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+        words = x.contiguous().view(torch.uint8).view(x.shape[0], -1).view(torch.int32)
+        meta = torch.stack([expert.to(torch.int32), gate.to(torch.float32).view(torch.int32)], dim=1)
+        return torch.cat([words, meta], dim=1)
+
+    @staticmethod
+    def _unpack(buf: torch.Tensor, dtype: torch.dtype, H: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        n = buf.shape[1] - 2
+        x = buf[:, :n].contiguous().view(torch.uint8).view(buf.shape[0], -1).view(dtype)
+        expert = buf[:, n].contiguous()
+        gate = buf[:, n + 1].contiguous().view(torch.float32)
+        return x[:, :H], expert, gate
+
+    def _all_to_all(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        if self.world == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, group=self.group)
+
+    def dispatch_plan(self, ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(dest rank, slot index inside the block for that rank, valid) per pair, [b*k] each."""
+        flat = ids.reshape(-1).to(torch.int64)
+        valid = flat >= 0
+        dest = torch.where(valid, flat // self.local_experts, torch.zeros_like(flat))
+        onehot = torch.nn.functional.one_hot(dest, self.world) * valid[:, None]
+        index = (torch.cumsum(onehot, dim=0) - 1).gather(1, dest[:, None]).view(-1)
+        return dest, index, valid
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, gates: torch.Tensor) -> torch.Tensor:
+        """x [b, H], ids [b, k] global expert ids (-1 = dropped slot), gates [b, k] -> [b, H] of x.dtype."""
+        b, H = x.shape
+        k = ids.shape[1]
+        cap = b * k
+        G = self.world
+        dest, index, valid = self.dispatch_plan(ids)
+        flat = ids.reshape(-1).to(torch.int64)
+        token = torch.arange(cap, device=x.device) // k
+        # 1. dispatch
+        if (H * x.element_size()) % 4:
+            raise ValueError("rows must be a whole number of 32-bit words")
+        words = H * x.element_size() // 4
+        send = torch.zeros(G * cap, words + 2, dtype=torch.int32, device=x.device)
+        send[:, words] = -1  # expert -1: unused row
+        slot = dest * cap + index
+        rows = self._pack(x[token[valid]], flat[valid] - dest[valid] * self.local_experts, gates.reshape(-1)[valid])
+        send[slot[valid]] = rows
+        recv = torch.empty_like(send)
+        self._all_to_all(recv, send)
+        # 2. local experts
+        rx, rexp, rgate = self._unpack(recv, x.dtype, H)
+        y = self.local_ffn(rx, rexp, rgate)
+        if y.dtype != torch.float32 or y.shape != (G * cap, H):
+            raise ValueError("local_ffn must return f32 [rows, H]")
+        back = torch.empty_like(y)
+        self._all_to_all(back, y.contiguous())
+        # 3. combine in slot order (+ shared), cast
+        back = torch.cat([back, torch.zeros(1, H, dtype=back.dtype, device=back.device)])
+        src = torch.where(valid, slot, torch.full_like(slot, G * cap)).view(b, k)
+        acc = back[src[:, 0]]
+        for s in range(1, k):
+            acc = acc + back[src[:, s]]
+        if self.shared_fn is not None:
+            acc = acc + self.shared_fn(x)
+        return acc.to(x.dtype)
+
+    __call__ = forward
+
+
+# ---------------------------------------------------------------- GPU defaults
+
+def gpu_local_ffn(local_layer) -> LocalFFN:
+    """Owner-side expert FFN on the B200 kernels: FP4 shards run ds_grouped_ffn
+    (top_k = 1, f32 rows); Q3 shards run the decode kernels on 8-row chunks."""
+    from . import _abi, grouped, moe
+
+    if local_layer.w1.fmt == _abi.DS_FMT_FP4:
+        ffn = grouped.GroupedFFN(local_layer, 1)
+
+        def run(xr, expert, gate):
+            return ffn(xr.to(torch.bfloat16).contiguous(), expert.view(-1, 1).contiguous(),
+                       gate.view(-1, 1).contiguous(), route_before_down=True, out_dtype=torch.float32)
+        return run
+
+    def run_q3(xr, expert, gate):
+        R, H = xr.shape
+        out = torch.zeros(R, H, dtype=torch.float32, device=xr.device)
+        for r0 in range(0, R, moe.MAX_DECODE_TOKENS):
+            r1 = min(R, r0 + moe.MAX_DECODE_TOKENS)
+            out[r0:r1] = moe.moe_decode(xr[r0:r1].float().contiguous(), local_layer,
+                                        expert[r0:r1].view(-1, 1).contiguous(),
+                                        gate[r0:r1].view(-1, 1).contiguous())
+        return out
+    return run_q3
+
+
+def gpu_shared_fn(local_layer) -> SharedFn | None:
+    """Shared expert on the decode kernels (no routed slot), f32 math, output
+    rounded to the activation dtype before it is added (reference order)."""
+    from . import moe
+
+    if local_layer.shared_w1 is None:
+        return None
+
+    def run(x):
+        b, H = x.shape
+        out = torch.empty(b, H, dtype=torch.float32, device=x.device)
+        for t0 in range(0, b, moe.MAX_DECODE_TOKENS):
+            t1 = min(b, t0 + moe.MAX_DECODE_TOKENS)
+            n = t1 - t0
+            ids = torch.full((n, 1), -1, dtype=torch.int32, device=x.device)
+            w = torch.zeros(n, 1, dtype=torch.float32, device=x.device)
+            out[t0:t1] = moe.moe_decode(x[t0:t1].float().contiguous(), local_layer, ids, w)
+        return out.to(x.dtype).float()
+    return run
+
+
+def gpu_layer(local_layer, n_experts: int, top_k: int, group=None) -> ExpertParallelMoE:
+    """ExpertParallelMoE over this rank's shard `local_layer` (global experts
+    [rank * E_l, (rank + 1) * E_l) as built with synthetic.make_layer(expert_offset=...))."""
+    return ExpertParallelMoE(n_experts, top_k, gpu_local_ffn(local_layer), gpu_shared_fn(local_layer), group)

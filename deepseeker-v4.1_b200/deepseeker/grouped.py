@@ -142,7 +142,8 @@ class GroupedFFN:
         return n.value
 
     def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor,
-                 out: torch.Tensor | None = None, route_before_down: bool | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, route_before_down: bool | None = None,
+                 out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
         x = require_cuda(x, "x", torch.bfloat16)
         T, H = x.shape
         if H != self.layer.hidden:
@@ -156,9 +157,13 @@ class GroupedFFN:
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
         if out is None:
-            out = torch.empty_like(x)
+            out = torch.empty(T, H, dtype=out_dtype, device=x.device)
+        if out.dtype not in (torch.bfloat16, torch.float32) or out.shape != (T, H) or not out.is_contiguous():
+            raise ValueError("out must be a contiguous [T, H] bf16 or f32 tensor")
+        odt = _abi.DS_F32 if out.dtype == torch.float32 else _abi.DS_BF16
         _abi.call("ds_grouped_ffn", ctypes.byref(d), ptr(self.w13_sf), ptr(self.w2_sf), ptr(x), _abi.DS_BF16, T,
-                  ptr(topk_ids), ptr(topk_w), ptr(out), ptr(self._ws), self._ws.numel(), stream_handle(x.device))
+                  ptr(topk_ids), ptr(topk_w), ptr(out), odt, ptr(self._ws), self._ws.numel(),
+                  stream_handle(x.device))
         return out
 
 

@@ -34,8 +34,10 @@ def quantize_fp4(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def make_bank(fmt: str, n_experts: int, rows: int, cols: int, seed: int, std: float = 0.02,
-              device: torch.device | str = "cuda") -> ExpertBank:
-    """Stacked [E, rows, cols] bank; expert e uses seed `seed * 100003 + e`."""
+              device: torch.device | str = "cuda", expert_offset: int = 0) -> ExpertBank:
+    """Stacked [E, rows, cols] bank; local expert e is global expert
+    `expert_offset + e` and uses seed `seed * 100003 + expert_offset + e`, so an
+    expert-parallel shard holds exactly the experts of the unsharded bank."""
     device = torch.device(device)
     per = max(1, _CHUNK_ELEMS // (rows * cols))
     if fmt == "fp4":
@@ -43,7 +45,7 @@ def make_bank(fmt: str, n_experts: int, rows: int, cols: int, seed: int, std: fl
         scales = torch.empty((n_experts, rows, cols // 32), dtype=torch.uint8, device=device)
         for e0 in range(0, n_experts, per):
             e1 = min(n_experts, e0 + per)
-            w = torch.cat([_normal((rows, cols), std, seed * 100003 + e, device) for e in range(e0, e1)])
+            w = torch.cat([_normal((rows, cols), std, seed * 100003 + expert_offset + e, device) for e in range(e0, e1)])
             p, s = quantize_fp4(w)
             data[e0:e1] = p.view(e1 - e0, rows, cols // 2)
             scales[e0:e1] = s.view(e1 - e0, rows, cols // 32)
@@ -54,7 +56,7 @@ def make_bank(fmt: str, n_experts: int, rows: int, cols: int, seed: int, std: fl
         biases = torch.empty_like(scales)
         for e0 in range(0, n_experts, per):
             e1 = min(n_experts, e0 + per)
-            w = torch.cat([_normal((rows, cols), std, seed * 100003 + e, device) for e in range(e0, e1)])
+            w = torch.cat([_normal((rows, cols), std, seed * 100003 + expert_offset + e, device) for e in range(e0, e1)])
             q, s, b = quantize_q3(w)
             data[e0:e1] = q.view(e1 - e0, rows, -1)
             scales[e0:e1] = s.view(e1 - e0, rows, -1)
@@ -64,11 +66,14 @@ def make_bank(fmt: str, n_experts: int, rows: int, cols: int, seed: int, std: fl
 
 
 def make_layer(fmt: str, hidden: int, inter: int, n_experts: int, seed: int, shared_inter: int | None = None,
-               std: float = 0.02, device: torch.device | str = "cuda", limit: float | None = 10.0) -> MoEWeights:
-    """One MoE layer: w1/w3 [E, I, H], w2 [E, H, I] in `fmt`, shared expert bf16 (None to omit)."""
-    w1 = make_bank(fmt, n_experts, inter, hidden, seed * 10 + 1, std, device)
-    w3 = make_bank(fmt, n_experts, inter, hidden, seed * 10 + 3, std, device)
-    w2 = make_bank(fmt, n_experts, hidden, inter, seed * 10 + 2, std, device)
+               std: float = 0.02, device: torch.device | str = "cuda", limit: float | None = 10.0,
+               expert_offset: int = 0) -> MoEWeights:
+    """One MoE layer: w1/w3 [E, I, H], w2 [E, H, I] in `fmt`, shared expert bf16 (None to omit).
+
+    expert_offset: the layer holds global experts [offset, offset + E) (an expert-parallel shard)."""
+    w1 = make_bank(fmt, n_experts, inter, hidden, seed * 10 + 1, std, device, expert_offset)
+    w3 = make_bank(fmt, n_experts, inter, hidden, seed * 10 + 3, std, device, expert_offset)
+    w2 = make_bank(fmt, n_experts, hidden, inter, seed * 10 + 2, std, device, expert_offset)
     sw = [None, None, None]
     if shared_inter:
         sw = [_normal(shape, std, seed * 10 + 7 + i, device).to(torch.bfloat16)

@@ -219,12 +219,14 @@ int ds_grouped_ffn_workspace_size(const DsMoeDesc* desc, int64_t tokens, size_t*
  * moe_layer expert loop for FP4 banks (src/deepseeker/grouped.py:34-56,
  * src/deepseeker/mlx_forward.py:388-419).  FP4 banks only, hidden and inter
  * multiples of 128, x bf16 [tokens, hidden], no shared expert (add it
- * separately); topk_ids [tokens, k] (-1 = dropped slot); out bf16.
- * desc->route_before_down selects where the route weight is applied. */
+ * separately); topk_ids [tokens, k] (-1 = dropped slot); out [tokens, hidden]
+ * of out_dtype (DS_BF16, or DS_F32 for partial sums that are combined later,
+ * as the expert-parallel path does).  desc->route_before_down selects where
+ * the route weight is applied. */
 int ds_grouped_ffn(const DsMoeDesc* desc, const void* w13_sf, const void* w2_sf,
                    const void* x, int x_dtype, int64_t tokens, const int32_t* topk_ids,
-                   const float* topk_w, void* out, void* workspace, size_t workspace_bytes,
-                   void* stream);
+                   const float* topk_w, void* out, int out_dtype, void* workspace,
+                   size_t workspace_bytes, void* stream);
 
 /* ---- dense-weight pair FFN (grouped_swiglu / naive_swiglu with dense experts) */
 

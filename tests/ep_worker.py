@@ -1,0 +1,110 @@
+"""Rank body for the expert-parallel tests (spawned processes; gloo on CPU or
+NCCL on GPUs).  Imported by tests/test_ep_host.py and tests/test_ep_gpu.py."""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+for p in (str(ROOT / "deepseeker-v4.1_b200"), str(ROOT)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+H, I, E, K, B, LIMIT = 64, 32, 8, 3, 5, 10.0
+
+
+def cpu_problem(seed: int = 0):
+    """Dense f32 experts + shared expert + tokens and routing (with dropped slots)."""
+    g = torch.Generator().manual_seed(seed)
+    w1 = torch.randn(E, I, H, generator=g) * 0.2
+    w3 = torch.randn(E, I, H, generator=g) * 0.2
+    w2 = torch.randn(E, H, I, generator=g) * 0.2
+    sh = (torch.randn(16, H, generator=g) * 0.2, torch.randn(16, H, generator=g) * 0.2,
+          torch.randn(H, 16, generator=g) * 0.2)
+    x = torch.randn(B, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(B, E, generator=g)
+    w, ids = torch.softmax(logits, -1).topk(K, dim=-1)
+    ids = ids.to(torch.int32)
+    ids[1, 2] = -1        # a dropped slot
+    ids[3, :] = torch.tensor([0, 1, 2], dtype=torch.int32)   # all on rank 0 when G = 2
+    return w1, w3, w2, sh, x, ids, (w / w.sum(-1, keepdim=True)).float()
+
+
+def cpu_ep(world: int, rank: int, seed: int = 0):
+    """ExpertParallelMoE with row-by-row f32 experts (batch-independent results)."""
+    from deepseeker.ep import ExpertParallelMoE
+    from oracle import moe as omoe
+
+    w1, w3, w2, sh, x, ids, w = cpu_problem(seed)
+    El = E // world
+
+    def local_ffn(xr, expert, gate):
+        out = torch.zeros(xr.shape[0], H)
+        for r in range(xr.shape[0]):
+            e = int(expert[r])
+            if e < 0:
+                continue
+            ge = rank * El + e
+            h = omoe.swiglu_hidden(xr[r:r + 1].float(), w1[ge], w3[ge], LIMIT) * gate[r]
+            out[r] = (h @ w2[ge].T)[0]
+        return out
+
+    def shared_fn(xx):
+        return omoe.shared_expert(xx.float(), *sh, limit=LIMIT).to(xx.dtype).float()
+
+    return ExpertParallelMoE(E, K, local_ffn, shared_fn), x, ids, w
+
+
+def rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        if mode.startswith("cpu"):
+            dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+            if mode == "cpu_dead_peer" and rank == 1:
+                q.put((rank, "left"))           # leaves between steps: never joins the exchange
+                dist.destroy_process_group()
+                return
+            ep, x, ids, w = cpu_ep(world, rank)
+            try:
+                out = ep(x, ids, w)
+            except RuntimeError as e:
+                q.put((rank, f"error: {type(e).__name__}: {str(e)[:300]}"))
+                return
+            q.put((rank, out))
+        else:
+            run_gpu_rank(rank, world, q)
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, f"exception: {e!r}"))
+
+
+def gpu_problem(rank: int, world: int):
+    from deepseeker import synthetic
+    from oracle import moe as omoe
+
+    dev = torch.device("cuda", rank)
+    Hg, Ig, Eg, Kg, Bg = 1024, 512, 16, 4, 6
+    El = Eg // world
+    layer = synthetic.make_layer("fp4", Hg, Ig, El, seed=5, shared_inter=512, device=dev, expert_offset=rank * El)
+    g = torch.Generator().manual_seed(77)
+    x = torch.randn(Bg, Hg, generator=g).to(torch.bfloat16).to(dev)
+    w, ids = omoe.route_softmax_topk(torch.randn(Bg, Eg, generator=g), Kg)
+    return layer, x, ids.to(torch.int32).to(dev), w.float().to(dev), Eg, Kg
+
+
+def run_gpu_rank(rank: int, world: int, q) -> None:
+    from deepseeker import ep
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    layer, x, ids, w, Eg, Kg = gpu_problem(rank, world)
+    out = ep.gpu_layer(layer, Eg, Kg)(x, ids, w)
+    torch.cuda.synchronize()
+    q.put((rank, out.cpu()))

@@ -1,0 +1,64 @@
+"""Expert-parallel MoE on B200 ranks.
+
+* one GPU: the EP path (exchange degenerates to a copy) against the fused
+  decode layer ds_moe_decode, which is checked against the CPU oracle;
+* two GPUs (skipped with fewer): NCCL ranks, each holding half of the experts;
+  output must equal the one-rank output bit for bit.
+"""
+from __future__ import annotations
+
+import multiprocessing as mp
+import socket
+
+import pytest
+import torch
+
+from tests import ep_worker
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_l2(a, b):
+    a, b = a.double().cpu(), b.double().cpu()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def test_ep_single_rank_matches_decode(cuda):
+    from deepseeker import ep, moe
+
+    layer, x, ids, w, E, K = ep_worker.gpu_problem(0, 1)
+    out = ep.gpu_layer(layer, E, K)(x, ids, w)
+    ref = moe.moe_decode(x, layer, ids, w)
+    assert out.dtype == torch.bfloat16
+    assert rel_l2(out, ref) <= 1e-3
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_ranks_bitwise_equal_one_rank(cuda):
+    from deepseeker import ep
+
+    layer, x, ids, w, E, K = ep_worker.gpu_problem(0, 1)
+    single = ep.gpu_layer(layer, E, K)(x, ids, w).cpu()
+    del layer
+    torch.cuda.synchronize()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=ep_worker.rank_main, args=(r, 2, port, "gpu", q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r, v = q.get(timeout=300)
+            res[r] = v
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in (0, 1):
+        assert isinstance(res[r], torch.Tensor), res[r]
+        assert torch.equal(res[r], single), f"rank {r}: rel {rel_l2(res[r], single)}"
