@@ -534,6 +534,10 @@ def run_decode(args) -> dict:
     L = args.layers
     layers = [synthetic.make_layer(fmt, H, I, E, seed=1000 * (rank + 1) + l, shared_inter=IS, std=0.02,
                                    device=dev) for l in range(L)]
+    use_t5 = fmt == "fp4" and os.environ.get("DEEPSEEKER_DECODE_NO_T5") != "1"
+    if use_t5:
+        for layer in layers:
+            layer.prepare_tc()   # scale atoms: ds_moe_decode then runs its tcgen05 kernels
     total_steps = args.warmup + args.steps
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
@@ -660,12 +664,15 @@ def run_decode(args) -> dict:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                          "traffic": traffic,
-                         "kernel": "ds_moe_decode: " + ("moe_tc_gate_up + moe_tc_down" if fmt == "fp4"
-                                                        else "moe_gate_up_kernel + moe_down_kernel (q3)"),
+                         "kernel": "ds_moe_decode: " + (
+                             ("t5_prep + t5_gemm(gate/up) + t5_h + t5_gemm(down) + t5_combine"
+                              if use_t5 else "moe_tc_gate_up + moe_tc_down")
+                             if fmt == "fp4" else "moe_gate_up_kernel + moe_down_kernel (q3)"),
                          "bytes_per_launch": step_bytes, "peak_kind": kind},
             "e2e": {"value": round(world * tokens * args.steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * (H * 2 + E * 4), "d2h_bytes_per_step": tokens * H * 2},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": (6 if use_t5 else 3)
+                            * args.steps,
             "clocks": clocks,
         }
     if dist is not None:

@@ -633,6 +633,20 @@ extern "C" int ds_grouped_prepare_scales(const DsMoeDesc* desc, void* w13_sf, vo
   return DS_OK;
 }
 
+extern "C" int ds_fp4_scale_atoms(const void* scales, int64_t n_experts, int rows, int cols, void* atoms,
+                                  void* stream) {
+  DS_REQUIRE(scales && atoms, DS_EINVAL, "fp4_scale_atoms: null pointer");
+  DS_REQUIRE(n_experts >= 1 && rows > 0 && cols > 0 && rows % 128 == 0 && cols % 128 == 0, DS_EINVAL,
+             "fp4_scale_atoms: rows and cols must be positive multiples of 128");
+  DS_REQUIRE(ds::aligned(scales, 4) && ds::aligned(atoms, 16), DS_EALIGN,
+             "fp4_scale_atoms: scales 4-byte, atoms 16-byte aligned");
+  const int64_t words = n_experts * (rows / 128) * (cols / 128) * 128;
+  prep_scales_kernel<<<ds::sm_count() * 4, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(scales), nullptr, 1, words, rows, cols, static_cast<uint32_t*>(atoms));
+  DS_CHECK_LAUNCH("prep_scales_kernel (atoms)");
+  return DS_OK;
+}
+
 extern "C" int ds_grouped_ffn_workspace_size(const DsMoeDesc* desc, int64_t tokens, size_t* bytes) {
   int st = validate(desc, tokens);
   if (st != DS_OK) return st;

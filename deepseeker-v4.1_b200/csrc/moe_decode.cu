@@ -23,6 +23,7 @@
 // read exactly once per layer.
 #include <stdlib.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "moe_decode.cuh"
@@ -783,7 +784,11 @@ extern "C" int ds_moe_decode_workspace_size(const DsMoeDesc* desc, int64_t token
   int st = validate(desc, tokens);
   if (st != DS_OK) return st;
   DS_REQUIRE(bytes != nullptr, DS_EINVAL, "moe_decode_workspace_size: null output");
-  *bytes = ws_layout(desc, tokens).total;
+  size_t total = ws_layout(desc, tokens).total;
+  if (desc->w1.format == DS_FMT_FP4 && desc->w1.scales_tc && desc->w3.scales_tc && desc->w2.scales_tc &&
+      tokens <= ds::decode::kMaxTokens)
+    total = std::max(total, ds::decode::t5_workspace_bytes(*desc, (int)tokens));
+  *bytes = total;
   return DS_OK;
 }
 
@@ -819,6 +824,15 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
     const char* v = getenv("DEEPSEEKER_DECODE_GENERIC");
     return v != nullptr && v[0] == '1';
   }();
+  // FP4 banks with prepared scale atoms take the tcgen05 kernels (1..8
+  // tokens); DEEPSEEKER_DECODE_NO_T5=1 keeps them on the older kernels.
+  static const bool no_t5 = [] {
+    const char* v = getenv("DEEPSEEKER_DECODE_NO_T5");
+    return v != nullptr && v[0] == '1';
+  }();
+  if (!force_generic && !no_t5 && ds::decode::t5_supported(a) &&
+      workspace_bytes >= ds::decode::t5_workspace_bytes(*desc, (int)tokens))
+    return ds::decode::launch_t5(a, workspace, workspace_bytes, s);
   if (!force_generic && ds::decode::tc_supported(a)) return ds::decode::launch_tc(a, s);
   return desc->w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
 }

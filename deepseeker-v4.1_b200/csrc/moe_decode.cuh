@@ -36,5 +36,11 @@ int launch_tc(const DecodeArgs& a, cudaStream_t st);
 // so no host heap either).
 int launch_tc_uncached(const DecodeArgs& a, cudaStream_t st);
 
+// tcgen05 pipeline for 1..8 tokens (moe_decode_t5.cu): FP4 banks that carry
+// prepared scale atoms, bf16 x.  Needs its own workspace size.
+bool t5_supported(const DecodeArgs& a);
+size_t t5_workspace_bytes(const DsMoeDesc& d, int tokens);
+int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t st);
+
 }  // namespace decode
 }  // namespace ds

@@ -1,0 +1,873 @@
+// Decode MoE layer (1..8 tokens, FP4 routed banks with prepared scale atoms,
+// bf16 x, optional bf16 shared expert) on tcgen05 tensor cores.
+//
+// Same contract as the other decode kernels (moe_layer's expert loop,
+// src/deepseeker/mlx_forward.py:388-419; shared add mlx_runner.py:776-781):
+// for every distinct routed expert e (ascending id),
+// h = silu(min(x W1e^T, L)) * clip(x W3e^T, +-L) * gate, out += h W2e^T; plus
+// the shared expert, its output rounded to bf16 before the add.
+//
+// Launch chain (programmatic dependent launch between the kernels):
+//   prep    : distinct experts of the batch ("slots", ascending), the gate of
+//             every (slot, token), and x as six e2m1 pieces per token with
+//             per-32 ue8m0 scales (each piece re-scaled to the block maximum
+//             of the remaining residual: about 12-14 significant bits);
+//   gate/up : persistent tcgen05 kernel over items of 64 KB of weights:
+//             shared-expert tiles first (bf16, kind::f16, B = x itself -- no
+//             dependency on prep, so they stream while prep runs), then the
+//             routed FP4 tiles (kind::mxf4 block-scaled: A = the packed
+//             weights as stored, B = the x pieces, one MMA row per piece);
+//             every item is 128 weight rows x a K slice, its f32 partial sum
+//             goes to a workspace slot;
+//   h       : sums the K slices, applies SiLU/clamp/gate, writes h as six
+//             e2m1 pieces (routed) or bf16 hi/lo (shared);
+//   down    : the same kernel over W2 tiles (its producer prefetches weight
+//             stages before waiting for the previous grid);
+//   combine : adds the slots in ascending expert order and the shared expert
+//             rounded to bf16, writes bf16 rows.
+//
+// kind::mxf4 reads FP4 operands packed (two codes per byte) with the 128-byte
+// swizzle, so the weights go from HBM to shared memory unchanged (128-byte
+// TMA rows: 256 codes) and a stage of shared memory holds exactly its HBM
+// bytes; nine stages keep ~144 KB of weights in flight per SM, which is what
+// the ~3 us TMA + MMA-commit round trip needs to stream at HBM rate.  Roles
+// per CTA: TMA producer, single-thread MMA issuer, four stager warps (scale
+// atoms into tensor memory, one warp per lane quarter), four epilogue warps.
+// Every wait is bounded; a timeout sets kErrWaitTimeout and an abort flag
+// that ends every role.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "moe_decode.cuh"
+#include "ptx.cuh"
+#include "tc5.cuh"
+
+namespace ds {
+namespace decode {
+namespace {
+
+using namespace ds::ptx;
+
+constexpr int kThreads = 320;                  // 10 warps
+constexpr int kMaxStages = 8;
+constexpr int kASlot = 32768;                  // 2 chunks x 128 rows x 128 B (FP4 K = 512 packed, or bf16 K = 128)
+constexpr int kSfSlot = 4096;                  // 4 weight atoms + 4 activation atoms
+constexpr int kAtom = 512;
+constexpr int kPieces = 6;                     // e2m1 pieces per activation row
+constexpr int kPieceRows = 8 * kPieces;        // piece rows per slot (8 tokens max)
+constexpr int kStagesPerItem = 2;              // 64 KB of weights per item
+constexpr int kMaxSlots5 = 64;
+constexpr int kMaxT = 8;
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr size_t kSmemMax = 227 * 1024;
+
+enum { PH_GATEUP = 0, PH_DOWN = 1 };
+
+// Workspace (byte offsets, 256-aligned; built on the host by t5_layout).
+struct T5Layout {
+  size_t ints, slot_expert, gate, xq, sfx, part_a, part_as, hq, sfh, hb, part_b, part_bs, total;
+  int KPa, KPas, KPb, KPbs;  // K slices per item kind
+};
+
+struct T5Params {
+  CUtensorMap w[2];   // routed packed FP4 (gate/up: W1, W3; down: W2 in w[0]), UINT8 {128 B, rows, K/256}
+  CUtensorMap s[2];   // shared bf16 (gate/up: sW1, sW3; down: sW2), UINT8 {128 B, rows, 2K/128}
+  CUtensorMap bq;     // routed B operand pieces (packed e2m1), UINT8 {128 B, rows, K/256}
+  CUtensorMap bs;     // shared B operand bf16, UINT8 {128 B, rows, 2K/128}
+  const uint8_t* sfa[2];      // weight scale atoms [E][rows/128][K/128][512]
+  const uint8_t* sfb;         // B-operand scale atoms
+  size_t sfb_slot_stride;     // bytes between slots of sfb (0: shared by all slots)
+  const int32_t* slot_expert;
+  const int32_t* n_slots;
+  float* part;                // routed partials
+  float* part_sh;             // shared partials
+  int* err;
+  int T, phase, n_sh_items;
+  int rows_r, rows_s;         // output rows of a routed / shared matrix
+  int K_r, K_s;               // input features of a routed / shared matrix
+  int KP_r, KP_s;             // K slices per routed / shared item
+  int N_r;                    // MMA N of routed items (piece rows rounded up to 16)
+  int bq_rows_per_slot;       // rows of the routed B operand per slot (0 gate/up: x pieces shared)
+  int nst;                    // stages in the ring
+  int stage_bytes;            // A slot + B slot + scale slot
+  int b_slot;                 // bytes of the B slot (N_r rows x 2 chunks x 128 B, >= 4 KB)
+  const float* slot_gate;     // [kMaxSlots5][kMaxT]
+  uint8_t* hq;                // gate/up output: routed h pieces [slot][48][I/2]
+  uint8_t* sfh;               // gate/up output: their scale atoms [slot][I/128][512]
+  __nv_bfloat16* hb;          // gate/up output: shared h hi/lo [16][Is]
+  __nv_bfloat16* out;         // down output [T][H]
+  float limit;
+};
+
+// Bounded wait: suspended try_waits (the thread resumes when the phase
+// completes), an abort check and a %globaltimer limit between them.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      *abort = 1;
+      atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = wait_or_abort(bar, parity, abort, err) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)mbar_try_wait(bar, parity);
+  return ok != 0;
+}
+
+struct Item {
+  int shared, slot, m, rt, kp;
+};
+
+__device__ __forceinline__ Item decode_item(const T5Params& p, int idx) {
+  Item it;
+  const int mats = p.phase == PH_GATEUP ? 2 : 1;
+  if (idx < p.n_sh_items) {
+    const int RT = p.rows_s / 128;
+    it.shared = 1;
+    it.slot = 0;
+    it.kp = idx % p.KP_s;
+    idx /= p.KP_s;
+    it.rt = idx % RT;
+    it.m = idx / RT;
+  } else {
+    idx -= p.n_sh_items;
+    const int RT = p.rows_r / 128;
+    it.shared = 0;
+    it.kp = idx % p.KP_r;
+    idx /= p.KP_r;
+    it.rt = idx % RT;
+    idx /= RT;
+    it.m = idx % mats;
+    it.slot = idx / mats;
+  }
+  return it;
+}
+
+__device__ __forceinline__ float silu_glu(float g, float u, float limit) {
+  if (limit > 0.0f) {
+    g = fminf(g, limit);
+    u = fminf(fmaxf(u, -limit), limit);
+  }
+  return (g / (1.0f + expf(-g))) * u;
+}
+
+// ue8m0 byte of the scale that maps a block maximum `amax` into (3, 6] (the
+// top of the e2m1 range): 2^(E-2) when the maximum's mantissa is <= 1.5,
+// else 2^(E-1).  Zero blocks get scale 1.
+__device__ __forceinline__ int e2m1_scale(float amax) {
+  const uint32_t b = __float_as_uint(amax);
+  const int ef = (int)(b >> 23);
+  if (ef == 0) return 127;
+  const int s = (b & 0x7FFFFFu) <= 0x400000u ? ef - 2 : ef - 1;
+  return min(max(s, 1), 253);
+}
+__device__ __forceinline__ float scale_of(int sfb) { return __uint_as_float((uint32_t)sfb << 23); }
+__device__ __forceinline__ float inv_scale_of(int sfb) { return __uint_as_float((uint32_t)(254 - sfb) << 23); }
+__device__ __forceinline__ int atom_off(int r, int kb) { return (r & 31) * 16 + (r >> 5) * 4 + kb; }
+
+// ------------------------------------------------------------------ fused tails (one warp, 32 rows)
+// The partial sums of a row are independent loads; they are issued in
+// batches so that many are in flight per lane.
+
+// h of one routed slot for rows r0 + lane of I (one 32-row block) as e2m1
+// pieces: sums the K slices of the gate/up partials, SiLU/clamp, route gate.
+__device__ void tail_h_routed(const T5Params& p, int slot, int r0, int lane) {
+  const int I = p.rows_r, T = p.T, KP = p.KP_r;
+  const int i = r0 + lane;
+  uint8_t* hq = p.hq + (size_t)slot * kPieceRows * (I / 2);
+  uint8_t* sf = p.sfh + ((size_t)slot * (I / 128) + r0 / 128) * kAtom;
+  const float* pg = p.part + (((size_t)slot * 2 + 0) * KP * I + i) * T;
+  const float* pu = p.part + (((size_t)slot * 2 + 1) * KP * I + i) * T;
+  for (int t = 0; t < T; ++t) {
+    float gs[8], us[8];
+#pragma unroll
+    for (int kp = 0; kp < 8; ++kp) {
+      gs[kp] = kp < KP ? __ldcg(pg + (size_t)kp * I * T + t) : 0.0f;
+      us[kp] = kp < KP ? __ldcg(pu + (size_t)kp * I * T + t) : 0.0f;
+    }
+    float g = 0.0f, u = 0.0f;
+#pragma unroll
+    for (int kp = 0; kp < 8; ++kp) {
+      g += gs[kp];
+      u += us[kp];
+    }
+    float r = silu_glu(g, u, p.limit) * p.slot_gate[slot * kMaxT + t];
+#pragma unroll 1
+    for (int pc = 0; pc < kPieces; ++pc) {
+      float am = fabsf(r);
+#pragma unroll
+      for (int d = 16; d; d >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, d));
+      const int sc = e2m1_scale(am);
+      const uint32_t code = tc5::f32x2_to_e2m1x2(r * inv_scale_of(sc), 0.0f) & 0xFu;
+      float q0, q1;
+      tc5::e2m1x2_to_f32x2(code, q0, q1);
+      r = fmaf(-q0, scale_of(sc), r);
+      const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
+      const int row = t * kPieces + pc;
+      if ((lane & 1) == 0) hq[(size_t)row * (I / 2) + i / 2] = (uint8_t)(code | (hi << 4));
+      if (lane == 0) sf[atom_off(row, (r0 & 127) >> 5)] = (uint8_t)sc;
+    }
+  }
+}
+
+// Shared-expert h for rows r0 + lane of Is as bf16 hi/lo (rows 2t, 2t+1).
+__device__ void tail_h_shared(const T5Params& p, int r0, int lane) {
+  const int Is = p.rows_s, T = p.T, KP = p.KP_s;
+  const int i = r0 + lane;
+  for (int t = 0; t < T; ++t) {
+    float g = 0.0f, u = 0.0f;
+    for (int k0 = 0; k0 < KP; k0 += 8) {
+      float gs[8], us[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        gs[k] = k0 + k < KP ? __ldcg(p.part_sh + (((size_t)0 * KP + k0 + k) * Is + i) * T + t) : 0.0f;
+        us[k] = k0 + k < KP ? __ldcg(p.part_sh + (((size_t)1 * KP + k0 + k) * Is + i) * T + t) : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        g += gs[k];
+        u += us[k];
+      }
+    }
+    const float h = silu_glu(g, u, p.limit);
+    const __nv_bfloat16 hi = __float2bfloat16_rn(h);
+    p.hb[(size_t)(2 * t) * Is + i] = hi;
+    p.hb[(size_t)(2 * t + 1) * Is + i] = __float2bfloat16_rn(h - __bfloat162float(hi));
+  }
+}
+
+// Output rows r0 + lane of H: routed slots in ascending expert order (each
+// slot's K slices in order), then the shared expert rounded to bf16.
+__device__ void tail_combine(const T5Params& p, int r0, int lane) {
+  const int H = p.rows_r, T = p.T, ns = *p.n_slots, KP = p.KP_r;
+  const int h = r0 + lane;
+  for (int t = 0; t < T; ++t) {
+    float acc = 0.0f;
+    for (int s0 = 0; s0 < ns; s0 += 4) {
+      float e[4][4];
+#pragma unroll
+      for (int ds = 0; ds < 4; ++ds)
+#pragma unroll
+        for (int kp = 0; kp < 4; ++kp)
+          e[ds][kp] = (s0 + ds < ns && kp < KP)
+                          ? __ldcg(p.part + (((size_t)(s0 + ds) * KP + kp) * H + h) * T + t)
+                          : 0.0f;
+#pragma unroll
+      for (int ds = 0; ds < 4; ++ds) {
+        float es = 0.0f;
+#pragma unroll
+        for (int kp = 0; kp < 4; ++kp) es += e[ds][kp];
+        if (s0 + ds < ns) acc += es;
+      }
+      for (int kp = 4; kp < KP; ++kp)   // K slices beyond 4 (inter > 4096): rare, added in order
+        for (int ds = 0; ds < 4 && s0 + ds < ns; ++ds) acc += __ldcg(p.part + (((size_t)(s0 + ds) * KP + kp) * H + h) * T + t);
+    }
+    if (p.n_sh_items) {
+      float sh = 0.0f;
+      for (int k0 = 0; k0 < p.KP_s; k0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = k0 + k < p.KP_s ? __ldcg(p.part_sh + ((size_t)(k0 + k) * H + h) * T + t) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sh += v[k];
+      }
+      acc += __bfloat162float(__float2bfloat16_rn(sh));
+    }
+    p.out[(size_t)t * H + h] = __float2bfloat16_rn(acc);
+  }
+}
+
+// ------------------------------------------------------------------ gate/up and down GEMM kernel
+
+__global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_constant__ T5Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* ring = smem;                          // nst x [A 32 KB][B b_slot][SF 4 KB]
+  __shared__ __align__(8) uint64_t full[kMaxStages], staged[kMaxStages], empty[kMaxStages], accfull[2], accempty[2],
+      done;
+  const int S = p.nst;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  launch_dependents();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&staged[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], 4);
+    }
+    mbar_init(&done, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tc5::alloc(&tmem_base, 512);
+  __syncthreads();
+  tc5::fence_after();
+  const uint32_t tb = tmem_base;                 // D buffers at columns 0 and 64; scale ring from 128
+  const uint32_t tsf0 = tb + 128;                // 32 columns per stage
+  volatile int* abort = &abort_flag;
+  // the down phase consumes what the gate/up launch produced; its producer
+  // first prefetches weight tiles, every other role waits right away
+  if (p.phase == PH_DOWN && warp != 0) wait_prior_grid();
+  // gate/up: shared items need nothing from prep; routed items do
+  int n_items = p.n_sh_items;
+  bool routed_known = false;
+  auto know_routed = [&]() {
+    if (!routed_known) {
+      if (p.phase == PH_GATEUP || warp == 0) wait_prior_grid();
+      const int mats = p.phase == PH_GATEUP ? 2 : 1;
+      n_items = p.n_sh_items + *p.n_slots * mats * (p.rows_r / 128) * p.KP_r;
+      routed_known = true;
+    }
+  };
+  if (p.n_sh_items == 0 || (p.phase == PH_DOWN && warp != 0)) know_routed();
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int g = 0;
+      // down: issue the weight half of the first stages of this CTA's shared
+      // items before waiting for the gate/up grid; their activation halves
+      // (h, produced by that grid) follow after the wait
+      int pre = 0;
+      if (p.phase == PH_DOWN) {
+        for (int item = blockIdx.x; item < p.n_sh_items && pre < S; item += gridDim.x) {
+          const Item it = decode_item(p, item);
+          for (int j = 0; j < kStagesPerItem && pre < S; ++j, ++pre) {
+            mbar_arrive_expect_tx(&full[pre], kASlot + 2 * 16 * 128);
+            tma_load_3d(ring + pre * p.stage_bytes, &p.s[it.m], 0, it.rt * 128, 2 * (it.kp * kStagesPerItem + j),
+                        &full[pre]);
+          }
+        }
+        know_routed();
+      }
+      for (int item = blockIdx.x;; item += gridDim.x) {
+        if (item >= n_items) {
+          know_routed();
+          if (item >= n_items) break;
+        }
+        const Item it = decode_item(p, item);
+        int e = 0;
+        if (!it.shared) e = p.slot_expert[it.slot];
+        for (int j = 0; j < kStagesPerItem; ++j, ++g) {
+          const int s = g % S;
+          if (g >= S && !wait_or_abort(&empty[s], ((g / S) - 1) & 1, abort, p.err)) goto drain;
+          uint8_t* sa = ring + s * p.stage_bytes;
+          uint8_t* sb = sa + kASlot;
+          uint8_t* sf = sb + p.b_slot;
+          const int kc = it.kp * kStagesPerItem + j;  // stage index along K (two 128-byte chunks each)
+          if (it.shared) {
+            if (g >= pre) {
+              mbar_arrive_expect_tx(&full[s], kASlot + 2 * 16 * 128);
+              tma_load_3d(sa, &p.s[it.m], 0, it.rt * 128, 2 * kc, &full[s]);
+            }
+            tma_load_3d(sb, &p.bs, 0, 0, 2 * kc, &full[s]);
+          } else {
+            mbar_arrive_expect_tx(&full[s], kASlot + 2 * p.N_r * 128 + kSfSlot);
+            tma_load_3d(sa, &p.w[it.m], 0, e * p.rows_r + it.rt * 128, 2 * kc, &full[s]);
+            tma_load_3d(sb, &p.bq, 0, it.slot * p.bq_rows_per_slot, 2 * kc, &full[s]);
+            const int KC = p.K_r / 128;
+            bulk_g2s(sf, p.sfa[it.m] + (((size_t)e * (p.rows_r / 128) + it.rt) * KC + 4 * kc) * kAtom, 4 * kAtom,
+                     &full[s]);
+            bulk_g2s(sf + 4 * kAtom, p.sfb + it.slot * p.sfb_slot_stride + (size_t)(4 * kc) * kAtom, 4 * kAtom,
+                     &full[s]);
+          }
+        }
+      }
+    drain:
+      for (int j = g - S < 0 ? 0 : g - S; j < g; ++j) mbar_wait_bounded(&full[j % S], (j / S) & 1, 200000000ull);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int g = 0, li = 0;
+      for (int item = blockIdx.x;; item += gridDim.x, ++li) {
+        if (item >= n_items) {
+          know_routed();
+          if (item >= n_items) break;
+        }
+        const Item it = decode_item(p, item);
+        const int b = li & 1;
+        if (li >= 2 && !wait_or_abort(&accempty[b], ((li >> 1) - 1) & 1, abort, p.err)) break;
+        tc5::fence_after();
+        const uint32_t dacc = tb + b * 64;
+        for (int j = 0; j < kStagesPerItem; ++j, ++g) {
+          const int s = g % S;
+          if (!wait_or_abort(&full[s], (g / S) & 1, abort, p.err) ||
+              !wait_or_abort(&staged[s], (g / S) & 1, abort, p.err))
+            goto mma_out;
+          tc5::fence_after();
+          const uint32_t sa = smem_u32(ring + s * p.stage_bytes), sb = sa + kASlot;
+          const uint32_t tsf = tsf0 + s * 32;
+          if (it.shared) {
+            const uint32_t idesc = tc5::idesc_bf16(16);
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int sub = 0; sub < 4; ++sub)
+                tc5::mma_bf16(dacc, tc5::sdesc_sw128(sa + c * 16384 + sub * 32),
+                              tc5::sdesc_sw128(sb + c * 16 * 128 + sub * 32), idesc, (j | c | sub) != 0);
+            tc5::commit(&empty[s]);
+          } else {
+            // each 128-byte row chunk = 256 codes = 4 MMAs of K = 64; scale word 2c + kk/2, byte pair kk%2
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                tc5::mma_mxf4(dacc, tc5::sdesc_sw128(sa + c * 16384 + kk * 32),
+                              tc5::sdesc_sw128(sb + c * p.N_r * 128 + kk * 32), tc5::idesc_mxf4(p.N_r, (kk & 1) * 2),
+                              tsf + 4 * (2 * c + (kk >> 1)), tsf + 16 + 4 * (2 * c + (kk >> 1)), (j | c | kk) != 0);
+            tc5::commit(&empty[s]);
+          }
+        }
+        tc5::commit(&accfull[b]);
+      }
+    mma_out:
+      tc5::commit(&done);
+      mbar_wait_bounded(&done, 0, 1000000000ull);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- stagers
+    const int q = warp & 3;
+    int g = 0;
+    for (int item = blockIdx.x;; item += gridDim.x) {
+      if (item >= n_items) {
+        know_routed();
+        if (item >= n_items) break;
+      }
+      const Item it = decode_item(p, item);
+      for (int j = 0; j < kStagesPerItem; ++j, ++g) {
+        const int s = g % S;
+        if (!warp_wait(&full[s], (g / S) & 1, abort, p.err)) goto st_out;
+        if (!it.shared) {
+          const uint4* sf = reinterpret_cast<const uint4*>(ring + s * p.stage_bytes + kASlot + p.b_slot);
+          const uint32_t t = tc5::lane_quarter(tsf0 + s * 32, q);
+#pragma unroll
+          for (int a = 0; a < 8; ++a) {
+            const uint4 v = sf[a * 32 + lane];
+            tc5::st_x4(t + 4 * a, v.x, v.y, v.z, v.w);
+          }
+          tc5::wait_st();
+        }
+        tc5::fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&staged[s]);
+      }
+    }
+  st_out:;
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    int li = 0;
+    for (int item = blockIdx.x;; item += gridDim.x, ++li) {
+      if (item >= n_items) {
+        know_routed();
+        if (item >= n_items) break;
+      }
+      const Item it = decode_item(p, item);
+      const int b = li & 1;
+      if (!warp_wait(&accfull[b], (li >> 1) & 1, abort, p.err)) break;
+      tc5::fence_after();
+      const uint32_t dacc = tc5::lane_quarter(tb + b * 64, q);
+      float v[48];
+      tc5::ld_x16_nowait(dacc, *reinterpret_cast<float(*)[16]>(v));
+      if (!it.shared && p.N_r > 16) tc5::ld_x16_nowait(dacc + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+      if (!it.shared && p.N_r > 32) tc5::ld_x16_nowait(dacc + 32, *reinterpret_cast<float(*)[16]>(v + 32));
+      tc5::wait_ld();
+      tc5::fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accempty[b]);
+      const int row = it.rt * 128 + q * 32 + lane;
+      const int T = p.T;
+      if (it.shared) {
+        float* dst = p.phase == PH_GATEUP
+                         ? p.part_sh + (((size_t)it.m * p.KP_s + it.kp) * p.rows_s + row) * T
+                         : p.part_sh + ((size_t)it.kp * p.rows_s + row) * T;
+        for (int t = 0; t < T; ++t) dst[t] = p.phase == PH_GATEUP ? v[t] : v[2 * t] + v[2 * t + 1];
+      } else {
+        float* dst = p.phase == PH_GATEUP
+                         ? p.part + ((((size_t)it.slot * 2 + it.m) * p.KP_r + it.kp) * p.rows_r + row) * T
+                         : p.part + (((size_t)it.slot * p.KP_r + it.kp) * p.rows_r + row) * T;
+        for (int t = 0; t < T; ++t) {
+          float acc = 0.0f;
+#pragma unroll
+          for (int pc = 0; pc < kPieces; ++pc) acc += v[kPieces * t + pc];
+          dst[t] = acc;
+        }
+      }
+
+    }
+  }
+  tc5::fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc5::fence_after();
+    tc5::dealloc(tb, 512);
+  }
+}
+
+// h between the two GEMM launches: one CTA per 128-row tile of one slot
+// (the last grid row is the shared expert), one row per thread.
+__global__ void __launch_bounds__(128) t5_h_kernel(const __grid_constant__ T5Params p) {
+  wait_prior_grid();
+  launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * 128 + warp * 32;
+  if (blockIdx.y == gridDim.y - 1) {
+    if (p.n_sh_items && r0 < p.rows_s) tail_h_shared(p, r0, lane);
+  } else if ((int)blockIdx.y < *p.n_slots && r0 < p.rows_r) {
+    tail_h_routed(p, blockIdx.y, r0, lane);
+  }
+}
+
+// Output rows after the down launch: one row per thread.
+__global__ void __launch_bounds__(128) t5_combine_kernel(const __grid_constant__ T5Params p) {
+  wait_prior_grid();
+  tail_combine(p, blockIdx.x * 128 + (threadIdx.x >> 5) * 32, threadIdx.x & 31);
+}
+
+// ------------------------------------------------------------------ prep: slots, gates, x pieces
+
+struct PrepArgs {
+  const __nv_bfloat16* x;
+  const int32_t* ids;
+  const float* gates;
+  int T, k, H, E;
+  int32_t* n_slots;
+  int32_t* slot_expert;   // [kMaxSlots5]
+  float* slot_gate;       // [kMaxSlots5][kMaxT]
+  uint8_t* xq;            // [48 piece rows][H/2] packed e2m1 (row t*6+p: piece p of token t)
+  uint8_t* sfx;           // [H/128][512]
+  int* err;
+};
+
+__global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
+  wait_prior_grid();
+  launch_dependents();
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (blockIdx.x == 0 && threadIdx.x < 32) {
+    // distinct valid experts, ascending; one warp, at most 128 entries
+    const int lane = threadIdx.x, n = a.T * a.k;
+    __shared__ int ids[kMaxEntries];
+    __shared__ int first[kMaxEntries];
+    for (int j = lane; j < n; j += 32) {
+      int e = a.ids[j];
+      if (e >= a.E) {
+        atomicOr(a.err, kErrExpertRange);
+        e = -1;
+      }
+      ids[j] = e;
+    }
+    __syncwarp();
+    for (int j = lane; j < n; j += 32) {
+      int f = ids[j] >= 0;
+      for (int i = 0; i < j && f; ++i) f = ids[i] != ids[j];
+      first[j] = f;
+    }
+    __syncwarp();
+    int count = 0;
+    for (int j = 0; j < n; ++j) count += first[j];
+    for (int j = lane; j < n; j += 32) {
+      if (!first[j]) continue;
+      int rank = 0;
+      for (int i = 0; i < n; ++i) rank += first[i] && ids[i] < ids[j];
+      a.slot_expert[rank] = ids[j];
+      for (int t = 0; t < a.T; ++t) {
+        float gt = 0.0f;
+        for (int c = 0; c < a.k; ++c)
+          if (ids[t * a.k + c] == ids[j]) {
+            gt = a.gates[t * a.k + c];
+            break;
+          }
+        a.slot_gate[rank * kMaxT + t] = gt;
+      }
+    }
+    if (lane == 0) *a.n_slots = count;
+  }
+  // x pieces: one thread per (token, 32-block), all 8 token slots written
+  // (rows of tokens >= T are zero); piece rows t * kPieces + p
+  const int nb = a.H / 32;
+  for (int w = tid; w < a.T * nb; w += gridDim.x * blockDim.x) {
+    const int t = w / nb, blk = w % nb;
+    float v[32];
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)t * a.H + blk * 32);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 u = src[c];
+        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+          v[c * 8 + 2 * d] = __uint_as_float(wd[d] << 16);
+          v[c * 8 + 2 * d + 1] = __uint_as_float(wd[d] & 0xFFFF0000u);
+        }
+      }
+    }
+    uint8_t* sf = a.sfx + (size_t)(blk / 4) * kAtom;
+#pragma unroll 1
+    for (int pc = 0; pc < kPieces; ++pc) {
+      float am = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) am = fmaxf(am, fabsf(v[j]));
+      const int sc = e2m1_scale(am);
+      const float inv = inv_scale_of(sc), scl = scale_of(sc);
+      uint32_t packed[4];
+#pragma unroll
+      for (int wd = 0; wd < 4; ++wd) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int c = 0; c < 8; c += 2) {
+          const int j = wd * 8 + c;
+          const uint32_t b = tc5::f32x2_to_e2m1x2(v[j] * inv, v[j + 1] * inv);
+          float q0, q1;
+          tc5::e2m1x2_to_f32x2(b, q0, q1);
+          v[j] = fmaf(-q0, scl, v[j]);
+          v[j + 1] = fmaf(-q1, scl, v[j + 1]);
+          word |= b << (4 * c);
+        }
+        packed[wd] = word;
+      }
+      const int row = t * kPieces + pc;
+      *reinterpret_cast<uint4*>(a.xq + (size_t)row * (a.H / 2) + blk * 16) =
+          make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      sf[atom_off(row, blk & 3)] = (uint8_t)sc;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn5() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// Rows of `row_bytes` bytes viewed as {128 B, rows, row_bytes / 128}, box {128, box_rows, box_chunks}.
+bool map3(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows,
+          uint32_t box_chunks, bool swizzle) {
+  const cuuint64_t dims[3] = {128, rows, row_bytes / 128};
+  const cuuint64_t strides[2] = {row_bytes, 128};
+  const cuuint32_t box[3] = {128, box_rows, box_chunks};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return encode_fn5()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+T5Layout t5_layout(const DsMoeDesc& d, int T) {
+  T5Layout L;
+  const size_t H = d.hidden, I = d.inter, Is = d.shared_w1 ? d.shared_inter : 0;
+  const int S = std::min<int>(T * d.top_k, d.n_experts);
+  L.KPa = (int)(H / (512 * kStagesPerItem));
+  L.KPas = (int)(H / (128 * kStagesPerItem));
+  L.KPb = (int)(I / (512 * kStagesPerItem));
+  L.KPbs = Is ? (int)(Is / (128 * kStagesPerItem)) : 0;
+  size_t o = 0;
+  L.ints = o;        o += 256;
+  L.slot_expert = o; o += up256(kMaxSlots5 * 4);
+  L.gate = o;        o += up256(kMaxSlots5 * kMaxT * 4);
+  L.xq = o;          o += up256(kPieceRows * H / 2);
+  L.sfx = o;         o += up256((H / 128) * kAtom);
+  L.part_a = o;      o += up256((size_t)S * 2 * L.KPa * I * T * 4);
+  L.part_as = o;     o += up256((size_t)2 * L.KPas * Is * T * 4);
+  L.hq = o;          o += up256((size_t)S * kPieceRows * I / 2);
+  L.sfh = o;         o += up256((size_t)S * (I / 128) * kAtom);
+  L.hb = o;          o += up256(16 * Is * 2);
+  L.part_b = o;      o += up256((size_t)S * L.KPb * H * T * 4);
+  L.part_bs = o;     o += up256((size_t)L.KPbs * H * T * 4);
+  L.total = o;
+  return L;
+}
+
+}  // namespace
+
+bool t5_supported(const DecodeArgs& a) {
+  const DsMoeDesc& d = a.d;
+  if (a.x_f32 || d.w1.format != DS_FMT_FP4 || a.tokens < 1 || a.tokens > kMaxT) return false;
+  if (!d.w1.scales_tc || !d.w3.scales_tc || !d.w2.scales_tc) return false;
+  if (d.hidden % 1024 != 0 || d.inter % 1024 != 0) return false;
+  if (d.top_k > 16 || a.max_slots > kMaxSlots5) return false;
+  if ((uint64_t)d.n_experts * d.inter >= (1ull << 31) || (uint64_t)d.n_experts * d.hidden >= (1ull << 31)) return false;
+  const bool sh = d.shared_w1 != nullptr;
+  if (sh && (d.shared_inter % 256 != 0)) return false;
+  if (!ds::aligned(a.x, 16) || !ds::aligned(d.w1.data, 16) || !ds::aligned(d.w3.data, 16) ||
+      !ds::aligned(d.w2.data, 16) || !ds::aligned(d.w1.scales_tc, 16) || !ds::aligned(d.w3.scales_tc, 16) ||
+      !ds::aligned(d.w2.scales_tc, 16))
+    return false;
+  if (sh && (!ds::aligned(d.shared_w1, 16) || !ds::aligned(d.shared_w3, 16) || !ds::aligned(d.shared_w2, 16)))
+    return false;
+  return encode_fn5() != nullptr;
+}
+
+size_t t5_workspace_bytes(const DsMoeDesc& d, int tokens) { return t5_layout(d, tokens).total; }
+
+int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const DsMoeDesc& d = a.d;
+  const int T = a.tokens, H = d.hidden, I = d.inter, E = d.n_experts;
+  const bool sh = d.shared_w1 != nullptr;
+  const int Is = sh ? d.shared_inter : 0;
+  const T5Layout L = t5_layout(d, T);
+  DS_REQUIRE(workspace_bytes >= L.total, DS_EINVAL, "moe_decode: workspace %zu bytes < %zu (tensor-core path)",
+             workspace_bytes, L.total);
+  char* ws = static_cast<char*>(workspace);
+  int32_t* ints = reinterpret_cast<int32_t*>(ws + L.ints);   // [0] error bits, [1] n_slots
+  int32_t* slot_expert = reinterpret_cast<int32_t*>(ws + L.slot_expert);
+  float* slot_gate = reinterpret_cast<float*>(ws + L.gate);
+  uint8_t* xq = reinterpret_cast<uint8_t*>(ws + L.xq);
+  uint8_t* sfx = reinterpret_cast<uint8_t*>(ws + L.sfx);
+  float* part_a = reinterpret_cast<float*>(ws + L.part_a);
+  float* part_as = reinterpret_cast<float*>(ws + L.part_as);
+  uint8_t* hq = reinterpret_cast<uint8_t*>(ws + L.hq);
+  uint8_t* sfh = reinterpret_cast<uint8_t*>(ws + L.sfh);
+  __nv_bfloat16* hb = reinterpret_cast<__nv_bfloat16*>(ws + L.hb);
+  float* part_b = reinterpret_cast<float*>(ws + L.part_b);
+  float* part_bs = reinterpret_cast<float*>(ws + L.part_bs);
+  int* err = a.err;
+  const int S = a.max_slots;
+
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+
+  // 1. prep
+  PrepArgs pa;
+  pa.x = static_cast<const __nv_bfloat16*>(a.x);
+  pa.ids = a.ids;
+  pa.gates = a.gates;
+  pa.T = T;
+  pa.k = d.top_k;
+  pa.H = H;
+  pa.E = E;
+  pa.n_slots = ints + 1;
+  pa.slot_expert = slot_expert;
+  pa.slot_gate = slot_gate;
+  pa.xq = xq;
+  pa.sfx = sfx;
+  pa.err = err;
+  cfg.gridDim = dim3(std::max(1, (T * (H / 32) + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel, pa));
+
+  // 2. gate/up
+  T5Params p;
+  memset(&p, 0, sizeof(p));
+  const int NB = (kPieces * T + 15) / 16 * 16;   // piece rows of the batch, MMA N
+  bool ok = map3(&p.w[0], d.w1.data, (uint64_t)E * I, H / 2, 128, 2, true) &&
+            map3(&p.w[1], d.w3.data, (uint64_t)E * I, H / 2, 128, 2, true) &&
+            map3(&p.bq, xq, kPieceRows, H / 2, NB, 2, true) &&
+            (!sh || (map3(&p.s[0], d.shared_w1, Is, (uint64_t)H * 2, 128, 2, true) &&
+                     map3(&p.s[1], d.shared_w3, Is, (uint64_t)H * 2, 128, 2, true) &&
+                     map3(&p.bs, a.x, T, (uint64_t)H * 2, 16, 2, true)));
+  DS_REQUIRE(ok, DS_ECUDA, "moe_decode: tensor map encoding failed (tensor-core gate/up)");
+  p.sfa[0] = static_cast<const uint8_t*>(d.w1.scales_tc);
+  p.sfa[1] = static_cast<const uint8_t*>(d.w3.scales_tc);
+  p.sfb = sfx;
+  p.sfb_slot_stride = 0;
+  p.slot_expert = slot_expert;
+  p.n_slots = ints + 1;
+  p.part = part_a;
+  p.part_sh = part_as;
+  p.err = err;
+  p.T = T;
+  p.phase = PH_GATEUP;
+  p.rows_r = I;
+  p.rows_s = Is;
+  p.K_r = H;
+  p.K_s = H;
+  p.KP_r = L.KPa;
+  p.KP_s = L.KPas;
+  p.N_r = NB;
+  p.bq_rows_per_slot = 0;
+  p.b_slot = std::max(4096, NB * 2 * 128);
+  p.stage_bytes = kASlot + p.b_slot + kSfSlot;
+  p.nst = std::min<int>(kMaxStages, (int)((kSmemMax - 1024) / p.stage_bytes));
+  const size_t smem = 1024 + (size_t)p.nst * p.stage_bytes;
+  p.n_sh_items = sh ? 2 * (Is / 128) * L.KPas : 0;
+  p.slot_gate = slot_gate;
+  p.hq = hq;
+  p.sfh = sfh;
+  p.hb = hb;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.limit = d.swiglu_limit;
+  DS_CHECK_CUDA(cudaFuncSetAttribute(t5_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cfg.gridDim = dim3(ds::sm_count());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_gemm_kernel, p));
+
+  // 3. h
+  cfg.gridDim = dim3(std::max(I, Is) / 128, S + 1);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_h_kernel, p));
+
+  // 4. down
+  T5Params q = p;
+  ok = map3(&q.w[0], d.w2.data, (uint64_t)E * H, I / 2, 128, 2, true) &&
+       map3(&q.bq, hq, (uint64_t)S * kPieceRows, I / 2, NB, 2, true) &&
+       (!sh || (map3(&q.s[0], d.shared_w2, H, (uint64_t)Is * 2, 128, 2, true) &&
+                map3(&q.bs, hb, 16, (uint64_t)Is * 2, 16, 2, true)));
+  DS_REQUIRE(ok, DS_ECUDA, "moe_decode: tensor map encoding failed (tensor-core down)");
+  q.sfa[0] = static_cast<const uint8_t*>(d.w2.scales_tc);
+  q.sfa[1] = nullptr;
+  q.sfb = sfh;
+  q.sfb_slot_stride = (size_t)(I / 128) * kAtom;
+  q.part = part_b;
+  q.part_sh = part_bs;
+  q.phase = PH_DOWN;
+  q.rows_r = H;
+  q.rows_s = H;
+  q.K_r = I;
+  q.K_s = Is;
+  q.KP_r = L.KPb;
+  q.KP_s = L.KPbs;
+  q.N_r = NB;
+  q.bq_rows_per_slot = kPieceRows;
+  q.n_sh_items = sh ? (H / 128) * L.KPbs : 0;
+  cfg.gridDim = dim3(ds::sm_count());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_gemm_kernel, q));
+
+  // 5. combine
+  cfg.gridDim = dim3(H / 128);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_combine_kernel, q));
+
+  return DS_OK;
+}
+
+}  // namespace decode
+}  // namespace ds

@@ -17,6 +17,7 @@
 //   * the accumulator of an M = 128 MMA: row m in lane m, column n in column n.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include "ptx.cuh"
@@ -49,6 +50,55 @@ __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc, ui
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Instruction descriptor, kind::mxf4 block-scaled (scale_vec::2X), M = 128,
+// A = B = E2M1, ue8m0 scales, K = 64; sf_id (0 or 2) picks the byte pair of
+// the 4-block scale word that this K step uses.
+__device__ __forceinline__ uint32_t idesc_mxf4(int n, uint32_t sf_id) {
+  return (sf_id << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | (8u << 24) | (sf_id << 29);
+}
+
+// D (+)= A * B, both packed e2m1 (two codes per byte, K-major, 128-byte swizzle), K = 64.
+__device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// f32 pair -> e2m1 pair (round to nearest even, saturating to +-6): lo in
+// bits 0..3, hi in bits 4..7.
+__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{ .reg .b8 t; cvt.rn.satfinite.e2m1x2.f32 t, %1, %2; cvt.u32.u8 %0, t; }" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// e2m1 pair (bits 0..7) -> two f32 (exact).
+__device__ __forceinline__ void e2m1x2_to_f32x2(uint32_t b, float& lo, float& hi) {
+  uint32_t h2;
+  asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(h2) : "r"(b));
+  lo = __half2float(__ushort_as_half((uint16_t)(h2 & 0xFFFFu)));
+  hi = __half2float(__ushort_as_half((uint16_t)(h2 >> 16)));
+}
+
+// Instruction descriptor, kind::f16 with bf16 A and B, f32 accumulate, M = 128.
+__device__ __forceinline__ uint32_t idesc_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | (8u << 24);
+}
+
+// D (+)= A * B, bf16 operands in shared memory (K = 16 per instruction).
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 

@@ -23,7 +23,7 @@ DS_ROUTE_SOFTMAX, DS_ROUTE_SQRTSOFTPLUS, DS_ROUTE_SCORES = 0, 1, 2
 
 class DsExpertBank(Structure):
     _fields_ = [("format", c_int32), ("n_experts", c_int32), ("rows", c_int32), ("cols", c_int32),
-                ("data", c_void_p), ("scales", c_void_p), ("biases", c_void_p)]
+                ("data", c_void_p), ("scales", c_void_p), ("biases", c_void_p), ("scales_tc", c_void_p)]
 
 
 class DsMoeDesc(Structure):
@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "ds_moe_align_capacity": (c_int, [c_int64, c_int, c_int, c_int, POINTER(c_int64), POINTER(c_int64)]),
     "ds_moe_align": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_int64, c_void_p, c_int64,
                              c_void_p, c_void_p]),
+    "ds_fp4_scale_atoms": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p]),
     "ds_grouped_scales_size": (c_int, [POINTER(DsMoeDesc), POINTER(c_size_t), POINTER(c_size_t)]),
     "ds_grouped_prepare_scales": (c_int, [POINTER(DsMoeDesc), c_void_p, c_void_p, c_void_p]),
     "ds_grouped_ffn_workspace_size": (c_int, [POINTER(DsMoeDesc), c_int64, POINTER(c_size_t)]),

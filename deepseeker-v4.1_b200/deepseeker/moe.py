@@ -87,6 +87,7 @@ class ExpertBank:
     data: torch.Tensor
     scales: torch.Tensor
     biases: torch.Tensor | None = None
+    scales_tc: torch.Tensor | None = None   # FP4: tensor-core scale atoms (prepare_atoms)
 
     @property
     def n_experts(self) -> int:
@@ -121,7 +122,19 @@ class ExpertBank:
 
     def c_struct(self) -> _abi.DsExpertBank:
         return _abi.DsExpertBank(self.fmt, self.n_experts, self.rows, self.cols, self.data.data_ptr(),
-                                 self.scales.data_ptr(), 0 if self.biases is None else self.biases.data_ptr())
+                                 self.scales.data_ptr(), 0 if self.biases is None else self.biases.data_ptr(),
+                                 0 if self.scales_tc is None else self.scales_tc.data_ptr())
+
+    def prepare_atoms(self) -> "ExpertBank":
+        """FP4: build the tensor-core scale atoms once (same byte count as the scales)."""
+        if self.fmt != _abi.DS_FMT_FP4:
+            raise NotImplementedError("scale atoms exist for FP4 banks only")
+        if self.scales_tc is None:
+            atoms = torch.empty_like(self.scales)
+            _abi.call("ds_fp4_scale_atoms", ptr(self.scales), self.n_experts, self.rows, self.cols, ptr(atoms),
+                      stream_handle(self.scales.device))
+            self.scales_tc = atoms
+        return self
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.data, self.scales, self.biases) if t is not None)
@@ -143,6 +156,12 @@ class MoEWeights:
     @property
     def hidden(self) -> int:
         return self.w1.cols
+
+    def prepare_tc(self) -> "MoEWeights":
+        """FP4 layers: prepare the scale atoms the tcgen05 decode kernels read."""
+        for b in (self.w1, self.w3, self.w2):
+            b.prepare_atoms()
+        return self
 
     @property
     def inter(self) -> int:

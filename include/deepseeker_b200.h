@@ -138,6 +138,10 @@ typedef struct DsExpertBank {
   const void* data;   /* FP4 [E,N,K/2] u8 | Q3 [E,N,K*3/32] u32 | BF16 [E,N,K] */
   const void* scales; /* FP4 [E,N,K/32] u8 | Q3 [E,N,K/64] f16 | BF16 NULL     */
   const void* biases; /* Q3 [E,N,K/64] f16 | otherwise NULL                   */
+  const void* scales_tc; /* FP4 only, optional: the scales re-laid into tensor-
+                            core atoms by ds_fp4_scale_atoms; when w1, w3 and w2
+                            all carry them, ds_moe_decode runs its tcgen05
+                            kernels.  NULL otherwise.                         */
 } DsExpertBank;
 
 typedef struct DsMoeDesc {
@@ -198,6 +202,14 @@ int ds_moe_align(const int32_t* topk_ids, int64_t m, int k, int n_experts, int b
                  int64_t blocks_cap, int32_t* n_pad, void* stream);
 
 /* ---- batched grouped expert FFN (FP4 banks, tcgen05) ------------------- */
+
+/* FP4 bank scales [E, rows, cols/32] (ue8m0) -> tensor-core scale atoms
+ * [E][rows/128][cols/128][512 B]: byte (r%32)*16 + (r/32)*4 + b of an atom is
+ * the scale of row r, k-block b of that 128 x 128 tile.  rows and cols must be
+ * multiples of 128; atoms holds E*rows*cols/32 bytes (the size of the scales).
+ * Run once per resident bank; set DsExpertBank.scales_tc to the result. */
+int ds_fp4_scale_atoms(const void* scales, int64_t n_experts, int rows, int cols, void* atoms,
+                       void* stream);
 
 /* Bytes of the re-laid-out block scales the grouped kernels read: W1 and W3
  * together (w13_bytes) and W2 (w2_bytes); same totals as the bank scales. */
