@@ -547,12 +547,25 @@ def run_decode(args) -> dict:
     ws = moe._workspace(dev, moe.decode_workspace_bytes(layers[0], tokens, K_TOP))
     stream = torch.cuda.current_stream(dev)
 
-    # routing (device) + decode for step i on layer i % L
+    # routing (device) + decode for step i on layer i % L, replayed from one
+    # CUDA graph per layer (moe.DecodeGraph); the step's x and logits are
+    # copied into the graph's input buffers first
+    use_graph = os.environ.get("DEEPSEEKER_BENCH_NO_GRAPH") != "1"
+    graphs = [moe.DecodeGraph(layer, tokens, K_TOP, dev) for layer in layers] if use_graph else None
+
     def step(i, ev=None):
-        w, ids = moe.route_softmax_topk(logits[i], K_TOP)
-        if ev is not None:
-            ev[0].record(stream)
-        moe.moe_decode(xs[i], layers[i % L], ids, w, out=outs[i % L], workspace=ws)
+        if use_graph:
+            gr = graphs[i % L]
+            gr.x.copy_(xs[i])
+            gr.logits.copy_(logits[i])
+            if ev is not None:
+                ev[0].record(stream)
+            gr.replay()
+        else:
+            w, ids = moe.route_softmax_topk(logits[i], K_TOP)
+            if ev is not None:
+                ev[0].record(stream)
+            moe.moe_decode(xs[i], layers[i % L], ids, w, out=outs[i % L], workspace=ws)
         if ev is not None:
             ev[1].record(stream)
 
@@ -607,11 +620,17 @@ def run_decode(args) -> dict:
     do = torch.empty(tokens, H, dtype=torch.bfloat16, device=dev)
 
     def e2e_step(s):
-        dx.copy_(pin_x[s], non_blocking=True)
-        dl.copy_(pin_l[s], non_blocking=True)
-        w, ids = moe.route_softmax_topk(dl, K_TOP)
-        moe.moe_decode(dx, layers[s % L], ids, w, out=do, workspace=ws)
-        pin_o[s].copy_(do, non_blocking=True)
+        if use_graph:
+            gr = graphs[s % L]
+            gr.x.copy_(pin_x[s], non_blocking=True)
+            gr.logits.copy_(pin_l[s], non_blocking=True)
+            pin_o[s].copy_(gr.replay(), non_blocking=True)
+        else:
+            dx.copy_(pin_x[s], non_blocking=True)
+            dl.copy_(pin_l[s], non_blocking=True)
+            w, ids = moe.route_softmax_topk(dl, K_TOP)
+            moe.moe_decode(dx, layers[s % L], ids, w, out=do, workspace=ws)
+            pin_o[s].copy_(do, non_blocking=True)
         stream.synchronize()
     for s in range(min(args.warmup, e2e_steps)):
         e2e_step(s)

@@ -40,6 +40,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 #include "moe_decode.cuh"
 #include "ptx.cuh"
@@ -62,7 +63,7 @@ constexpr int kStagesPerItem = 2;              // 64 KB of weights per item
 constexpr int kMaxSlots5 = 64;
 constexpr int kMaxT = 8;
 constexpr uint64_t kWaitNs = 2000000000ull;
-constexpr size_t kSmemMax = 227 * 1024;
+constexpr size_t kSmemMax = 225 * 1024;   // dynamic shared memory cap (leaves room for the static part)
 
 enum { PH_GATEUP = 0, PH_DOWN = 1 };
 
@@ -396,34 +397,36 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      int g = 0, li = 0;
+      // ring position kept incrementally (no division in the issue loop);
+      // the stagers arrive on staged[s] only after observing full[s]
+      int s = 0, ph = 0, li = 0;
+      const uint32_t ring0 = smem_u32(ring);
+      const uint32_t idesc_sh = tc5::idesc_bf16(16);
+      uint32_t idesc_r[2];
+      idesc_r[0] = tc5::idesc_mxf4(p.N_r, 0);
+      idesc_r[1] = tc5::idesc_mxf4(p.N_r, 2);
+      const uint32_t bchunk = (uint32_t)p.N_r * 128;
       for (int item = blockIdx.x;; item += gridDim.x, ++li) {
         if (item >= n_items) {
           know_routed();
           if (item >= n_items) break;
         }
-        const Item it = decode_item(p, item);
+        const bool shared = item < p.n_sh_items;
         const int b = li & 1;
         if (li >= 2 && !wait_or_abort(&accempty[b], ((li >> 1) - 1) & 1, abort, p.err)) break;
-        tc5::fence_after();
         const uint32_t dacc = tb + b * 64;
-        for (int j = 0; j < kStagesPerItem; ++j, ++g) {
-          const int s = g % S;
-          if (!wait_or_abort(&full[s], (g / S) & 1, abort, p.err) ||
-              !wait_or_abort(&staged[s], (g / S) & 1, abort, p.err))
-            goto mma_out;
+        for (int j = 0; j < kStagesPerItem; ++j) {
+          if (!wait_or_abort(&staged[s], ph, abort, p.err)) goto mma_out;
           tc5::fence_after();
-          const uint32_t sa = smem_u32(ring + s * p.stage_bytes), sb = sa + kASlot;
+          const uint32_t sa = ring0 + s * p.stage_bytes, sb = sa + kASlot;
           const uint32_t tsf = tsf0 + s * 32;
-          if (it.shared) {
-            const uint32_t idesc = tc5::idesc_bf16(16);
+          if (shared) {
 #pragma unroll
             for (int c = 0; c < 2; ++c)
 #pragma unroll
               for (int sub = 0; sub < 4; ++sub)
                 tc5::mma_bf16(dacc, tc5::sdesc_sw128(sa + c * 16384 + sub * 32),
-                              tc5::sdesc_sw128(sb + c * 16 * 128 + sub * 32), idesc, (j | c | sub) != 0);
-            tc5::commit(&empty[s]);
+                              tc5::sdesc_sw128(sb + c * 16 * 128 + sub * 32), idesc_sh, (j | c | sub) != 0);
           } else {
             // each 128-byte row chunk = 256 codes = 4 MMAs of K = 64; scale word 2c + kk/2, byte pair kk%2
 #pragma unroll
@@ -431,9 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
                 tc5::mma_mxf4(dacc, tc5::sdesc_sw128(sa + c * 16384 + kk * 32),
-                              tc5::sdesc_sw128(sb + c * p.N_r * 128 + kk * 32), tc5::idesc_mxf4(p.N_r, (kk & 1) * 2),
+                              tc5::sdesc_sw128(sb + c * bchunk + kk * 32), idesc_r[kk & 1],
                               tsf + 4 * (2 * c + (kk >> 1)), tsf + 16 + 4 * (2 * c + (kk >> 1)), (j | c | kk) != 0);
-            tc5::commit(&empty[s]);
+          }
+          tc5::commit(&empty[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
           }
         }
         tc5::commit(&accfull[b]);
@@ -445,17 +452,16 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
   } else if (warp < 6) {
     // ---------------------------------------------------------------- stagers
     const int q = warp & 3;
-    int g = 0;
+    int s = 0, ph = 0;
     for (int item = blockIdx.x;; item += gridDim.x) {
       if (item >= n_items) {
         know_routed();
         if (item >= n_items) break;
       }
-      const Item it = decode_item(p, item);
-      for (int j = 0; j < kStagesPerItem; ++j, ++g) {
-        const int s = g % S;
-        if (!warp_wait(&full[s], (g / S) & 1, abort, p.err)) goto st_out;
-        if (!it.shared) {
+      const bool shared = item < p.n_sh_items;
+      for (int j = 0; j < kStagesPerItem; ++j) {
+        if (!warp_wait(&full[s], ph, abort, p.err)) goto st_out;
+        if (!shared) {
           const uint4* sf = reinterpret_cast<const uint4*>(ring + s * p.stage_bytes + kASlot + p.b_slot);
           const uint32_t t = tc5::lane_quarter(tsf0 + s * 32, q);
 #pragma unroll
@@ -468,6 +474,10 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
         tc5::fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&staged[s]);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
       }
     }
   st_out:;
@@ -680,6 +690,24 @@ bool map3(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, u
 
 size_t up256(size_t v) { return (v + 255) / 256 * 256; }
 
+// Tensor maps of one call that do not depend on x, cached by what they
+// encode (bank pointers, geometry, workspace, tokens, slots): a layer keeps
+// its banks and a decode loop its workspace, so steady state encodes only
+// the x map.
+struct MapSet {
+  const void* key[12];
+  int geo[8];
+  CUtensorMap w1, w3, w2, sw1, sw3, sw2, xq, hq, hb;
+};
+constexpr int kMapCache = 32;
+std::mutex g_map_mu;
+MapSet g_maps[kMapCache];
+int g_map_n = 0, g_map_next = 0;
+
+bool same_key(const MapSet& m, const void* const* k, const int* geo) {
+  return memcmp(m.key, k, sizeof(m.key)) == 0 && memcmp(m.geo, geo, sizeof(m.geo)) == 0;
+}
+
 T5Layout t5_layout(const DsMoeDesc& d, int T) {
   T5Layout L;
   const size_t H = d.hidden, I = d.inter, Is = d.shared_w1 ? d.shared_inter : 0;
@@ -783,13 +811,47 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   T5Params p;
   memset(&p, 0, sizeof(p));
   const int NB = (kPieces * T + 15) / 16 * 16;   // piece rows of the batch, MMA N
-  bool ok = map3(&p.w[0], d.w1.data, (uint64_t)E * I, H / 2, 128, 2, true) &&
-            map3(&p.w[1], d.w3.data, (uint64_t)E * I, H / 2, 128, 2, true) &&
-            map3(&p.bq, xq, kPieceRows, H / 2, NB, 2, true) &&
-            (!sh || (map3(&p.s[0], d.shared_w1, Is, (uint64_t)H * 2, 128, 2, true) &&
-                     map3(&p.s[1], d.shared_w3, Is, (uint64_t)H * 2, 128, 2, true) &&
-                     map3(&p.bs, a.x, T, (uint64_t)H * 2, 16, 2, true)));
-  DS_REQUIRE(ok, DS_ECUDA, "moe_decode: tensor map encoding failed (tensor-core gate/up)");
+  MapSet ms;
+  {
+    const void* key[12] = {d.w1.data, d.w3.data, d.w2.data, d.shared_w1, d.shared_w3, d.shared_w2,
+                           workspace, nullptr, nullptr, nullptr, nullptr, nullptr};
+    const int geo[8] = {H, I, E, Is, T, S, 0, 0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    key[7] = reinterpret_cast<const void*>((uintptr_t)dev + 1);
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    int hit = -1;
+    for (int i = 0; i < g_map_n; ++i)
+      if (same_key(g_maps[i], key, geo)) hit = i;
+    if (hit >= 0) {
+      ms = g_maps[hit];
+    } else {
+      memset(&ms, 0, sizeof(ms));
+      memcpy(ms.key, key, sizeof(key));
+      memcpy(ms.geo, geo, sizeof(geo));
+      bool ok = map3(&ms.w1, d.w1.data, (uint64_t)E * I, H / 2, 128, 2, true) &&
+                map3(&ms.w3, d.w3.data, (uint64_t)E * I, H / 2, 128, 2, true) &&
+                map3(&ms.w2, d.w2.data, (uint64_t)E * H, I / 2, 128, 2, true) &&
+                map3(&ms.xq, xq, kPieceRows, H / 2, NB, 2, true) &&
+                map3(&ms.hq, hq, (uint64_t)S * kPieceRows, I / 2, NB, 2, true) &&
+                (!sh || (map3(&ms.sw1, d.shared_w1, Is, (uint64_t)H * 2, 128, 2, true) &&
+                         map3(&ms.sw3, d.shared_w3, Is, (uint64_t)H * 2, 128, 2, true) &&
+                         map3(&ms.sw2, d.shared_w2, H, (uint64_t)Is * 2, 128, 2, true) &&
+                         map3(&ms.hb, hb, 16, (uint64_t)Is * 2, 16, 2, true)));
+      DS_REQUIRE(ok, DS_ECUDA, "moe_decode: tensor map encoding failed (tensor-core path)");
+      const int slot = g_map_n < kMapCache ? g_map_n++ : (g_map_next++ % kMapCache);
+      g_maps[slot] = ms;
+    }
+  }
+  p.w[0] = ms.w1;
+  p.w[1] = ms.w3;
+  p.bq = ms.xq;
+  if (sh) {
+    p.s[0] = ms.sw1;
+    p.s[1] = ms.sw3;
+    DS_REQUIRE(map3(&p.bs, a.x, T, (uint64_t)H * 2, 16, 2, true), DS_ECUDA,
+               "moe_decode: tensor map encoding failed (x)");
+  }
   p.sfa[0] = static_cast<const uint8_t*>(d.w1.scales_tc);
   p.sfa[1] = static_cast<const uint8_t*>(d.w3.scales_tc);
   p.sfb = sfx;
@@ -820,7 +882,9 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   p.hb = hb;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.limit = d.swiglu_limit;
-  DS_CHECK_CUDA(cudaFuncSetAttribute(t5_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  static const cudaError_t attr_rc =
+      cudaFuncSetAttribute(t5_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemMax);
+  DS_CHECK_CUDA(attr_rc);
   cfg.gridDim = dim3(ds::sm_count());
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
@@ -834,11 +898,12 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
 
   // 4. down
   T5Params q = p;
-  ok = map3(&q.w[0], d.w2.data, (uint64_t)E * H, I / 2, 128, 2, true) &&
-       map3(&q.bq, hq, (uint64_t)S * kPieceRows, I / 2, NB, 2, true) &&
-       (!sh || (map3(&q.s[0], d.shared_w2, H, (uint64_t)Is * 2, 128, 2, true) &&
-                map3(&q.bs, hb, 16, (uint64_t)Is * 2, 16, 2, true)));
-  DS_REQUIRE(ok, DS_ECUDA, "moe_decode: tensor map encoding failed (tensor-core down)");
+  q.w[0] = ms.w2;
+  q.bq = ms.hq;
+  if (sh) {
+    q.s[0] = ms.sw2;
+    q.bs = ms.hb;
+  }
   q.sfa[0] = static_cast<const uint8_t*>(d.w2.scales_tc);
   q.sfa[1] = nullptr;
   q.sfb = sfh;

@@ -35,12 +35,14 @@ __device__ __forceinline__ bool beats(const KeyIdx& a, const KeyIdx& b, bool tie
 // kernel on the stream (the MoE layer, launched with programmatic stream
 // serialisation) start its prologue; that kernel waits for this one before
 // reading the routing.
+// kPer = keys per lane (n_experts <= 32 * kPer), a compile-time bound so the
+// per-round scans cover only the live keys.
+template <int kPer>
 __global__ void __launch_bounds__(32)
 route_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int n_experts,
                   int top_k, int kind, float route_scale, int32_t* __restrict__ ids,
                   float* __restrict__ weights) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  constexpr int kPer = kMaxExperts / 32;
   const int row = blockIdx.x, lane = threadIdx.x;
   const float* lg = logits + (int64_t)row * n_experts;
   const bool ties_high = (kind != DS_ROUTE_SOFTMAX);
@@ -141,8 +143,21 @@ extern "C" int ds_route_topk(const float* logits, const float* bias, int64_t row
   if (rows == 0) return DS_OK;
   DS_REQUIRE(rows <= 0x7fffffff, DS_EINVAL, "route_topk: too many rows");
   DS_REQUIRE(logits && ids && weights, DS_EINVAL, "route_topk: null pointer");
-  route_topk_kernel<<<(unsigned)rows, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned g = (unsigned)rows;
+  const int per = (n_experts + 31) / 32;
+  if (per <= 1)
+    route_topk_kernel<1><<<g, 32, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
+  else if (per <= 2)
+    route_topk_kernel<2><<<g, 32, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
+  else if (per <= 4)
+    route_topk_kernel<4><<<g, 32, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
+  else if (per <= 8)
+    route_topk_kernel<8><<<g, 32, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
+  else if (per <= 16)
+    route_topk_kernel<16><<<g, 32, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
+  else
+    route_topk_kernel<32><<<g, 32, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
   DS_CHECK_LAUNCH("route_topk_kernel");
   return DS_OK;
 }

@@ -40,15 +40,22 @@ def sqrtsoftplus_scores(x: torch.Tensor, gate_w: torch.Tensor) -> torch.Tensor:
 
 
 def _route(inp: torch.Tensor, bias: torch.Tensor | None, top_k: int, kind: int,
-           route_scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+           route_scale: float, out: tuple[torch.Tensor, torch.Tensor] | None = None
+           ) -> tuple[torch.Tensor, torch.Tensor]:
     inp = require_cuda(inp, "router input", torch.float32)
     if inp.dim() != 2:
         raise ValueError("router input must be [rows, n_experts]")
     rows, n_exp = inp.shape
     if bias is not None:
         bias = require_cuda(bias.float(), "bias")
-    ids = torch.empty((rows, top_k), dtype=torch.int32, device=inp.device)
-    w = torch.empty((rows, top_k), dtype=torch.float32, device=inp.device)
+    if out is not None:
+        w, ids = out
+        if (w.shape != (rows, top_k) or ids.shape != (rows, top_k) or w.dtype != torch.float32
+                or ids.dtype != torch.int32 or not (w.is_contiguous() and ids.is_contiguous())):
+            raise ValueError("out must be (weights f32 [rows, k], ids int32 [rows, k]), contiguous")
+    else:
+        ids = torch.empty((rows, top_k), dtype=torch.int32, device=inp.device)
+        w = torch.empty((rows, top_k), dtype=torch.float32, device=inp.device)
     _abi.call("ds_route_topk", ptr(inp), ptr(bias), rows, n_exp, top_k, kind, ctypes.c_float(route_scale),
               ptr(ids), ptr(w), stream_handle(inp.device))
     return w, ids
@@ -69,9 +76,12 @@ def route_sqrtsoftplus(logits: torch.Tensor, bias: torch.Tensor | None, top_k: i
     return _route(logits, bias, top_k, _abi.DS_ROUTE_SQRTSOFTPLUS, route_scale)
 
 
-def route_softmax_topk(logits: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Softmax over experts, top-k (ties -> lower id), gates renormalised to 1."""
-    return _route(logits, None, top_k, _abi.DS_ROUTE_SOFTMAX, 1.0)
+def route_softmax_topk(logits: torch.Tensor, top_k: int,
+                       out: tuple[torch.Tensor, torch.Tensor] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Softmax over experts, top-k (ties -> lower id), gates renormalised to 1.
+
+    out: optional preallocated (weights, ids) to write into."""
+    return _route(logits, None, top_k, _abi.DS_ROUTE_SOFTMAX, 1.0, out)
 
 
 # ------------------------------------------------------------------ banks
@@ -151,7 +161,8 @@ class MoEWeights:
     shared_w2: torch.Tensor | None = None    # [H, Is] bf16
     swiglu_limit: float = 10.0
     route_before_down: bool = True
-    _desc: _abi.DsMoeDesc | None = field(default=None, repr=False)
+    _descs: dict = field(default_factory=dict, repr=False)
+    _ws_bytes: dict = field(default_factory=dict, repr=False)
 
     @property
     def hidden(self) -> int:
@@ -161,7 +172,25 @@ class MoEWeights:
         """FP4 layers: prepare the scale atoms the tcgen05 decode kernels read."""
         for b in (self.w1, self.w3, self.w2):
             b.prepare_atoms()
+        self._descs.clear()
+        self._ws_bytes.clear()
         return self
+
+    def cached_desc(self, top_k: int) -> _abi.DsMoeDesc:
+        """desc(top_k), built once per top_k (the banks are immutable once resident)."""
+        d = self._descs.get(top_k)
+        if d is None:
+            d = self._descs[top_k] = self.desc(top_k)
+        return d
+
+    def decode_workspace_bytes(self, tokens: int, top_k: int) -> int:
+        key = (tokens, top_k)
+        n = self._ws_bytes.get(key)
+        if n is None:
+            c = ctypes.c_size_t(0)
+            _abi.call("ds_moe_decode_workspace_size", ctypes.byref(self.cached_desc(top_k)), tokens, ctypes.byref(c))
+            n = self._ws_bytes[key] = c.value
+        return n
 
     @property
     def inter(self) -> int:
@@ -207,10 +236,7 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
 
 
 def decode_workspace_bytes(weights: MoEWeights, tokens: int, top_k: int) -> int:
-    n = ctypes.c_size_t(0)
-    d = weights.desc(top_k)
-    _abi.call("ds_moe_decode_workspace_size", ctypes.byref(d), tokens, ctypes.byref(n))
-    return n.value
+    return weights.decode_workspace_bytes(tokens, top_k)
 
 
 def moe_decode(x: torch.Tensor, weights: MoEWeights, topk_ids: torch.Tensor, topk_w: torch.Tensor,
@@ -230,10 +256,13 @@ def moe_decode(x: torch.Tensor, weights: MoEWeights, topk_ids: torch.Tensor, top
     k = topk_ids.shape[1]
     if topk_ids.shape != (T, k) or topk_w.shape != (T, k):
         raise ValueError("topk_ids / topk_w must be [T, k]")
-    d = weights.desc(k)
-    need = ctypes.c_size_t(0)
-    _abi.call("ds_moe_decode_workspace_size", ctypes.byref(d), T, ctypes.byref(need))
-    ws = workspace if workspace is not None else _workspace(x.device, need.value)
+    d = weights.cached_desc(k)
+    if (bool(d.route_before_down) != bool(weights.route_before_down)
+            or d.swiglu_limit != ctypes.c_float(weights.swiglu_limit or 0.0).value):
+        weights._descs.clear()
+        d = weights.cached_desc(k)
+    need = weights.decode_workspace_bytes(T, k)
+    ws = workspace if workspace is not None else _workspace(x.device, need)
     if out is None:
         out = torch.empty_like(x)
     xdt = _abi.DS_F32 if x.dtype == torch.float32 else _abi.DS_BF16
@@ -271,3 +300,38 @@ def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None
         r1 = min(xb.shape[0], r0 + MAX_DECODE_TOKENS)
         moe_decode(xb[r0:r1], weights, idx[r0:r1].contiguous(), w[r0:r1].contiguous(), out=out[r0:r1])
     return out.reshape(x.shape).to(x.dtype)
+
+
+class DecodeGraph:
+    """Softmax top-k routing + ``moe_decode`` for one resident layer and a fixed
+    token count, captured once into a CUDA graph over static device buffers.
+
+    A decode loop writes the step's activations into ``x`` and router logits
+    into ``logits`` (device copies, or host copies from pinned memory), calls
+    ``replay()`` and reads ``out``: one graph launch per layer instead of the
+    router + decode launches and their host-side argument handling.
+    """
+
+    def __init__(self, weights: MoEWeights, tokens: int, top_k: int, device: torch.device | str | None = None):
+        device = torch.device(device) if device is not None else weights.w1.data.device
+        self.weights, self.tokens, self.top_k = weights, tokens, top_k
+        H, E = weights.hidden, weights.n_experts
+        self.x = torch.zeros(tokens, H, dtype=torch.bfloat16, device=device)
+        self.logits = torch.zeros(tokens, E, dtype=torch.float32, device=device)
+        self.w = torch.empty(tokens, top_k, dtype=torch.float32, device=device)
+        self.ids = torch.empty(tokens, top_k, dtype=torch.int32, device=device)
+        self.out = torch.empty(tokens, H, dtype=torch.bfloat16, device=device)
+        self.workspace = torch.empty(weights.decode_workspace_bytes(tokens, top_k), dtype=torch.uint8, device=device)
+        self._step()                      # first call outside the capture: module load, attributes, caches
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+
+    def _step(self) -> None:
+        route_softmax_topk(self.logits, self.top_k, out=(self.w, self.ids))
+        moe_decode(self.x, self.weights, self.ids, self.w, out=self.out, workspace=self.workspace)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
