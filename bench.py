@@ -38,6 +38,7 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
+os.environ.setdefault("NCCL_DEBUG", "WARN")   # keep stdout to the one JSON line
 sys.path.insert(0, str(ROOT / "deepseeker-v4.1_b200"))
 sys.path.insert(0, str(ROOT))
 
@@ -256,7 +257,11 @@ def run_ep(args) -> dict:
     b = args.batch
     layers = [synthetic.make_layer(fmt, H, I, El, seed=1000 + l, shared_inter=IS, std=0.02, device=dev,
                                    expert_offset=rank * El) for l in range(L)]
-    eps = [ep.gpu_layer(layer, E, K_TOP) for layer in layers]
+    # decode-sized batches: all-gather / local decode / reduce-scatter; larger: all-to-all dispatch
+    small = fmt == "fp4" and world * b <= 8
+    eps = [ep.gpu_decode_layer(layer, E, K_TOP) if small else ep.gpu_layer(layer, E, K_TOP)
+           for l, layer in enumerate(layers)]
+    graphs = None
     total_steps = args.warmup + args.steps
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
@@ -265,10 +270,18 @@ def run_ep(args) -> dict:
     stream = torch.cuda.current_stream(dev)
 
     def step(i, ev=None):
-        w, ids = moe.route_softmax_topk(logits[i], K_TOP)
-        if ev is not None:
-            ev[0].record(stream)
-        out = eps[i % L](xs[i], ids, w)
+        if graphs is not None:
+            gr = graphs[i % L]
+            gr.x.copy_(xs[i])
+            gr.logits.copy_(logits[i])
+            if ev is not None:
+                ev[0].record(stream)
+            out = gr.replay()
+        else:
+            w, ids = moe.route_softmax_topk(logits[i], K_TOP)
+            if ev is not None:
+                ev[0].record(stream)
+            out = eps[i % L](xs[i], ids, w)
         if ev is not None:
             ev[1].record(stream)
         return out
@@ -302,10 +315,16 @@ def run_ep(args) -> dict:
     dl = torch.empty(b, E, dtype=torch.float32, device=dev)
 
     def e2e_step(s_):
-        dx.copy_(pin_x[s_], non_blocking=True)
-        dl.copy_(pin_l[s_], non_blocking=True)
-        w, ids = moe.route_softmax_topk(dl, K_TOP)
-        out = eps[s_ % L](dx, ids, w)
+        if graphs is not None:
+            gr = graphs[s_ % L]
+            gr.x.copy_(pin_x[s_], non_blocking=True)
+            gr.logits.copy_(pin_l[s_], non_blocking=True)
+            out = gr.replay()
+        else:
+            dx.copy_(pin_x[s_], non_blocking=True)
+            dl.copy_(pin_l[s_], non_blocking=True)
+            w, ids = moe.route_softmax_topk(dl, K_TOP)
+            out = eps[s_ % L](dx, ids, w)
         pin_o.copy_(out, non_blocking=True)
         stream.synchronize()
     for s_ in range(min(3, e2e_steps)):
@@ -348,17 +367,19 @@ def run_ep(args) -> dict:
                                    "token(s) per GPU per step",
                        "format": fmt, "tokens_per_step_per_gpu": b, "layers_rotated": L,
                        "l2": f"rotating {L} resident layer shards per GPU",
-                       "parallelism": f"ep{world} (NCCL all_to_all_single dispatch + combine)"},
+                       "parallelism": (f"ep{world} (NCCL all_gather tokens + local decode + reduce_scatter)"
+                                       if small else f"ep{world} (NCCL all_to_all_single dispatch + combine)")},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None,
                          "kernel": "ep layer step (dispatch + local experts + combine), per GPU",
                          "bytes_per_launch": int(step_bytes), "peak_kind": kind},
             "e2e": {"value": round(world * b * max(e2e_steps, 1) / (e2e_ms * 1e-3), 2) if e2e_steps else None,
                     "unit": "tokens/s", "h2d_bytes_per_step": b * (H * 2 + E * 4), "d2h_bytes_per_step": b * H * 2},
-            "gpu_launches": args.steps * (1 + 5 + 2 * ((b + 7) // 8)),
+            "gpu_launches": args.steps * ((1 + 5 + 5) if small else (1 + 5 + 2 * ((b + 7) // 8))),
             "clocks": clocks,
         }
     del eps
+    torch.cuda.synchronize(dev)
     dist.barrier()
     dist.destroy_process_group()
     return result

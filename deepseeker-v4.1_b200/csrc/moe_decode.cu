@@ -833,6 +833,8 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
   if (!force_generic && !no_t5 && ds::decode::t5_supported(a) &&
       workspace_bytes >= ds::decode::t5_workspace_bytes(*desc, (int)tokens))
     return ds::decode::launch_t5(a, workspace, workspace_bytes, s);
+  DS_REQUIRE(!desc->out_f32 || x_dtype == DS_F32, DS_ENOTSUP,
+             "moe_decode: out_f32 with bf16 x needs FP4 banks with scale atoms (tensor-core kernels)");
   if (!force_generic && ds::decode::tc_supported(a)) return ds::decode::launch_tc(a, s);
   return desc->w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
 }
@@ -897,6 +899,8 @@ extern "C" int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x
              "moe_decode_noalloc: this layer needs %zu bytes of scratch, the static limit is %zu "
              "(use ds_moe_decode with a workspace)",
              w.total, kNoAllocScratchBytes);
+  DS_REQUIRE(!desc->out_f32 || x_dtype == DS_F32, DS_ENOTSUP,
+             "moe_decode_noalloc: out_f32 with bf16 x is not supported here (use ds_moe_decode)");
   void* scratch = nullptr;
   if ((st = noalloc_scratch(&scratch)) != DS_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -99,7 +99,8 @@ struct T5Params {
   uint8_t* hq;                // gate/up output: routed h pieces [slot][48][I/2]
   uint8_t* sfh;               // gate/up output: their scale atoms [slot][I/128][512]
   __nv_bfloat16* hb;          // gate/up output: shared h hi/lo [16][Is]
-  __nv_bfloat16* out;         // down output [T][H]
+  void* out;                  // down output [T][H]: bf16, or f32 when out_f32
+  int out_f32;
   float limit;
 };
 
@@ -286,7 +287,8 @@ __device__ void tail_combine(const T5Params& p, int r0, int lane) {
       }
       acc += __bfloat162float(__float2bfloat16_rn(sh));
     }
-    p.out[(size_t)t * H + h] = __float2bfloat16_rn(acc);
+    if (p.out_f32) static_cast<float*>(p.out)[(size_t)t * H + h] = acc;
+    else static_cast<__nv_bfloat16*>(p.out)[(size_t)t * H + h] = __float2bfloat16_rn(acc);
   }
 }
 
@@ -880,7 +882,8 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   p.hq = hq;
   p.sfh = sfh;
   p.hb = hb;
-  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.out = a.out;
+  p.out_f32 = d.out_f32 ? 1 : 0;
   p.limit = d.swiglu_limit;
   static const cudaError_t attr_rc =
       cudaFuncSetAttribute(t5_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemMax);

@@ -30,7 +30,8 @@ class DsMoeDesc(Structure):
     _fields_ = [("hidden", c_int32), ("inter", c_int32), ("n_experts", c_int32), ("top_k", c_int32),
                 ("w1", DsExpertBank), ("w3", DsExpertBank), ("w2", DsExpertBank),
                 ("shared_w1", c_void_p), ("shared_w3", c_void_p), ("shared_w2", c_void_p),
-                ("shared_inter", c_int32), ("swiglu_limit", c_float), ("route_before_down", c_int32)]
+                ("shared_inter", c_int32), ("swiglu_limit", c_float), ("route_before_down", c_int32),
+                ("out_f32", c_int32)]
 
 
 # name -> (restype, argtypes); every symbol include/deepseeker_b200.h declares

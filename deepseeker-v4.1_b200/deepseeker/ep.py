@@ -1,6 +1,15 @@
 """Expert-parallel MoE layer: routed experts sharded over the ranks of a
-process group, token rows exchanged with all-to-all (NCCL over NVLink on B200
-ranks; the CPU tests drive the same host logic over gloo).
+process group (NCCL over NVLink on B200 ranks; the CPU tests drive the same
+host logic over gloo).  Two exchange schemes:
+
+* ``ExpertParallelMoE`` -- token rows dispatched to the owners of their
+  experts and combined back with all-to-all (any batch size; below);
+* ``ExpertParallelDecode`` -- for decode-sized batches (ranks x tokens <= 8):
+  the tokens are all-gathered, every rank runs the fused decode layer over
+  all of them restricted to its own experts (f32 partial outputs), the
+  partials are reduce-scattered back to their home ranks, which add the
+  shared expert.  Every rank streams only the weights of its own experts
+  that the batch uses, i.e. about one decode layer's worth per rank.
 
 Rank g owns global experts [g * E_l, (g + 1) * E_l), E_l = E / G; the shared
 expert is replicated.  One layer step for the b tokens a rank holds (its
@@ -174,3 +183,103 @@ def gpu_layer(local_layer, n_experts: int, top_k: int, group=None) -> ExpertPara
     """ExpertParallelMoE over this rank's shard `local_layer` (global experts
     [rank * E_l, (rank + 1) * E_l) as built with synthetic.make_layer(expert_offset=...))."""
     return ExpertParallelMoE(n_experts, top_k, gpu_local_ffn(local_layer), gpu_shared_fn(local_layer), group)
+
+
+# ---------------------------------------------------------------- decode-sized batches
+
+# local_partial(x_all [G*b, H], ids_local [G*b, k] (-1 = not this rank's), gates [G*b, k]) -> f32 [G*b, H]
+LocalPartial = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+class ExpertParallelDecode:
+    def __init__(self, n_experts: int, top_k: int, local_partial: LocalPartial, shared_fn: SharedFn | None = None,
+                 group: dist.ProcessGroup | None = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if n_experts % self.world:
+            raise ValueError(f"{n_experts} experts do not shard over {self.world} ranks")
+        self.n_experts, self.top_k = n_experts, top_k
+        self.local_experts = n_experts // self.world
+        self.first_expert = self.rank * self.local_experts
+        self.local_partial, self.shared_fn = local_partial, shared_fn
+        self._nccl = dist.is_initialized() and dist.get_backend(group) == "nccl"
+
+    def _gather(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return t
+        out = torch.empty((self.world * t.shape[0], *t.shape[1:]), dtype=t.dtype, device=t.device)
+        if self._nccl:
+            dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        else:
+            dist.all_gather(list(out.chunk(self.world)), t.contiguous(), group=self.group)
+        return out
+
+    def _reduce_scatter(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return t
+        b = t.shape[0] // self.world
+        if self._nccl:
+            out = torch.empty((b, *t.shape[1:]), dtype=t.dtype, device=t.device)
+            dist.reduce_scatter_tensor(out, t.contiguous(), group=self.group)
+            return out
+        t = t.contiguous().clone()
+        dist.all_reduce(t, group=self.group)
+        return t[self.rank * b:(self.rank + 1) * b].contiguous()
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, gates: torch.Tensor) -> torch.Tensor:
+        """x [b, H] (same b on every rank), ids [b, k] global ids (-1 = dropped), gates [b, k] -> [b, H] of x.dtype."""
+        b, H = x.shape
+        k = ids.shape[1]
+        # one gather of 32-bit words per token: activations, ids, gates
+        words = (H * x.element_size()) // 4
+        row = torch.cat([x.contiguous().view(torch.uint8).view(b, -1).view(torch.int32), ids.to(torch.int32),
+                         gates.to(torch.float32).view(torch.int32)], dim=1)
+        rg = self._gather(row)
+        xg = rg[:, :words].contiguous().view(torch.uint8).view(rg.shape[0], -1).view(x.dtype)
+        ig = rg[:, words:words + k].contiguous()
+        gg = rg[:, words + k:].contiguous().view(torch.float32)
+        mine = (ig >= self.first_expert) & (ig < self.first_expert + self.local_experts)
+        il = torch.where(mine, ig - self.first_expert, torch.full_like(ig, -1))
+        part = self.local_partial(xg, il, gg)
+        if part.dtype != torch.float32 or part.shape != xg.shape:
+            raise ValueError("local_partial must return f32 [rows, H]")
+        acc = self._reduce_scatter(part)
+        if self.shared_fn is not None:
+            acc = acc + self.shared_fn(x)
+        return acc.to(x.dtype)
+
+    __call__ = forward
+
+
+def gpu_decode_layer(local_layer, n_experts: int, top_k: int, group=None,
+                     shared_rank: int | None = None) -> ExpertParallelDecode:
+    """ExpertParallelDecode on the decode kernels: routed partials in f32 from
+    this rank's FP4 shard (scale atoms prepared).
+
+    ``shared_rank=None``: every rank evaluates the shared expert for its own
+    tokens after the reduce-scatter (gpu_shared_fn).  ``shared_rank=r``: rank
+    r evaluates it for every gathered token inside its routed decode call (its
+    output is rounded to bf16 before it joins the f32 partial, the reference's
+    order) and the reduce-scatter adds it to each token exactly once; the
+    other ranks skip it."""
+    from . import moe
+
+    local_layer.prepare_tc()
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    shared_fn = None
+    if shared_rank is None:
+        shared_fn = gpu_shared_fn(local_layer)
+    if (shared_rank is not None and rank == shared_rank) or local_layer.shared_w1 is None:
+        layer = local_layer
+    else:
+        layer = moe.MoEWeights(local_layer.w1, local_layer.w3, local_layer.w2, swiglu_limit=local_layer.swiglu_limit,
+                               route_before_down=local_layer.route_before_down)
+
+    def local_partial(xg, il, gg):
+        out = torch.empty(xg.shape, dtype=torch.float32, device=xg.device)
+        for r0 in range(0, xg.shape[0], moe.MAX_DECODE_TOKENS):
+            r1 = min(xg.shape[0], r0 + moe.MAX_DECODE_TOKENS)
+            moe.moe_decode(xg[r0:r1], layer, il[r0:r1], gg[r0:r1], out=out[r0:r1], out_f32=True)
+        return out
+    return ExpertParallelDecode(n_experts, top_k, local_partial, shared_fn, group)

@@ -240,10 +240,13 @@ def decode_workspace_bytes(weights: MoEWeights, tokens: int, top_k: int) -> int:
 
 
 def moe_decode(x: torch.Tensor, weights: MoEWeights, topk_ids: torch.Tensor, topk_w: torch.Tensor,
-               out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+               out_f32: bool = False) -> torch.Tensor:
     """Fused routed-expert MoE for up to 8 tokens: x [T, H] bf16 (or f32) -> [T, H] of x's dtype.
 
-    topk_ids [T, k] int32 (-1 = dropped slot), topk_w [T, k] f32.
+    topk_ids [T, k] int32 (-1 = dropped slot), topk_w [T, k] f32.  out_f32
+    (bf16 x, FP4 banks with prepared scale atoms): f32 output without the final
+    rounding, for partial sums that are added across ranks.
     """
     x = require_cuda(x, "x", (torch.bfloat16, torch.float32))
     if x.dim() != 2 or x.shape[1] != weights.hidden:
@@ -263,8 +266,14 @@ def moe_decode(x: torch.Tensor, weights: MoEWeights, topk_ids: torch.Tensor, top
         d = weights.cached_desc(k)
     need = weights.decode_workspace_bytes(T, k)
     ws = workspace if workspace is not None else _workspace(x.device, need)
+    if out_f32 and x.dtype != torch.float32:
+        d = _abi.DsMoeDesc.from_buffer_copy(d)
+        d.out_f32 = 1
+    odt = torch.float32 if (out_f32 or x.dtype == torch.float32) else x.dtype
     if out is None:
-        out = torch.empty_like(x)
+        out = torch.empty(x.shape, dtype=odt, device=x.device)
+    elif out.dtype != odt or out.shape != x.shape or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {tuple(x.shape)} {odt} tensor")
     xdt = _abi.DS_F32 if x.dtype == torch.float32 else _abi.DS_BF16
     _abi.call("ds_moe_decode", ctypes.byref(d), ptr(x), xdt, T, ptr(topk_ids), ptr(topk_w), ptr(out), ptr(ws),
               ws.numel() * ws.element_size(), stream_handle(x.device))

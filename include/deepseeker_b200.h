@@ -161,6 +161,11 @@ typedef struct DsMoeDesc {
   int32_t route_before_down; /* 1: h *= gate before the down projection
                                 (moe_layer, mlx_forward.py:404-405);
                                 0: y *= gate after it (grouped.py:50-53)       */
+  int32_t out_f32;       /* ds_moe_decode with bf16 x: 1 writes the layer
+                            output in f32 without the final rounding (partial
+                            sums that another rank adds to), 0 = x's dtype.
+                            Needs the tensor-core decode kernels (FP4 banks
+                            with scale atoms); DS_ENOTSUP otherwise.         */
 } DsMoeDesc;
 
 /* Workspace bytes ds_moe_decode needs for `tokens` rows. */

@@ -60,6 +60,32 @@ def cpu_ep(world: int, rank: int, seed: int = 0):
     return ExpertParallelMoE(E, K, local_ffn, shared_fn), x, ids, w
 
 
+def cpu_ep_decode(world: int, rank: int, seed: int = 0):
+    """ExpertParallelDecode with the oracle's f32 expert math (row by row)."""
+    from deepseeker.ep import ExpertParallelDecode
+    from oracle import moe as omoe
+
+    w1, w3, w2, sh, x, ids, w = cpu_problem(seed)
+    El = E // world
+
+    def local_partial(xg, il, gg):
+        out = torch.zeros(xg.shape[0], H)
+        for r in range(xg.shape[0]):
+            for c in range(il.shape[1]):
+                e = int(il[r, c])
+                if e < 0:
+                    continue
+                ge = rank * El + e
+                h = omoe.swiglu_hidden(xg[r:r + 1].float(), w1[ge], w3[ge], LIMIT) * gg[r, c]
+                out[r] += (h @ w2[ge].T)[0]
+        return out
+
+    def shared_fn(xx):
+        return omoe.shared_expert(xx.float(), *sh, limit=LIMIT).to(xx.dtype).float()
+
+    return ExpertParallelDecode(E, K, local_partial, shared_fn), x, ids, w
+
+
 def rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -70,7 +96,7 @@ def rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
                 q.put((rank, "left"))           # leaves between steps: never joins the exchange
                 dist.destroy_process_group()
                 return
-            ep, x, ids, w = cpu_ep(world, rank)
+            ep, x, ids, w = cpu_ep_decode(world, rank) if mode == "cpu_decode" else cpu_ep(world, rank)
             try:
                 out = ep(x, ids, w)
             except RuntimeError as e:
@@ -78,7 +104,7 @@ def rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
                 return
             q.put((rank, out))
         else:
-            run_gpu_rank(rank, world, q)
+            run_gpu_rank(rank, world, q, decode=(mode == "gpu_decode"))
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, f"exception: {e!r}"))
@@ -89,7 +115,7 @@ def gpu_problem(rank: int, world: int):
     from oracle import moe as omoe
 
     dev = torch.device("cuda", rank)
-    Hg, Ig, Eg, Kg, Bg = 1024, 512, 16, 4, 6
+    Hg, Ig, Eg, Kg, Bg = 1024, 1024, 16, 4, 6
     El = Eg // world
     layer = synthetic.make_layer("fp4", Hg, Ig, El, seed=5, shared_inter=512, device=dev, expert_offset=rank * El)
     g = torch.Generator().manual_seed(77)
@@ -98,13 +124,16 @@ def gpu_problem(rank: int, world: int):
     return layer, x, ids.to(torch.int32).to(dev), w.float().to(dev), Eg, Kg
 
 
-def run_gpu_rank(rank: int, world: int, q) -> None:
+def run_gpu_rank(rank: int, world: int, q, decode: bool = False) -> None:
     from deepseeker import ep
 
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     layer, x, ids, w, Eg, Kg = gpu_problem(rank, world)
-    out = ep.gpu_layer(layer, Eg, Kg)(x, ids, w)
+    if decode:
+        out = ep.gpu_decode_layer(layer, Eg, Kg)(x[:4], ids[:4], w[:4])
+    else:
+        out = ep.gpu_layer(layer, Eg, Kg)(x, ids, w)
     torch.cuda.synchronize()
     q.put((rank, out.cpu()))

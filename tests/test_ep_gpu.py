@@ -33,6 +33,52 @@ def test_ep_single_rank_matches_decode(cuda):
     assert rel_l2(out, ref) <= 1e-3
 
 
+def test_ep_decode_scheme_single_rank_matches_decode(cuda):
+    from deepseeker import ep, moe
+
+    layer, x, ids, w, E, K = ep_worker.gpu_problem(0, 1)
+    out = ep.gpu_decode_layer(layer, E, K)(x[:4], ids[:4], w[:4])
+    ref = moe.moe_decode(x[:4], layer, ids[:4], w[:4])
+    assert out.dtype == torch.bfloat16
+    assert rel_l2(out, ref) <= 1e-3
+
+
+def spawn_gpu(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=ep_worker.rank_main, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r, v = q.get(timeout=300)
+            res[r] = v
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    return res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_decode_scheme_two_ranks(cuda):
+    from deepseeker import ep
+
+    layer, x, ids, w, E, K = ep_worker.gpu_problem(0, 1)
+    single = ep.gpu_decode_layer(layer, E, K)(x[:4], ids[:4], w[:4]).cpu()
+    del layer
+    torch.cuda.synchronize()
+    res = spawn_gpu("gpu_decode")
+    for r in (0, 1):
+        assert isinstance(res[r], torch.Tensor), res[r]
+        assert rel_l2(res[r], single) <= 1e-3
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_two_ranks_bitwise_equal_one_rank(cuda):
     from deepseeker import ep

@@ -80,3 +80,19 @@ def test_peer_that_left_fails_the_exchange_not_hangs():
     res = spawn(2, "cpu_dead_peer", timeout=90.0)
     assert res[1] == "left"
     assert isinstance(res[0], str) and res[0].startswith(("error", "exception")), res[0]
+
+
+def test_decode_scheme_two_ranks_match_one_rank():
+    """All-gather / local partial / reduce-scatter scheme (ExpertParallelDecode)."""
+    ep1, x, ids, w = ep_worker.cpu_ep_decode(1, 0)
+    single = ep1(x, ids, w)
+    res = spawn(2, "cpu_decode")
+    for r in (0, 1):
+        assert isinstance(res[r], torch.Tensor), res[r]
+        # f32 partial sums are added in another order; the bf16 results agree to the last place or two
+        diff = (res[r].float() - single.float()).abs().max()
+        assert float(diff) <= 2 ** -7 * float(single.float().abs().max()), float(diff)
+    from oracle import moe as omoe
+    w1, w3, w2, sh, *_ = ep_worker.cpu_problem()
+    ref = omoe.moe_combine(x, ids.long(), w, lambda e: (w1[e], w3[e], w2[e]), shared=sh, limit=ep_worker.LIMIT)
+    assert float((single.float() - ref.float()).abs().max()) <= 2 ** -7 * float(ref.float().abs().max())
