@@ -237,7 +237,9 @@ def run_ep(args) -> dict:
     """N > 1: config 2's layer expert-parallel over the N ranks (rank g owns
     experts [g*E/N, (g+1)*E/N) of every rotated layer, shared expert
     replicated); every rank decodes its own --batch tokens per step (weak
-    scaling), token rows dispatched / combined with NCCL all_to_all_single."""
+    scaling).  Ranks x tokens <= 8 (FP4): ds_ep_decode, token rows and partial
+    sums exchanged over NVLink peer memory by the library's kernels, one CUDA
+    graph per layer; otherwise NCCL all_to_all_single dispatch + combine."""
     import datetime
 
     import torch
@@ -257,11 +259,19 @@ def run_ep(args) -> dict:
     b = args.batch
     layers = [synthetic.make_layer(fmt, H, I, El, seed=1000 + l, shared_inter=IS, std=0.02, device=dev,
                                    expert_offset=rank * El) for l in range(L)]
-    # decode-sized batches: all-gather / local decode / reduce-scatter; larger: all-to-all dispatch
+    # decode-sized batches: token rows exchanged over NVLink peer memory by the
+    # library's own kernels (no collective call; one CUDA graph per layer);
+    # larger batches: NCCL all-to-all dispatch + combine
     small = fmt == "fp4" and world * b <= 8
-    eps = [ep.gpu_decode_layer(layer, E, K_TOP) if small else ep.gpu_layer(layer, E, K_TOP)
-           for l, layer in enumerate(layers)]
+    comm = None
     graphs = None
+    if small:
+        comm = ep.PeerComm(b, H, K_TOP, timeout_ms=30000)
+        eps = [ep.PeerDecodeLayer(comm, layer, E, K_TOP, rows=b) for layer in layers]
+        if os.environ.get("DEEPSEEKER_BENCH_NO_GRAPH") != "1":
+            graphs = [ep.PeerDecodeGraph(pl) for pl in eps]
+    else:
+        eps = [ep.gpu_layer(layer, E, K_TOP) for layer in layers]
     total_steps = args.warmup + args.steps
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
@@ -340,8 +350,17 @@ def run_ep(args) -> dict:
     e2e_ms = max(e0.elapsed_time(e1), 1e-9)
 
     per_expert = sum(bk.nbytes() // El for bk in (layers[0].w1, layers[0].w3, layers[0].w2))
-    # bytes one rank streams per step: its share of the routed experts + the shared expert for its tokens
-    step_bytes = b * K_TOP * per_expert + 3 * IS * H * 2 * ((b + 7) // 8)
+    # bytes one rank streams per step: the distinct experts of this rank that
+    # the step's routing of ALL ranks touches (counted from the timed steps'
+    # routing, gathered after the timing) + the shared expert for its tokens
+    timed_ids = torch.stack([moe.route_softmax_topk(logits[args.warmup + s_], K_TOP)[1]
+                             for s_ in range(args.steps)])                    # [steps, b, k]
+    all_ids = torch.empty((world,) + tuple(timed_ids.shape), dtype=timed_ids.dtype, device=dev)
+    dist.all_gather_into_tensor(all_ids, timed_ids.contiguous())
+    all_ids = all_ids.permute(1, 0, 2, 3).reshape(args.steps, -1).cpu()
+    mine = [len({int(e) for e in row.tolist() if rank * El <= e < (rank + 1) * El}) for row in all_ids]
+    distinct = statistics.mean(mine) if mine else float(b * K_TOP)
+    step_bytes = distinct * per_expert + 3 * IS * H * 2 * ((b + 7) // 8) + 2 * b * H * 2
     ms_t = torch.tensor([ms, e2e_ms, layer_ms], device=dev)
     dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms, e2e_ms, layer_ms = (float(v) for v in ms_t.cpu())
@@ -367,19 +386,26 @@ def run_ep(args) -> dict:
                                    "token(s) per GPU per step",
                        "format": fmt, "tokens_per_step_per_gpu": b, "layers_rotated": L,
                        "l2": f"rotating {L} resident layer shards per GPU",
-                       "parallelism": (f"ep{world} (NCCL all_gather tokens + local decode + reduce_scatter)"
-                                       if small else f"ep{world} (NCCL all_to_all_single dispatch + combine)")},
+                       "parallelism": (f"ep{world} (token rows and partial sums exchanged over NVLink peer "
+                                       "memory by the library's kernels, one CUDA graph per layer)"
+                                       if small else f"ep{world} (NCCL all_to_all_single dispatch + combine)"),
+                       "distinct_local_experts_per_step": round(distinct, 3)},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None,
                          "kernel": "ep layer step (dispatch + local experts + combine), per GPU",
                          "bytes_per_launch": int(step_bytes), "peak_kind": kind},
             "e2e": {"value": round(world * b * max(e2e_steps, 1) / (e2e_ms * 1e-3), 2) if e2e_steps else None,
                     "unit": "tokens/s", "h2d_bytes_per_step": b * (H * 2 + E * 4), "d2h_bytes_per_step": b * H * 2},
-            "gpu_launches": args.steps * ((1 + 5 + 5) if small else (1 + 5 + 2 * ((b + 7) // 8))),
+            "gpu_launches": args.steps * ((1 + 1 + 5 + 1) if small else (1 + 5 + 2 * ((b + 7) // 8))),
             "clocks": clocks,
         }
-    del eps
+    del graphs, eps
     torch.cuda.synchronize(dev)
+    dist.barrier()
+    if comm is not None:
+        if comm.status() != 0:
+            raise RuntimeError(f"rank {rank}: peer exchange reported error {comm.status()}")
+        comm.close()
     dist.barrier()
     dist.destroy_process_group()
     return result

@@ -1,0 +1,453 @@
+// Expert-parallel decode over NVLink peer memory (no collective library on
+// the data path).
+//
+// Ranks 0..G-1 each own E/G experts of a layer and decode b tokens per step.
+// One ds_ep_decode call per layer and rank:
+//
+//   1. ep_dispatch_kernel: every rank stores its b token rows (x, global ids,
+//      gates) into slot `rank` of every rank's receive area (P2P stores over
+//      NVLink into memory opened with CUDA IPC), raises a flag there, waits
+//      for all G flags of its own area and rewrites the gathered ids to local
+//      expert ids (-1 where another rank owns the expert).
+//   2. the tcgen05 decode kernels (moe_decode_t5.cu) over the G*b gathered
+//      rows: this rank's routed experts for every row, its own rows' shared
+//      expert, f32 partial rows out.
+//   3. ep_combine_kernel: every rank stores the partial rows of rank q's
+//      tokens into slot `rank` of q's reduce area, raises a flag there, waits
+//      for all G flags of its own area and sums the G slots in rank order
+//      into its bf16 output.
+//
+// Nothing on the path calls NCCL, so a step of many layers captures into one
+// CUDA graph.  Flags carry epochs: each kernel block keeps a counter in local
+// device memory and adds 1 to the flag it raises, so a flag reaches
+// epoch * blocks-per-peer when every block of that peer has stored its part.
+// Flags are never reset; graph replays keep counting.  A receive area is
+// written again only after its owner has moved past the step that reads it
+// (the next dispatch of a peer needs this rank's own next dispatch, which
+// follows this rank's combine), so one buffer of each kind suffices.
+//
+// Every wait is bounded by %globaltimer (the communicator's timeout); a
+// timeout sets the error word and an abort flag, and later kernels of an
+// aborted communicator return at once.  ds_ep_status reads the error word.
+//
+// The per-layer call it replaces is the reference's MoE block of a decode
+// step (src/deepseeker/mlx_runner.py:765-985 Runner.moe ->
+// src/deepseeker/mlx_forward.py:257-419 moe_layer), here spread over ranks.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "deepseeker_b200.h"
+#include "ds_common.cuh"
+#include "moe_decode.cuh"
+#include "ptx.cuh"
+
+namespace {
+
+constexpr int kMaxWorld = 8;
+constexpr int kDispatchBlocks = 2;   // blocks per peer in the dispatch kernel
+constexpr int kCombineBlocks = 4;    // blocks per peer in the combine kernel
+constexpr int kEpThreads = 256;
+constexpr int kErrTimeout = 2;
+
+size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Byte offsets inside one rank's region (identical on every rank).  The
+// first part (flags, receive and reduce areas) is written by peers; the rest
+// is local.
+struct EpLayout {
+  size_t flags_g, flags_r, recv_x, recv_ids, recv_w, rbuf;   // peer-visible
+  size_t ctr, err, ids_local, part;                           // local
+  size_t total;
+};
+
+EpLayout ep_layout(int world, int max_rows, int H, int k) {
+  EpLayout L;
+  const size_t R = (size_t)world * max_rows;
+  size_t o = 0;
+  L.flags_g = o;   o += 256;
+  L.flags_r = o;   o += 256;
+  L.recv_x = o;    o += up256(R * H * 2);
+  L.recv_ids = o;  o += up256(R * k * 4);
+  L.recv_w = o;    o += up256(R * k * 4);
+  L.rbuf = o;      o += up256(R * H * 4);
+  L.ctr = o;       o += 512;
+  L.err = o;       o += 256;
+  L.ids_local = o; o += up256(R * k * 4);
+  L.part = o;      o += up256(R * H * 4);
+  L.total = o;
+  return L;
+}
+
+struct EpArgs {
+  char* base[kMaxWorld];   // region of every rank, as mapped in this process (own at [rank])
+  EpLayout L;
+  int world, rank, rows, H, k;
+  int first_expert, local_experts;
+  const void* x;           // [rows, H] bf16 (dispatch)
+  const int32_t* ids;      // [rows, k] global ids
+  const float* gates;      // [rows, k]
+  void* out;               // [rows, H] bf16 (combine)
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ void red_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Thread 0 of the block waits until every flag in flags[0..n) reaches
+// `target` (or the timeout passes, or another block aborted); returns the
+// block-wide verdict (all threads call it).
+__device__ bool block_wait_flags(const uint32_t* flags, int n, uint32_t target, uint64_t timeout_ns,
+                                 int* err, volatile int* abort) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    int good = 1;
+    const uint64_t t0 = ds::ptx::globaltimer_ns();
+    for (int j = 0; j < n && good; ++j) {
+      for (uint32_t it = 0;; ++it) {
+        // wrap-safe "flag >= target"
+        if ((int32_t)(ld_acquire_sys(flags + j) - target) >= 0) break;
+        if ((it & 63u) == 63u) {
+          if (*abort || ds::ptx::globaltimer_ns() - t0 > timeout_ns) {
+            good = 0;
+            break;
+          }
+        }
+        __nanosleep(64);
+      }
+    }
+    if (!good) {
+      atomicOr(err, kErrTimeout);
+      *abort = 1;
+    }
+    ok = good;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// Block (q, part): push this rank's rows into slot `rank` of rank q's
+// receive area, raise q's flag, wait for q's rows in our own area, rewrite
+// their ids to local ids.
+__global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const __grid_constant__ EpArgs a) {
+  char* own = a.base[a.rank];
+  int* err = reinterpret_cast<int*>(own + a.L.err);
+  volatile int* abort = err + 1;
+  const int q = blockIdx.x / kDispatchBlocks, part = blockIdx.x % kDispatchBlocks;
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) {
+    uint32_t* ctr = reinterpret_cast<uint32_t*>(own + a.L.ctr) + blockIdx.x;
+    s_epoch = *ctr + 1;
+    *ctr = s_epoch;
+    s_abort = *abort;
+  }
+  __syncthreads();
+  if (s_abort) return;
+  const uint32_t epoch = s_epoch;
+  const int b = a.rows, H = a.H, k = a.k;
+  char* dst = a.base[q];
+  {
+    // x rows: b * H bf16 as 16-byte vectors, split over the blocks of this peer
+    const uint4* src = static_cast<const uint4*>(a.x);
+    uint4* to = reinterpret_cast<uint4*>(dst + a.L.recv_x + (size_t)a.rank * b * H * 2);
+    const int nv = b * H / 8;
+    for (int i = part * kEpThreads + threadIdx.x; i < nv; i += kDispatchBlocks * kEpThreads) to[i] = src[i];
+    if (part == 0) {
+      int32_t* ti = reinterpret_cast<int32_t*>(dst + a.L.recv_ids) + (size_t)a.rank * b * k;
+      float* tw = reinterpret_cast<float*>(dst + a.L.recv_w) + (size_t)a.rank * b * k;
+      for (int i = threadIdx.x; i < b * k; i += kEpThreads) {
+        ti[i] = a.ids[i];
+        tw[i] = a.gates[i];
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) red_release_sys(reinterpret_cast<uint32_t*>(dst + a.L.flags_g) + a.rank, 1u);
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(own + a.L.flags_g) + q;
+  if (!block_wait_flags(flags, 1, epoch * kDispatchBlocks, a.timeout_ns, err, abort)) return;
+  // slot q arrived: local ids (L2 reads: the rows were written over NVLink)
+  const int32_t* gi = reinterpret_cast<const int32_t*>(own + a.L.recv_ids) + (size_t)q * b * k;
+  int32_t* li = reinterpret_cast<int32_t*>(own + a.L.ids_local) + (size_t)q * b * k;
+  for (int i = part * kEpThreads + threadIdx.x; i < b * k; i += kDispatchBlocks * kEpThreads) {
+    const int32_t e = __ldcg(gi + i);
+    li[i] = (e >= a.first_expert && e < a.first_expert + a.local_experts) ? e - a.first_expert : -1;
+  }
+}
+
+// Block (q, part): push the partial rows of rank q's tokens into slot
+// `rank` of q's reduce area, raise q's flag, wait for every rank's slot in
+// our own area, sum the slots in rank order into the bf16 output.
+__global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const __grid_constant__ EpArgs a) {
+  char* own = a.base[a.rank];
+  int* err = reinterpret_cast<int*>(own + a.L.err);
+  volatile int* abort = err + 1;
+  const int q = blockIdx.x / kCombineBlocks, part = blockIdx.x % kCombineBlocks;
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) {
+    uint32_t* ctr = reinterpret_cast<uint32_t*>(own + a.L.ctr) + 64 + blockIdx.x;
+    s_epoch = *ctr + 1;
+    *ctr = s_epoch;
+    s_abort = *abort;
+  }
+  __syncthreads();
+  if (s_abort) return;
+  const uint32_t epoch = s_epoch;
+  const int b = a.rows, H = a.H, G = a.world;
+  const size_t slot_elems = (size_t)b * H;
+  {
+    const float4* src = reinterpret_cast<const float4*>(own + a.L.part) + (size_t)q * slot_elems / 4;
+    float4* to = reinterpret_cast<float4*>(a.base[q] + a.L.rbuf) + (size_t)a.rank * slot_elems / 4;
+    const int nv = (int)(slot_elems / 4);
+    for (int i = part * kEpThreads + threadIdx.x; i < nv; i += kCombineBlocks * kEpThreads) to[i] = src[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) red_release_sys(reinterpret_cast<uint32_t*>(a.base[q] + a.L.flags_r) + a.rank, 1u);
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(own + a.L.flags_r);
+  if (!block_wait_flags(flags, G, epoch * kCombineBlocks, a.timeout_ns, err, abort)) return;
+  // sum: this block's share of the b * H outputs, 4 at a time
+  const float4* rb = reinterpret_cast<const float4*>(own + a.L.rbuf);
+  const int nv = (int)(slot_elems / 4);
+  uint2* out = static_cast<uint2*>(a.out);
+  for (int i = blockIdx.x * kEpThreads + threadIdx.x; i < nv; i += gridDim.x * kEpThreads) {
+    float4 acc = __ldcg(rb + i);
+    for (int j = 1; j < G; ++j) {
+      const float4 v = __ldcg(rb + (size_t)j * nv + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&lo);
+    o.y = *reinterpret_cast<const uint32_t*>(&hi);
+    out[i] = o;
+  }
+}
+
+}  // namespace
+
+struct DsEp {
+  int world, rank, max_rows, hidden, top_k, device;
+  uint64_t timeout_ns;
+  EpLayout L;
+  char* own;                 // cudaMalloc'd region
+  char* base[kMaxWorld];     // every rank's region in this process
+  bool opened[kMaxWorld];    // base[j] came from cudaIpcOpenMemHandle
+  bool connected;
+};
+
+extern "C" int ds_ep_create(int world, int rank, int max_rows, int hidden, int top_k, int timeout_ms,
+                            DsEp** ep) {
+  DS_REQUIRE(ep != nullptr, DS_EINVAL, "ep_create: null output");
+  *ep = nullptr;
+  DS_REQUIRE(world >= 1 && world <= kMaxWorld, DS_EINVAL, "ep_create: world %d outside 1..%d", world, kMaxWorld);
+  DS_REQUIRE(rank >= 0 && rank < world, DS_EINVAL, "ep_create: rank %d outside 0..%d", rank, world - 1);
+  DS_REQUIRE(max_rows >= 1 && world * max_rows <= ds::decode::kMaxTokens, DS_EINVAL,
+             "ep_create: world * max_rows = %d outside 1..%d", world * max_rows, ds::decode::kMaxTokens);
+  DS_REQUIRE(hidden > 0 && hidden % 8 == 0, DS_EINVAL, "ep_create: hidden must be a positive multiple of 8");
+  DS_REQUIRE(top_k >= 1 && top_k <= 32, DS_EINVAL, "ep_create: top_k %d outside 1..32", top_k);
+  DS_REQUIRE(timeout_ms > 0, DS_EINVAL, "ep_create: timeout_ms must be positive");
+  DsEp* e = new DsEp;
+  memset(e, 0, sizeof(*e));
+  e->world = world;
+  e->rank = rank;
+  e->max_rows = max_rows;
+  e->hidden = hidden;
+  e->top_k = top_k;
+  e->timeout_ns = (uint64_t)timeout_ms * 1000000ull;
+  e->L = ep_layout(world, max_rows, hidden, top_k);
+  cudaError_t rc = cudaGetDevice(&e->device);
+  if (rc == cudaSuccess) rc = cudaMalloc(reinterpret_cast<void**>(&e->own), e->L.total);
+  if (rc == cudaSuccess) rc = cudaMemset(e->own, 0, e->L.total);
+  if (rc == cudaSuccess) rc = cudaDeviceSynchronize();
+  if (rc != cudaSuccess) {
+    if (e->own) cudaFree(e->own);
+    delete e;
+    return ds::cuda_status(rc, "ep_create: region allocation");
+  }
+  e->base[rank] = e->own;
+  *ep = e;
+  return DS_OK;
+}
+
+extern "C" size_t ds_ep_region_bytes(int world, int max_rows, int hidden, int top_k) {
+  return ep_layout(world, max_rows, hidden, top_k).total;
+}
+
+extern "C" int ds_ep_ipc_handle(DsEp* ep, void* handle) {
+  DS_REQUIRE(ep != nullptr && handle != nullptr, DS_EINVAL, "ep_ipc_handle: null argument");
+  cudaIpcMemHandle_t h;
+  DS_CHECK_CUDA(cudaIpcGetMemHandle(&h, ep->own));
+  static_assert(sizeof(h) == DS_EP_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return DS_OK;
+}
+
+extern "C" int ds_ep_connect(DsEp* ep, const void* handles) {
+  DS_REQUIRE(ep != nullptr && handles != nullptr, DS_EINVAL, "ep_connect: null argument");
+  DS_REQUIRE(!ep->connected, DS_EINVAL, "ep_connect: already connected");
+  const char* hs = static_cast<const char*>(handles);
+  for (int j = 0; j < ep->world; ++j) {
+    if (j == ep->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hs + (size_t)j * DS_EP_HANDLE_BYTES, sizeof(h));
+    void* p = nullptr;
+    const cudaError_t rc = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (rc != cudaSuccess) {
+      for (int i = 0; i < j; ++i)
+        if (ep->opened[i]) {
+          cudaIpcCloseMemHandle(ep->base[i]);
+          ep->opened[i] = false;
+          ep->base[i] = nullptr;
+        }
+      return ds::cuda_status(rc, "ep_connect: cudaIpcOpenMemHandle");
+    }
+    ep->base[j] = static_cast<char*>(p);
+    ep->opened[j] = true;
+  }
+  ep->connected = true;
+  return DS_OK;
+}
+
+extern "C" int ds_ep_connect_peers(DsEp* ep, DsEp* const* all) {
+  DS_REQUIRE(ep != nullptr && all != nullptr, DS_EINVAL, "ep_connect_peers: null argument");
+  DS_REQUIRE(!ep->connected, DS_EINVAL, "ep_connect_peers: already connected");
+  DS_REQUIRE(all[ep->rank] == ep, DS_EINVAL, "ep_connect_peers: all[rank] must be this communicator");
+  for (int j = 0; j < ep->world; ++j) {
+    const DsEp* o = all[j];
+    DS_REQUIRE(o != nullptr && o->world == ep->world && o->rank == j && o->max_rows == ep->max_rows &&
+                   o->hidden == ep->hidden && o->top_k == ep->top_k,
+               DS_EINVAL, "ep_connect_peers: communicator %d does not match", j);
+  }
+  for (int j = 0; j < ep->world; ++j) {
+    if (j == ep->rank) continue;
+    if (all[j]->device != ep->device) {
+      int can = 0;
+      DS_CHECK_CUDA(cudaDeviceCanAccessPeer(&can, ep->device, all[j]->device));
+      DS_REQUIRE(can, DS_ENOTSUP, "ep_connect_peers: device %d cannot access device %d", ep->device,
+                 all[j]->device);
+      const cudaError_t rc = cudaDeviceEnablePeerAccess(all[j]->device, 0);
+      if (rc == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else DS_CHECK_CUDA(rc);
+    }
+    ep->base[j] = all[j]->own;
+  }
+  ep->connected = true;
+  return DS_OK;
+}
+
+extern "C" int ds_ep_status(DsEp* ep, int32_t* err) {
+  DS_REQUIRE(ep != nullptr && err != nullptr, DS_EINVAL, "ep_status: null argument");
+  int32_t v[2] = {0, 0};
+  DS_CHECK_CUDA(cudaMemcpy(v, ep->own + ep->L.err, sizeof(v), cudaMemcpyDeviceToHost));
+  *err = v[0];
+  return DS_OK;
+}
+
+extern "C" int ds_ep_destroy(DsEp* ep) {
+  if (ep == nullptr) return DS_OK;
+  cudaError_t first = cudaSuccess;
+  for (int j = 0; j < ep->world; ++j)
+    if (ep->opened[j]) {
+      const cudaError_t rc = cudaIpcCloseMemHandle(ep->base[j]);
+      if (first == cudaSuccess) first = rc;
+    }
+  if (ep->own) {
+    const cudaError_t rc = cudaFree(ep->own);
+    if (first == cudaSuccess) first = rc;
+  }
+  delete ep;
+  if (first != cudaSuccess) return ds::cuda_status(first, "ep_destroy");
+  return DS_OK;
+}
+
+extern "C" int ds_ep_decode_workspace_size(DsEp* ep, const DsMoeDesc* desc, int64_t rows, size_t* bytes) {
+  DS_REQUIRE(ep != nullptr && desc != nullptr && bytes != nullptr, DS_EINVAL, "ep_decode_workspace_size: null");
+  DS_REQUIRE(rows >= 1 && rows <= ep->max_rows, DS_EINVAL, "ep_decode_workspace_size: rows %lld outside 1..%d",
+             (long long)rows, ep->max_rows);
+  *bytes = ds::decode::t5_workspace_bytes(*desc, (int)(ep->world * rows));
+  return DS_OK;
+}
+
+extern "C" int ds_ep_decode(DsEp* ep, const DsMoeDesc* desc, int32_t first_expert, const void* x, int64_t rows,
+                            const int32_t* topk_ids, const float* topk_w, void* out, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  DS_REQUIRE(ep != nullptr && desc != nullptr, DS_EINVAL, "ep_decode: null handle or descriptor");
+  DS_REQUIRE(ep->connected || ep->world == 1, DS_EINVAL, "ep_decode: communicator not connected");
+  DS_REQUIRE(x && topk_ids && topk_w && out && workspace, DS_EINVAL, "ep_decode: null pointer");
+  DS_REQUIRE(rows >= 1 && rows <= ep->max_rows, DS_EINVAL, "ep_decode: rows %lld outside 1..%d", (long long)rows,
+             ep->max_rows);
+  DS_REQUIRE(desc->hidden == ep->hidden && desc->top_k == ep->top_k, DS_EINVAL,
+             "ep_decode: descriptor hidden/top_k differ from the communicator's");
+  DS_REQUIRE(first_expert >= 0 && desc->n_experts > 0, DS_EINVAL, "ep_decode: bad expert range");
+  DS_REQUIRE(ds::aligned(x, 16) && ds::aligned(out, 8) && ds::aligned(workspace, 256), DS_EALIGN,
+             "ep_decode: x 16-byte, out 8-byte, workspace 256-byte aligned");
+  int dev = -1;
+  DS_CHECK_CUDA(cudaGetDevice(&dev));
+  DS_REQUIRE(dev == ep->device, DS_EINVAL, "ep_decode: current device %d, communicator device %d", dev,
+             ep->device);
+  const int G = ep->world, b = (int)rows, T = G * b;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  EpArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int j = 0; j < G; ++j) a.base[j] = ep->base[j];
+  a.L = ep->L;
+  a.world = G;
+  a.rank = ep->rank;
+  a.rows = b;
+  a.H = ep->hidden;
+  a.k = ep->top_k;
+  a.first_expert = first_expert;
+  a.local_experts = desc->n_experts;
+  a.x = x;
+  a.ids = topk_ids;
+  a.gates = topk_w;
+  a.out = out;
+  a.timeout_ns = ep->timeout_ns;
+
+  // decode over the gathered rows; the t5 path is required (f32 partial rows
+  // with the shared expert restricted to this rank's rows)
+  ds::decode::DecodeArgs d;
+  d.d = *desc;
+  d.d.out_f32 = 1;
+  d.x = ep->own + ep->L.recv_x;
+  d.x_f32 = 0;
+  d.tokens = T;
+  d.ids = reinterpret_cast<const int32_t*>(ep->own + ep->L.ids_local);
+  d.gates = reinterpret_cast<const float*>(ep->own + ep->L.recv_w);
+  d.out = ep->own + ep->L.part;
+  d.h = nullptr;
+  d.max_slots = std::min(T * desc->top_k, desc->n_experts);
+  d.h_stride = 0;
+  d.err = static_cast<int*>(workspace);
+  d.sh_row0 = ep->rank * b;
+  d.sh_row1 = ep->rank * b + b;
+  DS_REQUIRE(ds::decode::t5_supported(d), DS_ENOTSUP,
+             "ep_decode: needs FP4 banks with scale atoms, hidden and inter multiples of 1024 (tensor-core "
+             "decode kernels)");
+
+  ep_dispatch_kernel<<<G * kDispatchBlocks, kEpThreads, 0, st>>>(a);
+  DS_CHECK_LAUNCH("ep_dispatch_kernel");
+  int rc = ds::decode::launch_t5(d, workspace, workspace_bytes, st);
+  if (rc != DS_OK) return rc;
+  ep_combine_kernel<<<G * kCombineBlocks, kEpThreads, 0, st>>>(a);
+  DS_CHECK_LAUNCH("ep_combine_kernel");
+  return DS_OK;
+}

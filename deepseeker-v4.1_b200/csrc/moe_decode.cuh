@@ -26,6 +26,9 @@ struct DecodeArgs {
   int max_slots;      // routed slots reserved = min(T*k, E)
   int h_stride;       // max(I, shared_inter), multiple of 4
   int* err;           // device error word
+  // tcgen05 path only: the shared expert is added to output rows
+  // [sh_row0, sh_row1) (expert-parallel ranks add it to their own rows)
+  int sh_row0 = 0, sh_row1 = 1 << 30;
 };
 
 // Single-token tensor-core pipeline (moe_decode_tc.cu).  Returns true and

@@ -101,6 +101,7 @@ struct T5Params {
   __nv_bfloat16* hb;          // gate/up output: shared h hi/lo [16][Is]
   void* out;                  // down output [T][H]: bf16, or f32 when out_f32
   int out_f32;
+  int sh_t0, sh_t1;           // output rows that receive the shared expert
   float limit;
 };
 
@@ -276,7 +277,7 @@ __device__ void tail_combine(const T5Params& p, int r0, int lane) {
       for (int kp = 4; kp < KP; ++kp)   // K slices beyond 4 (inter > 4096): rare, added in order
         for (int ds = 0; ds < 4 && s0 + ds < ns; ++ds) acc += __ldcg(p.part + (((size_t)(s0 + ds) * KP + kp) * H + h) * T + t);
     }
-    if (p.n_sh_items) {
+    if (p.n_sh_items && t >= p.sh_t0 && t < p.sh_t1) {
       float sh = 0.0f;
       for (int k0 = 0; k0 < p.KP_s; k0 += 8) {
         float v[8];
@@ -884,6 +885,8 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   p.hb = hb;
   p.out = a.out;
   p.out_f32 = d.out_f32 ? 1 : 0;
+  p.sh_t0 = a.sh_row0;
+  p.sh_t1 = a.sh_row1;
   p.limit = d.swiglu_limit;
   static const cudaError_t attr_rc =
       cudaFuncSetAttribute(t5_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemMax);

@@ -64,6 +64,16 @@ SIGNATURES: dict[str, tuple] = {
     "ds_moe_decode_noalloc_max_scratch": (c_size_t, []),
     "ds_moe_decode_noalloc": (c_int, [POINTER(DsMoeDesc), c_void_p, c_int, c_int64, c_void_p, c_void_p,
                                       c_void_p, c_void_p]),
+    "ds_ep_create": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
+    "ds_ep_region_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "ds_ep_ipc_handle": (c_int, [c_void_p, c_void_p]),
+    "ds_ep_connect": (c_int, [c_void_p, c_void_p]),
+    "ds_ep_connect_peers": (c_int, [c_void_p, c_void_p]),
+    "ds_ep_decode_workspace_size": (c_int, [c_void_p, POINTER(DsMoeDesc), c_int64, POINTER(c_size_t)]),
+    "ds_ep_decode": (c_int, [c_void_p, POINTER(DsMoeDesc), c_int32, c_void_p, c_int64, c_void_p, c_void_p,
+                             c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ds_ep_status": (c_int, [c_void_p, POINTER(c_int32)]),
+    "ds_ep_destroy": (c_int, [c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -283,3 +283,185 @@ def gpu_decode_layer(local_layer, n_experts: int, top_k: int, group=None,
             moe.moe_decode(xg[r0:r1], layer, il[r0:r1], gg[r0:r1], out=out[r0:r1], out_f32=True)
         return out
     return ExpertParallelDecode(n_experts, top_k, local_partial, shared_fn, group)
+
+
+# ---------------------------------------------------------------- decode over peer memory (native exchange)
+
+class PeerComm:
+    """ds_ep_* communicator: one device region per rank, mapped into every
+    rank through CUDA IPC; the library's own kernels move the token rows and
+    partial outputs over NVLink, so a decode step contains no collective call
+    and captures into a CUDA graph (``PeerDecodeGraph``).
+
+    Setup uses the process group once (handle exchange, barrier).  Device
+    waits give up after ``timeout_ms``; ``status()`` then reports bit 2 and
+    later exchanges of this communicator return at once."""
+
+    def __init__(self, max_rows: int, hidden: int, top_k: int, group=None, timeout_ms: int = 5000,
+                 _local: tuple[int, int] | None = None):
+        import ctypes
+
+        from . import _abi
+
+        self.group = group
+        if _local is not None:
+            self.world, self.rank = _local
+        else:
+            self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+            self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.max_rows, self.hidden, self.top_k = max_rows, hidden, top_k
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        h = ctypes.c_void_p()
+        _abi.call("ds_ep_create", self.world, self.rank, max_rows, hidden, top_k, timeout_ms, ctypes.byref(h))
+        self._h = h
+        if _local is not None:
+            return                       # connected by local_group
+        try:
+            buf = ctypes.create_string_buffer(64)
+            _abi.call("ds_ep_ipc_handle", h, buf)
+            handles = [bytes(buf.raw)]
+            if self.world > 1:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(buf.raw), group=group)
+            joined = ctypes.create_string_buffer(b"".join(handles), 64 * self.world)
+            _abi.call("ds_ep_connect", h, joined)
+            if self.world > 1:
+                dist.barrier(group)      # nobody writes into a peer before it has connected
+        except Exception:
+            self.close()
+            raise
+
+    @classmethod
+    def local_group(cls, devices: list, max_rows: int, hidden: int, top_k: int,
+                    timeout_ms: int = 5000) -> list["PeerComm"]:
+        """Communicators of all ranks in THIS process, rank i on devices[i]
+        (ds_ep_connect_peers).  Ranks that share a device must never wait on
+        each other; that form only serves tests of the bounded waits."""
+        import ctypes
+
+        from . import _abi
+
+        n = len(devices)
+        comms = []
+        for i, d in enumerate(devices):
+            with torch.cuda.device(torch.device(d)):
+                comms.append(cls(max_rows, hidden, top_k, timeout_ms=timeout_ms, _local=(n, i)))
+        arr = (ctypes.c_void_p * n)(*[c.handle.value for c in comms])
+        for c in comms:
+            with torch.cuda.device(c.device):
+                _abi.call("ds_ep_connect_peers", c.handle, arr)
+        return comms
+
+    @property
+    def handle(self):
+        if self._h is None:
+            raise ValueError("communicator is closed")
+        return self._h
+
+    def status(self) -> int:
+        import ctypes
+
+        from . import _abi
+
+        v = ctypes.c_int32(0)
+        _abi.call("ds_ep_status", self.handle, ctypes.byref(v))
+        return v.value
+
+    def close(self) -> None:
+        from . import _abi
+
+        if getattr(self, "_h", None) is not None:
+            torch.cuda.synchronize(self.device)
+            h, self._h = self._h, None
+            _abi.call("ds_ep_destroy", h)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class PeerDecodeLayer:
+    """One layer of expert-parallel decode on ``PeerComm``: this rank's FP4
+    shard ``local_layer`` (global experts [rank * E_l, (rank + 1) * E_l),
+    scale atoms prepared here), ``rows`` tokens per rank and step.
+
+    ``layer(x [rows, H] bf16, ids [rows, k] int32 global, gates [rows, k] f32)``
+    -> [rows, H] bf16: all ranks' routed experts plus the shared expert, the
+    layer contract of moe_layer (src/deepseeker/mlx_forward.py:388-419).
+    Every rank calls its layers in the same order."""
+
+    def __init__(self, comm: PeerComm, local_layer, n_experts: int, top_k: int, rows: int):
+        import ctypes
+
+        from . import _abi
+
+        if n_experts % comm.world:
+            raise ValueError(f"{n_experts} experts do not shard over {comm.world} ranks")
+        if local_layer.n_experts != n_experts // comm.world:
+            raise ValueError("local_layer must hold n_experts / world experts")
+        if not 1 <= rows <= comm.max_rows or top_k != comm.top_k or local_layer.hidden != comm.hidden:
+            raise ValueError("rows / top_k / hidden do not match the communicator")
+        local_layer.prepare_tc()
+        self.comm, self.layer, self.rows, self.top_k = comm, local_layer, rows, top_k
+        self.first_expert = comm.rank * local_layer.n_experts
+        self.desc = local_layer.cached_desc(top_k)
+        c = ctypes.c_size_t(0)
+        _abi.call("ds_ep_decode_workspace_size", comm.handle, ctypes.byref(self.desc), rows, ctypes.byref(c))
+        self.workspace = torch.zeros(c.value, dtype=torch.uint8, device=comm.device)
+
+    def __call__(self, x: torch.Tensor, ids: torch.Tensor, gates: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        import ctypes
+
+        from . import _abi
+        from ._dev import ptr, stream_handle
+
+        b, k = self.rows, self.top_k
+        H = self.comm.hidden
+        if x.shape != (b, H) or x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise ValueError(f"x must be a contiguous [{b}, {H}] bf16 tensor")
+        if ids.shape != (b, k) or ids.dtype != torch.int32 or not ids.is_contiguous():
+            raise ValueError(f"ids must be a contiguous [{b}, {k}] int32 tensor")
+        if gates.shape != (b, k) or gates.dtype != torch.float32 or not gates.is_contiguous():
+            raise ValueError(f"gates must be a contiguous [{b}, {k}] f32 tensor")
+        if out is None:
+            out = torch.empty(b, H, dtype=torch.bfloat16, device=x.device)
+        _abi.call("ds_ep_decode", self.comm.handle, ctypes.byref(self.desc), self.first_expert, ptr(x), b, ptr(ids),
+                  ptr(gates), ptr(out), ptr(self.workspace), self.workspace.numel(), stream_handle(x.device))
+        return out
+
+
+class PeerDecodeGraph:
+    """Softmax top-k routing + ``PeerDecodeLayer`` captured into one CUDA graph
+    over static buffers (``x``, ``logits`` in; ``out`` out).  The exchange is
+    the library's own kernels, so the graph holds no collective call; every
+    rank must replay its graphs in the same order."""
+
+    def __init__(self, layer: PeerDecodeLayer):
+        from . import moe
+
+        self.layer = layer
+        b, k, H = layer.rows, layer.top_k, layer.comm.hidden
+        E = layer.layer.n_experts * layer.comm.world
+        dev = layer.comm.device
+        self.x = torch.zeros(b, H, dtype=torch.bfloat16, device=dev)
+        self.logits = torch.zeros(b, E, dtype=torch.float32, device=dev)
+        self.w = torch.empty(b, k, dtype=torch.float32, device=dev)
+        self.ids = torch.empty(b, k, dtype=torch.int32, device=dev)
+        self.out = torch.empty(b, H, dtype=torch.bfloat16, device=dev)
+        self._route = lambda: moe.route_softmax_topk(self.logits, k, out=(self.w, self.ids))
+        self._step()                      # eager once on every rank (the exchange pairs up)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+
+    def _step(self) -> None:
+        self._route()
+        self.layer(self.x, self.ids, self.w, out=self.out)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out

@@ -278,6 +278,52 @@ int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x_dtype, int
                           const int32_t* topk_ids, const float* topk_w, void* out,
                           void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Expert-parallel decode over NVLink peer memory.
+ *
+ * Replaces, across G ranks (one process per GPU), the per-layer MoE call of a
+ * decode step (src/deepseeker/mlx_runner.py:765-985 Runner.moe ->
+ * src/deepseeker/mlx_forward.py:257-419 moe_layer).  Rank r holds experts
+ * [first_expert, first_expert + desc->n_experts) of every layer and decodes
+ * `rows` tokens per step; the token rows are exchanged and the partial
+ * outputs summed by the library's own kernels through CUDA IPC mappings of
+ * every rank's region (no collective library on the data path, so a step
+ * captures into a CUDA graph).
+ *
+ * Setup, on every rank with its device current:
+ *   ds_ep_create -> ds_ep_ipc_handle -> (exchange the world handles, e.g.
+ *   torch.distributed.all_gather_object) -> ds_ep_connect(all handles, in
+ *   rank order) -> a barrier, so that no rank writes into a peer before the
+ *   peer has connected.
+ * Step: every rank calls ds_ep_decode for the same layers in the same order
+ * with the same `rows`.  Device waits give up after `timeout_ms`; the error
+ * word then holds bit 2 (ds_ep_status), and later calls of that
+ * communicator return without exchanging (outputs undefined).
+ * Limits: world <= 8, world * max_rows <= 8, FP4 banks with scale atoms,
+ * hidden and inter multiples of 1024 (the tcgen05 decode kernels). */
+#define DS_EP_HANDLE_BYTES 64
+typedef struct DsEp DsEp;
+int ds_ep_create(int world, int rank, int max_rows, int hidden, int top_k, int timeout_ms, DsEp** ep);
+size_t ds_ep_region_bytes(int world, int max_rows, int hidden, int top_k);
+int ds_ep_ipc_handle(DsEp* ep, void* handle /* DS_EP_HANDLE_BYTES */);
+int ds_ep_connect(DsEp* ep, const void* handles /* world * DS_EP_HANDLE_BYTES, rank order */);
+/* Same as ds_ep_connect for communicators created by ONE process (one per
+ * device, or several on one device: the single-device form exists to test
+ * the bounded waits, since ranks sharing a GPU must not wait on each other).
+ * all[world] in rank order, all[rank] == ep; peer access is enabled between
+ * distinct devices. */
+int ds_ep_connect_peers(DsEp* ep, DsEp* const* all);
+int ds_ep_decode_workspace_size(DsEp* ep, const DsMoeDesc* desc, int64_t rows, size_t* bytes);
+/* x [rows, hidden] bf16, topk_ids [rows, top_k] GLOBAL expert ids (-1 =
+ * none), topk_w [rows, top_k] f32 -> out [rows, hidden] bf16: routed experts
+ * of all ranks (route weight before the down projection) plus this layer's
+ * shared expert (desc->shared_*, evaluated by each rank for its own rows). */
+int ds_ep_decode(DsEp* ep, const DsMoeDesc* desc, int32_t first_expert, const void* x, int64_t rows,
+                 const int32_t* topk_ids, const float* topk_w, void* out, void* workspace,
+                 size_t workspace_bytes, void* stream);
+int ds_ep_status(DsEp* ep, int32_t* err);
+int ds_ep_destroy(DsEp* ep);
+
 #ifdef __cplusplus
 }
 #endif

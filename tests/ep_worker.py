@@ -103,6 +103,8 @@ def rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
                 q.put((rank, f"error: {type(e).__name__}: {str(e)[:300]}"))
                 return
             q.put((rank, out))
+        elif mode == "gpu_peer":
+            run_gpu_peer_rank(rank, world, q)
         else:
             run_gpu_rank(rank, world, q, decode=(mode == "gpu_decode"))
         dist.destroy_process_group()
@@ -137,3 +139,29 @@ def run_gpu_rank(rank: int, world: int, q, decode: bool = False) -> None:
         out = ep.gpu_layer(layer, Eg, Kg)(x, ids, w)
     torch.cuda.synchronize()
     q.put((rank, out.cpu()))
+
+
+def run_gpu_peer_rank(rank: int, world: int, q) -> None:
+    """PeerComm decode of the first 4 tokens on every rank: eager call, then
+    the same step replayed from a CUDA graph (routing from the oracle's logits
+    inside the graph); returns both outputs."""
+    from deepseeker import ep
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    layer, x, ids, w, Eg, Kg = gpu_problem(rank, world)
+    comm = ep.PeerComm(4, layer.hidden, Kg, timeout_ms=10000)
+    pl = ep.PeerDecodeLayer(comm, layer, Eg, Kg, rows=4)
+    eager = pl(x[:4].contiguous(), ids[:4].contiguous(), w[:4].contiguous())
+    g = torch.Generator().manual_seed(78)
+    logits = torch.randn(4, Eg, generator=g).to(x.device)
+    gr = ep.PeerDecodeGraph(pl)
+    gr.x.copy_(x[:4])
+    gr.logits.copy_(logits)
+    out_g = gr.replay().clone()
+    torch.cuda.synchronize()
+    status = comm.status()
+    del gr
+    comm.close()
+    q.put((rank, (eager.cpu(), out_g.cpu(), logits.cpu(), status)))
