@@ -272,14 +272,20 @@ def run_ep(args) -> dict:
             graphs = [ep.PeerDecodeGraph(pl) for pl in eps]
     else:
         eps = [ep.gpu_layer(layer, E, K_TOP) for layer in layers]
+    # graph mode: the L layers back to back in one CUDA graph (no collective
+    # inside: the exchange is the library's own kernels)
+    chain = moe.GraphChain(graphs) if graphs is not None and os.environ.get("DEEPSEEKER_BENCH_NO_CHAIN") != "1" \
+        else None
     total_steps = args.warmup + args.steps
+    n_in = (total_steps + 64 + L - 1) // L * L
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
-    logits = torch.randn(total_steps + 64, b, E, generator=g, device=dev)
-    xs = torch.randn(total_steps + 64, b, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(n_in, b, E, generator=g, device=dev)
+    xs = torch.randn(n_in, b, H, generator=g, device=dev).to(torch.bfloat16)
     stream = torch.cuda.current_stream(dev)
 
     def step(i, ev=None):
+        i %= n_in
         if graphs is not None:
             gr = graphs[i % L]
             gr.x.copy_(xs[i])
@@ -296,24 +302,66 @@ def run_ep(args) -> dict:
             ev[1].record(stream)
         return out
 
+    def run_steps(i0, n, timed=None):
+        """Steps i0 .. i0+n-1 (every rank the same); `timed` collects (start, end, layers)."""
+        i = i0
+        while i < i0 + n:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) \
+                if timed is not None else None
+            j = i % n_in
+            if chain is not None and j % L == 0 and i + L <= i0 + n:
+                chain.x.copy_(xs[j:j + L])
+                chain.logits.copy_(logits[j:j + L])
+                if ev is not None:
+                    ev[0].record(stream)
+                chain.replay()
+                if ev is not None:
+                    ev[1].record(stream)
+                    timed.append((ev[0], ev[1], L))
+                i += L
+            else:
+                step(i, ev)
+                if ev is not None:
+                    timed.append((ev[0], ev[1], 1))
+                i += 1
+
+    def agreed_steps(ms_per_step: float, target_ms: float) -> int:
+        """A step count (multiple of L) worth ~target_ms, the same on every rank."""
+        n = int(target_ms / max(ms_per_step, 1e-3)) // L * L
+        t = torch.tensor([min(max(n, L), 40000)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return int(t.item())
+
     with ClockSampler(local) as clk:
-        for i in range(max(args.warmup, 3)):
-            step(i)
+        w_steps = max(args.warmup, 3)
+        w_steps = (w_steps + L - 1) // L * L
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        run_steps(0, w_steps)
+        c1.record(stream)
+        torch.cuda.synchronize(dev)
+        if not args.quick:
+            # more warm-up, ~1 s, so that clocks settle and get sampled
+            extra = agreed_steps(c0.elapsed_time(c1) / w_steps, 1000.0)
+            run_steps(w_steps, extra)
+            w_steps += extra
         torch.cuda.synchronize(dev)
         dist.barrier()
         torch.cuda.synchronize(dev)
-        pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                 for _ in range(args.steps)]
+        timed = []
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        for s_ in range(args.steps):
-            step(args.warmup + s_, pairs[s_])
+        run_steps(w_steps, args.steps, timed)
         end.record(stream)
         torch.cuda.synchronize(dev)
         dist.barrier()
         torch.cuda.synchronize(dev)
         ms = start.elapsed_time(end)
-        layer_ms = statistics.mean(a.elapsed_time(c) for a, c in pairs)
+        layer_ms = sum(a.elapsed_time(c) for a, c, _ in timed) / sum(n for _, _, n in timed)
+        if not args.quick:
+            # keep the GPUs busy a little longer so the sampler sees the load
+            run_steps(0, agreed_steps(ms / args.steps, 500.0))
+            torch.cuda.synchronize(dev)
     clocks = clk.summary()
 
     # e2e: the step's x and logits from pinned host memory, output back to the host
@@ -353,14 +401,16 @@ def run_ep(args) -> dict:
     # bytes one rank streams per step: the distinct experts of this rank that
     # the step's routing of ALL ranks touches (counted from the timed steps'
     # routing, gathered after the timing) + the shared expert for its tokens
-    timed_ids = torch.stack([moe.route_softmax_topk(logits[args.warmup + s_], K_TOP)[1]
+    timed_ids = torch.stack([moe.route_softmax_topk(logits[(w_steps + s_) % n_in], K_TOP)[1]
                              for s_ in range(args.steps)])                    # [steps, b, k]
     all_ids = torch.empty((world,) + tuple(timed_ids.shape), dtype=timed_ids.dtype, device=dev)
     dist.all_gather_into_tensor(all_ids, timed_ids.contiguous())
     all_ids = all_ids.permute(1, 0, 2, 3).reshape(args.steps, -1).cpu()
     mine = [len({int(e) for e in row.tolist() if rank * El <= e < (rank + 1) * El}) for row in all_ids]
     distinct = statistics.mean(mine) if mine else float(b * K_TOP)
-    step_bytes = distinct * per_expert + 3 * IS * H * 2 * ((b + 7) // 8) + 2 * b * H * 2
+    # shared expert: split over the ranks when its inter divides into world slices of 256
+    shared_b = 3 * IS * H * 2 // world if (small and IS % (256 * world) == 0) else 3 * IS * H * 2 * ((b + 7) // 8)
+    step_bytes = distinct * per_expert + shared_b + 2 * b * H * 2
     ms_t = torch.tensor([ms, e2e_ms, layer_ms], device=dev)
     dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms, e2e_ms, layer_ms = (float(v) for v in ms_t.cpu())
@@ -382,12 +432,13 @@ def run_ep(args) -> dict:
             "dtype": f"{fmt} weights, bf16 activations, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights quantised on device; router logits N(0,1))",
             "config": {"workload": f"BASELINE config {'2' if fmt == 'fp4' else '3'} layer, expert-parallel over "
-                                   f"{world} GPUs ({El} experts each, shared expert replicated), {b} decode "
+                                   f"{world} GPUs ({El} experts each; shared expert split over the ranks by "
+                                   f"intermediate slices), {b} decode "
                                    "token(s) per GPU per step",
                        "format": fmt, "tokens_per_step_per_gpu": b, "layers_rotated": L,
                        "l2": f"rotating {L} resident layer shards per GPU",
                        "parallelism": (f"ep{world} (token rows and partial sums exchanged over NVLink peer "
-                                       "memory by the library's kernels, one CUDA graph per layer)"
+                                       "memory by the library's kernels; the rotated layers back to back in one CUDA graph)"
                                        if small else f"ep{world} (NCCL all_to_all_single dispatch + combine)"),
                        "distinct_local_experts_per_step": round(distinct, 3)},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -399,7 +450,7 @@ def run_ep(args) -> dict:
             "gpu_launches": args.steps * ((1 + 1 + 5 + 1) if small else (1 + 5 + 2 * ((b + 7) // 8))),
             "clocks": clocks,
         }
-    del graphs, eps
+    del chain, graphs, eps
     torch.cuda.synchronize(dev)
     dist.barrier()
     if comm is not None:
@@ -586,21 +637,26 @@ def run_decode(args) -> dict:
         for layer in layers:
             layer.prepare_tc()   # scale atoms: ds_moe_decode then runs its tcgen05 kernels
     total_steps = args.warmup + args.steps
+    n_in = (total_steps + 64 + L - 1) // L * L          # input slots, a whole number of layer rotations
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
-    logits = torch.randn(total_steps + 64, tokens, E, generator=g, device=dev)
-    xs = torch.randn(total_steps + 64, tokens, H, generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn(n_in, tokens, E, generator=g, device=dev)
+    xs = torch.randn(n_in, tokens, H, generator=g, device=dev).to(torch.bfloat16)
     outs = torch.empty(L, tokens, H, dtype=torch.bfloat16, device=dev)
     ws = moe._workspace(dev, moe.decode_workspace_bytes(layers[0], tokens, K_TOP))
     stream = torch.cuda.current_stream(dev)
 
-    # routing (device) + decode for step i on layer i % L, replayed from one
-    # CUDA graph per layer (moe.DecodeGraph); the step's x and logits are
-    # copied into the graph's input buffers first
+    # routing (device) + decode for step i on layer i % L.  Graph mode: the L
+    # layers' steps are captured back to back into one CUDA graph
+    # (moe.GraphChain over one moe.DecodeGraph per layer), so L consecutive
+    # steps are one launch whose inputs are staged by two copies; steps that
+    # do not fill a whole rotation replay their layer's own graph.
     use_graph = os.environ.get("DEEPSEEKER_BENCH_NO_GRAPH") != "1"
     graphs = [moe.DecodeGraph(layer, tokens, K_TOP, dev) for layer in layers] if use_graph else None
+    chain = moe.GraphChain(graphs) if use_graph and os.environ.get("DEEPSEEKER_BENCH_NO_CHAIN") != "1" else None
 
     def step(i, ev=None):
+        i %= n_in
         if use_graph:
             gr = graphs[i % L]
             gr.x.copy_(xs[i])
@@ -616,41 +672,63 @@ def run_decode(args) -> dict:
         if ev is not None:
             ev[1].record(stream)
 
+    def run_steps(i0, n, timed=None):
+        """Steps i0 .. i0+n-1; `timed` collects (start, end, layers) events."""
+        i = i0
+        while i < i0 + n:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) \
+                if timed is not None else None
+            j = i % n_in
+            if chain is not None and j % L == 0 and i + L <= i0 + n:
+                chain.x.copy_(xs[j:j + L])
+                chain.logits.copy_(logits[j:j + L])
+                if ev is not None:
+                    ev[0].record(stream)
+                chain.replay()
+                if ev is not None:
+                    ev[1].record(stream)
+                    timed.append((ev[0], ev[1], L))
+                i += L
+            else:
+                step(i, ev)
+                if ev is not None:
+                    timed.append((ev[0], ev[1], 1))
+                i += 1
+
     min_warm_s = 0.0 if args.quick else 1.0
     with ClockSampler(local) as clk:
         # warm-up: at least W steps and at least ~1 s so clocks settle and get sampled
         t0 = time.perf_counter()
         i = 0
         while i < args.warmup or time.perf_counter() - t0 < min_warm_s:
-            step(i % (total_steps + 64))
-            i += 1
-            if i % 256 == 0:
+            run_steps(i, L)
+            i += L
+            if i % 256 < L:
                 torch.cuda.synchronize(dev)
         torch.cuda.synchronize(dev)
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize(dev)
         # ---- timed region: K steps, inputs resident
-        pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                 for _ in range(args.steps)]
+        timed = []
+        i_start = (args.warmup + L - 1) // L * L
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        for s in range(args.steps):
-            step(args.warmup + s, pairs[s])
+        run_steps(i_start, args.steps, timed)
         end.record(stream)
         torch.cuda.synchronize(dev)
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize(dev)
         ms = start.elapsed_time(end)
-        decode_ms = [a.elapsed_time(b) for a, b in pairs]
+        decode_ms = [a.elapsed_time(b) / n for a, b, n in timed for _ in range(n)]
         # keep the GPU busy a little longer so the sampler sees the load
         t1 = time.perf_counter()
         j = 0
         while time.perf_counter() - t1 < (0.0 if args.quick else 0.6):
-            step(j % (total_steps + 64))
-            j += 1
-            if j % 256 == 0:
+            run_steps(j, L)
+            j += L
+            if j % 256 < L:
                 torch.cuda.synchronize(dev)
         torch.cuda.synchronize(dev)
     clocks = clk.summary()

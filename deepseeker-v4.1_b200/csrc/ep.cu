@@ -10,12 +10,16 @@
 //      for all G flags of its own area and rewrites the gathered ids to local
 //      expert ids (-1 where another rank owns the expert).
 //   2. the tcgen05 decode kernels (moe_decode_t5.cu) over the G*b gathered
-//      rows: this rank's routed experts for every row, its own rows' shared
-//      expert, f32 partial rows out.
+//      rows: this rank's routed experts for every row and slice `rank` of
+//      the shared expert's intermediate features for every row (when the
+//      shared inter splits into G slices of 256; otherwise the whole shared
+//      expert for its own rows), f32 partial rows out.
 //   3. ep_combine_kernel: every rank stores the partial rows of rank q's
-//      tokens into slot `rank` of q's reduce area, raises a flag there, waits
-//      for all G flags of its own area and sums the G slots in rank order
-//      into its bf16 output.
+//      tokens into slot `rank` of q's reduce areas, raises a flag there,
+//      waits for all G flags of its own area and sums the G slots in rank
+//      order into its bf16 output: routed partials, plus the shared sum
+//      rounded to bf16 first (the reference adds the shared expert's output
+//      in the activation dtype, src/deepseeker/mlx_runner.py:776-781).
 //
 // Nothing on the path calls NCCL, so a step of many layers captures into one
 // CUDA graph.  Flags carry epochs: each kernel block keeps a counter in local
@@ -59,8 +63,8 @@ size_t up256(size_t v) { return (v + 255) / 256 * 256; }
 // first part (flags, receive and reduce areas) is written by peers; the rest
 // is local.
 struct EpLayout {
-  size_t flags_g, flags_r, recv_x, recv_ids, recv_w, rbuf;   // peer-visible
-  size_t ctr, err, ids_local, part;                           // local
+  size_t flags_g, flags_r, recv_x, recv_ids, recv_w, rbuf, rbuf_sh;   // peer-visible
+  size_t ctr, err, ids_local, part, part_sh;                           // local
   size_t total;
 };
 
@@ -74,10 +78,12 @@ EpLayout ep_layout(int world, int max_rows, int H, int k) {
   L.recv_ids = o;  o += up256(R * k * 4);
   L.recv_w = o;    o += up256(R * k * 4);
   L.rbuf = o;      o += up256(R * H * 4);
+  L.rbuf_sh = o;   o += up256(R * H * 4);
   L.ctr = o;       o += 512;
   L.err = o;       o += 256;
   L.ids_local = o; o += up256(R * k * 4);
   L.part = o;      o += up256(R * H * 4);
+  L.part_sh = o;   o += up256(R * H * 4);
   L.total = o;
   return L;
 }
@@ -87,6 +93,7 @@ struct EpArgs {
   EpLayout L;
   int world, rank, rows, H, k;
   int first_expert, local_experts;
+  int split;               // 1: the shared expert's partial sums travel in their own area (rbuf_sh)
   const void* x;           // [rows, H] bf16 (dispatch)
   const int32_t* ids;      // [rows, k] global ids
   const float* gates;      // [rows, k]
@@ -140,6 +147,8 @@ __device__ bool block_wait_flags(const uint32_t* flags, int n, uint32_t target, 
 // receive area, raise q's flag, wait for q's rows in our own area, rewrite
 // their ids to local ids.
 __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const __grid_constant__ EpArgs a) {
+  ds::ptx::wait_prior_grid();        // x / ids / gates come from the previous kernel (router)
+  ds::ptx::launch_dependents();
   char* own = a.base[a.rank];
   int* err = reinterpret_cast<int*>(own + a.L.err);
   volatile int* abort = err + 1;
@@ -190,6 +199,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const __grid_co
 // `rank` of q's reduce area, raise q's flag, wait for every rank's slot in
 // our own area, sum the slots in rank order into the bf16 output.
 __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const __grid_constant__ EpArgs a) {
+  ds::ptx::wait_prior_grid();        // partial rows come from the decode kernels
+  ds::ptx::launch_dependents();
   char* own = a.base[a.rank];
   int* err = reinterpret_cast<int*>(own + a.L.err);
   volatile int* abort = err + 1;
@@ -212,14 +223,22 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const __grid_con
     float4* to = reinterpret_cast<float4*>(a.base[q] + a.L.rbuf) + (size_t)a.rank * slot_elems / 4;
     const int nv = (int)(slot_elems / 4);
     for (int i = part * kEpThreads + threadIdx.x; i < nv; i += kCombineBlocks * kEpThreads) to[i] = src[i];
+    if (a.split) {
+      const float4* ssrc = reinterpret_cast<const float4*>(own + a.L.part_sh) + (size_t)q * slot_elems / 4;
+      float4* sto = reinterpret_cast<float4*>(a.base[q] + a.L.rbuf_sh) + (size_t)a.rank * slot_elems / 4;
+      for (int i = part * kEpThreads + threadIdx.x; i < nv; i += kCombineBlocks * kEpThreads) sto[i] = ssrc[i];
+    }
   }
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) red_release_sys(reinterpret_cast<uint32_t*>(a.base[q] + a.L.flags_r) + a.rank, 1u);
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(own + a.L.flags_r);
   if (!block_wait_flags(flags, G, epoch * kCombineBlocks, a.timeout_ns, err, abort)) return;
-  // sum: this block's share of the b * H outputs, 4 at a time
+  // sum: this block's share of the b * H outputs, 4 at a time; routed
+  // partials in rank order, then (split) the shared expert's sum rounded to
+  // bf16 before it is added, as the unsplit layer does
   const float4* rb = reinterpret_cast<const float4*>(own + a.L.rbuf);
+  const float4* rs = reinterpret_cast<const float4*>(own + a.L.rbuf_sh);
   const int nv = (int)(slot_elems / 4);
   uint2* out = static_cast<uint2*>(a.out);
   for (int i = blockIdx.x * kEpThreads + threadIdx.x; i < nv; i += gridDim.x * kEpThreads) {
@@ -230,6 +249,20 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const __grid_con
       acc.y += v.y;
       acc.z += v.z;
       acc.w += v.w;
+    }
+    if (a.split) {
+      float4 sh = __ldcg(rs + i);
+      for (int j = 1; j < G; ++j) {
+        const float4 v = __ldcg(rs + (size_t)j * nv + i);
+        sh.x += v.x;
+        sh.y += v.y;
+        sh.z += v.z;
+        sh.w += v.w;
+      }
+      acc.x += __bfloat162float(__float2bfloat16_rn(sh.x));
+      acc.y += __bfloat162float(__float2bfloat16_rn(sh.y));
+      acc.z += __bfloat162float(__float2bfloat16_rn(sh.z));
+      acc.w += __bfloat162float(__float2bfloat16_rn(sh.w));
     }
     const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
     const __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
@@ -439,15 +472,41 @@ extern "C" int ds_ep_decode(DsEp* ep, const DsMoeDesc* desc, int32_t first_exper
   d.err = static_cast<int*>(workspace);
   d.sh_row0 = ep->rank * b;
   d.sh_row1 = ep->rank * b + b;
+  // shared expert: when its inter splits into G slices of 256, rank r
+  // evaluates slice r for all gathered rows (f32 partial sums, summed over
+  // the ranks in the combine); otherwise each rank evaluates all of it for
+  // its own rows
+  const bool sh = desc->shared_w1 != nullptr;
+  a.split = sh && desc->shared_inter % (256 * G) == 0;
+  if (a.split) {
+    const int Is = desc->shared_inter, Isl = Is / G, r = ep->rank;
+    d.d.shared_inter = Isl;
+    d.d.shared_w1 = static_cast<const __nv_bfloat16*>(desc->shared_w1) + (size_t)r * Isl * desc->hidden;
+    d.d.shared_w3 = static_cast<const __nv_bfloat16*>(desc->shared_w3) + (size_t)r * Isl * desc->hidden;
+    d.d.shared_w2 = static_cast<const __nv_bfloat16*>(desc->shared_w2) + (size_t)r * Isl;
+    d.sh_w2_ld = Is;
+    d.out_sh = reinterpret_cast<float*>(ep->own + ep->L.part_sh);
+  }
   DS_REQUIRE(ds::decode::t5_supported(d), DS_ENOTSUP,
              "ep_decode: needs FP4 banks with scale atoms, hidden and inter multiples of 1024 (tensor-core "
              "decode kernels)");
 
-  ep_dispatch_kernel<<<G * kDispatchBlocks, kEpThreads, 0, st>>>(a);
-  DS_CHECK_LAUNCH("ep_dispatch_kernel");
+  // programmatic dependent launches: each kernel starts while its
+  // predecessor drains and waits for it (griddepcontrol.wait) before it
+  // reads what the predecessor wrote
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(kEpThreads);
+  cfg.gridDim = dim3(G * kDispatchBlocks);
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, ep_dispatch_kernel, a));
   int rc = ds::decode::launch_t5(d, workspace, workspace_bytes, st);
   if (rc != DS_OK) return rc;
-  ep_combine_kernel<<<G * kCombineBlocks, kEpThreads, 0, st>>>(a);
-  DS_CHECK_LAUNCH("ep_combine_kernel");
+  cfg.gridDim = dim3(G * kCombineBlocks);
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, ep_combine_kernel, a));
   return DS_OK;
 }

@@ -102,6 +102,7 @@ struct T5Params {
   void* out;                  // down output [T][H]: bf16, or f32 when out_f32
   int out_f32;
   int sh_t0, sh_t1;           // output rows that receive the shared expert
+  float* out_sh;              // non-null: shared expert sum [T][H] f32 goes here, unrounded
   float limit;
 };
 
@@ -277,7 +278,7 @@ __device__ void tail_combine(const T5Params& p, int r0, int lane) {
       for (int kp = 4; kp < KP; ++kp)   // K slices beyond 4 (inter > 4096): rare, added in order
         for (int ds = 0; ds < 4 && s0 + ds < ns; ++ds) acc += __ldcg(p.part + (((size_t)(s0 + ds) * KP + kp) * H + h) * T + t);
     }
-    if (p.n_sh_items && t >= p.sh_t0 && t < p.sh_t1) {
+    if (p.n_sh_items && (p.out_sh != nullptr || (t >= p.sh_t0 && t < p.sh_t1))) {
       float sh = 0.0f;
       for (int k0 = 0; k0 < p.KP_s; k0 += 8) {
         float v[8];
@@ -286,7 +287,8 @@ __device__ void tail_combine(const T5Params& p, int r0, int lane) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) sh += v[k];
       }
-      acc += __bfloat162float(__float2bfloat16_rn(sh));
+      if (p.out_sh != nullptr) p.out_sh[(size_t)t * H + h] = sh;
+      else acc += __bfloat162float(__float2bfloat16_rn(sh));
     }
     if (p.out_f32) static_cast<float*>(p.out)[(size_t)t * H + h] = acc;
     else static_cast<__nv_bfloat16*>(p.out)[(size_t)t * H + h] = __float2bfloat16_rn(acc);
@@ -691,6 +693,18 @@ bool map3(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, u
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Same with a row stride wider than the rows (a column slice of a matrix).
+bool map3s(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint64_t stride_bytes,
+           uint32_t box_rows, uint32_t box_chunks) {
+  const cuuint64_t dims[3] = {128, rows, row_bytes / 128};
+  const cuuint64_t strides[2] = {stride_bytes, 128};
+  const cuuint32_t box[3] = {128, box_rows, box_chunks};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return encode_fn5()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 size_t up256(size_t v) { return (v + 255) / 256 * 256; }
 
 // Tensor maps of one call that do not depend on x, cached by what they
@@ -818,7 +832,8 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   {
     const void* key[12] = {d.w1.data, d.w3.data, d.w2.data, d.shared_w1, d.shared_w3, d.shared_w2,
                            workspace, nullptr, nullptr, nullptr, nullptr, nullptr};
-    const int geo[8] = {H, I, E, Is, T, S, 0, 0};
+    const int sh_ld = a.sh_w2_ld > 0 ? a.sh_w2_ld : Is;
+    const int geo[8] = {H, I, E, Is, T, S, sh_ld, 0};
     int dev = 0;
     cudaGetDevice(&dev);
     key[7] = reinterpret_cast<const void*>((uintptr_t)dev + 1);
@@ -839,7 +854,7 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
                 map3(&ms.hq, hq, (uint64_t)S * kPieceRows, I / 2, NB, 2, true) &&
                 (!sh || (map3(&ms.sw1, d.shared_w1, Is, (uint64_t)H * 2, 128, 2, true) &&
                          map3(&ms.sw3, d.shared_w3, Is, (uint64_t)H * 2, 128, 2, true) &&
-                         map3(&ms.sw2, d.shared_w2, H, (uint64_t)Is * 2, 128, 2, true) &&
+                         map3s(&ms.sw2, d.shared_w2, H, (uint64_t)Is * 2, (uint64_t)sh_ld * 2, 128, 2) &&
                          map3(&ms.hb, hb, 16, (uint64_t)Is * 2, 16, 2, true)));
       DS_REQUIRE(ok, DS_ECUDA, "moe_decode: tensor map encoding failed (tensor-core path)");
       const int slot = g_map_n < kMapCache ? g_map_n++ : (g_map_next++ % kMapCache);
@@ -887,6 +902,7 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   p.out_f32 = d.out_f32 ? 1 : 0;
   p.sh_t0 = a.sh_row0;
   p.sh_t1 = a.sh_row1;
+  p.out_sh = a.out_sh;
   p.limit = d.swiglu_limit;
   static const cudaError_t attr_rc =
       cudaFuncSetAttribute(t5_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemMax);

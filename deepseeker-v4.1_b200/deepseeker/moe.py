@@ -344,3 +344,33 @@ class DecodeGraph:
     def replay(self) -> torch.Tensor:
         self.graph.replay()
         return self.out
+
+
+class GraphChain:
+    """Several captured layers (``DecodeGraph`` or ``ep.PeerDecodeGraph``:
+    objects with static ``x``, ``logits``, ``out`` buffers and ``_step()``)
+    captured back to back into ONE CUDA graph, their inputs staged from two
+    stacked buffers: a decode step through many layers is one graph launch,
+    the way a serving loop runs its layer stack.
+
+    ``x [n, T, H]`` and ``logits [n, T, E]`` hold layer i's inputs at [i];
+    ``replay()`` runs all n layers (layer i's output in ``layers[i].out``)."""
+
+    def __init__(self, layers):
+        if not layers:
+            raise ValueError("GraphChain needs at least one layer")
+        self.layers = list(layers)
+        n = len(self.layers)
+        x0, l0 = self.layers[0].x, self.layers[0].logits
+        self.x = torch.zeros((n,) + tuple(x0.shape), dtype=x0.dtype, device=x0.device)
+        self.logits = torch.zeros((n,) + tuple(l0.shape), dtype=l0.dtype, device=l0.device)
+        torch.cuda.synchronize(x0.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            for i, layer in enumerate(self.layers):
+                layer.x.copy_(self.x[i])
+                layer.logits.copy_(self.logits[i])
+                layer._step()
+
+    def replay(self) -> None:
+        self.graph.replay()

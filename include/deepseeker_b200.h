@@ -317,7 +317,10 @@ int ds_ep_decode_workspace_size(DsEp* ep, const DsMoeDesc* desc, int64_t rows, s
 /* x [rows, hidden] bf16, topk_ids [rows, top_k] GLOBAL expert ids (-1 =
  * none), topk_w [rows, top_k] f32 -> out [rows, hidden] bf16: routed experts
  * of all ranks (route weight before the down projection) plus this layer's
- * shared expert (desc->shared_*, evaluated by each rank for its own rows). */
+ * shared expert (desc->shared_*, the full matrices on every rank: rank r
+ * evaluates intermediate slice r of it for all ranks' rows when
+ * shared_inter is a multiple of 256 * world, else all of it for its own
+ * rows; its output is rounded to bf16 before it joins the routed sum). */
 int ds_ep_decode(DsEp* ep, const DsMoeDesc* desc, int32_t first_expert, const void* x, int64_t rows,
                  const int32_t* topk_ids, const float* topk_w, void* out, void* workspace,
                  size_t workspace_bytes, void* stream);

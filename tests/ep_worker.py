@@ -112,14 +112,15 @@ def rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
         q.put((rank, f"exception: {e!r}"))
 
 
-def gpu_problem(rank: int, world: int):
+def gpu_problem(rank: int, world: int, shared_inter: int = 512):
     from deepseeker import synthetic
     from oracle import moe as omoe
 
     dev = torch.device("cuda", rank)
     Hg, Ig, Eg, Kg, Bg = 1024, 1024, 16, 4, 6
     El = Eg // world
-    layer = synthetic.make_layer("fp4", Hg, Ig, El, seed=5, shared_inter=512, device=dev, expert_offset=rank * El)
+    layer = synthetic.make_layer("fp4", Hg, Ig, El, seed=5, shared_inter=shared_inter, device=dev,
+                                 expert_offset=rank * El)
     g = torch.Generator().manual_seed(77)
     x = torch.randn(Bg, Hg, generator=g).to(torch.bfloat16).to(dev)
     w, ids = omoe.route_softmax_topk(torch.randn(Bg, Eg, generator=g), Kg)
@@ -161,7 +162,13 @@ def run_gpu_peer_rank(rank: int, world: int, q) -> None:
     gr.logits.copy_(logits)
     out_g = gr.replay().clone()
     torch.cuda.synchronize()
+    # shared inter 256 does not split over 2 ranks: each rank evaluates the
+    # whole shared expert for its own rows
+    layer2 = gpu_problem(rank, world, shared_inter=256)[0]
+    pl2 = ep.PeerDecodeLayer(comm, layer2, Eg, Kg, rows=4)
+    eager2 = pl2(x[:4].contiguous(), ids[:4].contiguous(), w[:4].contiguous())
+    torch.cuda.synchronize()
     status = comm.status()
     del gr
     comm.close()
-    q.put((rank, (eager.cpu(), out_g.cpu(), logits.cpu(), status)))
+    q.put((rank, (eager.cpu(), out_g.cpu(), logits.cpu(), status, eager2.cpu())))

@@ -6,9 +6,10 @@
 * one GPU, bounded waits: rank 0 of a two-rank group runs alone, its
   dispatch waits on a flag nothing raises, gives up after the timeout and
   reports it; the context stays usable;
-* two GPUs (skipped with fewer): each rank holds half of the experts; both
-  outputs within 1e-3 rel-L2 of the one-rank decode, graph replay equal to
-  the eager path.
+* two GPUs (skipped with fewer): each rank holds half of the experts and
+  half of the shared expert's intermediate features (or, when those do not
+  split, the whole shared expert for its own rows); outputs within 1e-3
+  rel-L2 of the one-rank decode, graph replays likewise.
 """
 from __future__ import annotations
 
@@ -102,6 +103,8 @@ def test_peer_two_ranks(cuda):
     layer.prepare_tc()
     x4, i4, w4 = x[:4].contiguous(), ids[:4].contiguous(), w[:4].contiguous()
     single = moe.moe_decode(x4, layer, i4, w4).cpu()
+    layer2 = ep_worker.gpu_problem(0, 1, shared_inter=256)[0].prepare_tc()
+    single2 = moe.moe_decode(x4, layer2, i4, w4).cpu()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
@@ -122,9 +125,10 @@ def test_peer_two_ranks(cuda):
                 p.kill()
     for r in (0, 1):
         assert isinstance(res[r], tuple), res[r]
-        eager, out_g, logits, status = res[r]
+        eager, out_g, logits, status, eager2 = res[r]
         assert status == 0
-        assert rel_l2(eager, single) <= 1e-3, rel_l2(eager, single)
+        assert rel_l2(eager, single) <= 1e-3, rel_l2(eager, single)            # shared expert split 2 ways
+        assert rel_l2(eager2, single2) <= 1e-3, rel_l2(eager2, single2)        # shared expert per own rows
         wr, ir = moe.route_softmax_topk(logits.to(x.device), K)
         ref_g = moe.moe_decode(x4, layer, ir, wr).cpu()
         assert rel_l2(out_g, ref_g) <= 1e-3, rel_l2(out_g, ref_g)
