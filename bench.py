@@ -269,13 +269,15 @@ def run_ep(args) -> dict:
         comm = ep.PeerComm(b, H, K_TOP, timeout_ms=30000)
         eps = [ep.PeerDecodeLayer(comm, layer, E, K_TOP, rows=b) for layer in layers]
         if os.environ.get("DEEPSEEKER_BENCH_NO_GRAPH") != "1":
-            graphs = [ep.PeerDecodeGraph(pl) for pl in eps]
+            stage_x = torch.zeros(L, b, H, dtype=torch.bfloat16, device=dev)
+            stage_l = torch.zeros(L, b, E, dtype=torch.float32, device=dev)
+            graphs = [ep.PeerDecodeGraph(pl, x=stage_x[l], logits=stage_l[l]) for l, pl in enumerate(eps)]
     else:
         eps = [ep.gpu_layer(layer, E, K_TOP) for layer in layers]
     # graph mode: the L layers back to back in one CUDA graph (no collective
     # inside: the exchange is the library's own kernels)
-    chain = moe.GraphChain(graphs) if graphs is not None and os.environ.get("DEEPSEEKER_BENCH_NO_CHAIN") != "1" \
-        else None
+    chain = moe.GraphChain(graphs, x=stage_x, logits=stage_l) \
+        if graphs is not None and os.environ.get("DEEPSEEKER_BENCH_NO_CHAIN") != "1" else None
     total_steps = args.warmup + args.steps
     n_in = (total_steps + 64 + L - 1) // L * L
     g = torch.Generator(device=dev)
@@ -652,8 +654,12 @@ def run_decode(args) -> dict:
     # steps are one launch whose inputs are staged by two copies; steps that
     # do not fill a whole rotation replay their layer's own graph.
     use_graph = os.environ.get("DEEPSEEKER_BENCH_NO_GRAPH") != "1"
-    graphs = [moe.DecodeGraph(layer, tokens, K_TOP, dev) for layer in layers] if use_graph else None
-    chain = moe.GraphChain(graphs) if use_graph and os.environ.get("DEEPSEEKER_BENCH_NO_CHAIN") != "1" else None
+    stage_x = torch.zeros(L, tokens, H, dtype=torch.bfloat16, device=dev)
+    stage_l = torch.zeros(L, tokens, E, dtype=torch.float32, device=dev)
+    graphs = [moe.DecodeGraph(layer, tokens, K_TOP, dev, x=stage_x[l], logits=stage_l[l])
+              for l, layer in enumerate(layers)] if use_graph else None
+    chain = moe.GraphChain(graphs, x=stage_x, logits=stage_l) \
+        if use_graph and os.environ.get("DEEPSEEKER_BENCH_NO_CHAIN") != "1" else None
 
     def step(i, ev=None):
         i %= n_in

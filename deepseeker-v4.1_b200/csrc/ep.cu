@@ -181,9 +181,14 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const __grid_co
       }
     }
   }
-  __threadfence_system();
+  // every thread's stores precede thread 0's system-scope fence (barrier),
+  // which precedes the flag (release): a peer that acquires the flag sees
+  // the rows
   __syncthreads();
-  if (threadIdx.x == 0) red_release_sys(reinterpret_cast<uint32_t*>(dst + a.L.flags_g) + a.rank, 1u);
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    red_release_sys(reinterpret_cast<uint32_t*>(dst + a.L.flags_g) + a.rank, 1u);
+  }
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(own + a.L.flags_g) + q;
   if (!block_wait_flags(flags, 1, epoch * kDispatchBlocks, a.timeout_ns, err, abort)) return;
   // slot q arrived: local ids (L2 reads: the rows were written over NVLink)
@@ -229,9 +234,11 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const __grid_con
       for (int i = part * kEpThreads + threadIdx.x; i < nv; i += kCombineBlocks * kEpThreads) sto[i] = ssrc[i];
     }
   }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) red_release_sys(reinterpret_cast<uint32_t*>(a.base[q] + a.L.flags_r) + a.rank, 1u);
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    red_release_sys(reinterpret_cast<uint32_t*>(a.base[q] + a.L.flags_r) + a.rank, 1u);
+  }
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(own + a.L.flags_r);
   if (!block_wait_flags(flags, G, epoch * kCombineBlocks, a.timeout_ns, err, abort)) return;
   // sum: this block's share of the b * H outputs, 4 at a time; routed

@@ -241,7 +241,7 @@ template <int NR, int NT>
 struct RowDot<DS_FMT_FP4, NR, NT> {
   static constexpr int U = 4;  // chunks per lane in flight, per row
   __device__ static void run(const uint8_t* const (&data)[NR], const uint8_t* const (&sc)[NR],
-                             int K, const float* xs, int xstride, int tokens,
+                             int K, const float* xs, int xstride, uint32_t tmask,
                              float (&acc)[NR][NT]) {
     const int lane = threadIdx.x & 31;
     const int nch = K / 32;
@@ -268,7 +268,7 @@ struct RowDot<DS_FMT_FP4, NR, NT> {
         if (c < nch) {
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
-            if (t < tokens) {
+            if ((tmask >> t) & 1u) {
 #pragma unroll
               for (int r = 0; r < NR; ++r) {
                 const float p = fp4_chunk_dot(w[r][u], xs + t * xstride, c);
@@ -286,7 +286,7 @@ template <int NR, int NT>
 struct RowDot<DS_FMT_BF16, NR, NT> {
   static constexpr int U = 4;
   __device__ static void run(const uint8_t* const (&data)[NR], const uint8_t* const (&)[NR], int K,
-                             const float* xs, int xstride, int tokens, float (&acc)[NR][NT]) {
+                             const float* xs, int xstride, uint32_t tmask, float (&acc)[NR][NT]) {
     const int lane = threadIdx.x & 31;
     const int nch = K / 8;
     for (int c0 = 0; c0 < nch; c0 += 32 * U) {
@@ -305,7 +305,7 @@ struct RowDot<DS_FMT_BF16, NR, NT> {
         if (c < nch) {
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
-            if (t < tokens) {
+            if ((tmask >> t) & 1u) {
 #pragma unroll
               for (int r = 0; r < NR; ++r) acc[r][t] += bf16_chunk_dot(w[r][u], xs + t * xstride, c);
             }
@@ -323,7 +323,7 @@ struct RowDotQ3 {
   static constexpr int U = 2;
   __device__ static void run(const uint8_t* const (&data)[NR], const __half* const (&sc)[NR],
                              const __half* const (&bi)[NR], int K, const float* xs, int xstride,
-                             const float* xg, int tokens, float (&acc)[NR][NT]) {
+                             const float* xg, uint32_t tmask, float (&acc)[NR][NT]) {
     const int lane = threadIdx.x & 31;
     const int ng = K / 64;
     for (int g0 = 0; g0 < ng; g0 += 32 * U) {
@@ -354,7 +354,7 @@ struct RowDotQ3 {
         if (g < ng) {
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
-            if (t < tokens) {
+            if ((tmask >> t) & 1u) {
               const float xsum = xg[t * (K / 64) + g];
 #pragma unroll
               for (int r = 0; r < NR; ++r) {
@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_kernel(const DecodeAr
         data[kRowsPerWarp + r] = p3.data; sc[kRowsPerWarp + r] = p3.sc; bi[kRowsPerWarp + r] = p3.bi;
       }
       if (FMT == DS_FMT_FP4) {
-        RowDot<DS_FMT_FP4, 2 * kRowsPerWarp, NT>::run(data, sc, H, xs, H, T, acc);
+        RowDot<DS_FMT_FP4, 2 * kRowsPerWarp, NT>::run(data, sc, H, xs, H, slots.mask[slot], acc);
       } else {
         const __half* s16[2 * kRowsPerWarp];
         const __half* b16[2 * kRowsPerWarp];
@@ -493,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_kernel(const DecodeAr
           s16[r] = reinterpret_cast<const __half*>(sc[r]);
           b16[r] = reinterpret_cast<const __half*>(bi[r]);
         }
-        RowDotQ3<2 * kRowsPerWarp, NT>::run(data, s16, b16, H, xs, H, xg, T, acc);
+        RowDotQ3<2 * kRowsPerWarp, NT>::run(data, s16, b16, H, xs, H, xg, slots.mask[slot], acc);
       }
     } else {
       const uint8_t* data[2 * kRowsPerWarp];
@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_kernel(const DecodeAr
         data[kRowsPerWarp + r] = ok ? static_cast<const uint8_t*>(a.d.shared_w3) + (size_t)n * H * 2 : nullptr;
         none[r] = none[kRowsPerWarp + r] = nullptr;
       }
-      RowDot<DS_FMT_BF16, 2 * kRowsPerWarp, NT>::run(data, none, H, xs, H, T, acc);
+      RowDot<DS_FMT_BF16, 2 * kRowsPerWarp, NT>::run(data, none, H, xs, H, (1u << T) - 1u, acc);
     }
 
     // reduce and apply the SwiGLU epilogue
@@ -603,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(const DecodeArgs 
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
       if (FMT == DS_FMT_FP4) {
-        RowDot<DS_FMT_FP4, kRowsPerWarp, NT>::run(data, sc, I, hslot, I, T, acc);
+        RowDot<DS_FMT_FP4, kRowsPerWarp, NT>::run(data, sc, I, hslot, I, mask, acc);
       } else {
         const __half* s16[kRowsPerWarp];
         const __half* b16[kRowsPerWarp];
@@ -613,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(const DecodeArgs 
           b16[r] = reinterpret_cast<const __half*>(bi[r]);
         }
         RowDotQ3<kRowsPerWarp, NT>::run(data, s16, b16, I, hslot, I,
-                                         xg_base + (size_t)(s - g0) * T * (I / 64), T, acc);
+                                         xg_base + (size_t)(s - g0) * T * (I / 64), mask, acc);
       }
 #pragma unroll
       for (int r = 0; r < kRowsPerWarp; ++r)
@@ -637,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(const DecodeArgs 
         data[r] = n < H ? static_cast<const uint8_t*>(a.d.shared_w2) + (size_t)n * Is * 2 : nullptr;
         none[r] = nullptr;
       }
-      RowDot<DS_FMT_BF16, kRowsPerWarp, NT>::run(data, none, Is, hsh, Is, T, shared_acc);
+      RowDot<DS_FMT_BF16, kRowsPerWarp, NT>::run(data, none, Is, hsh, Is, (1u << T) - 1u, shared_acc);
 #pragma unroll
       for (int r = 0; r < kRowsPerWarp; ++r)
 #pragma unroll

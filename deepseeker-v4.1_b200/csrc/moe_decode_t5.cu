@@ -348,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
       int g = 0;
+      const uint64_t wpol = policy_evict_first();   // weights: read once per step
       // down: issue the weight half of the first stages of this CTA's shared
       // items before waiting for the gate/up grid; their activation halves
       // (h, produced by that grid) follow after the wait
@@ -357,8 +358,8 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
           const Item it = decode_item(p, item);
           for (int j = 0; j < kStagesPerItem && pre < S; ++j, ++pre) {
             mbar_arrive_expect_tx(&full[pre], kASlot + 2 * 16 * 128);
-            tma_load_3d(ring + pre * p.stage_bytes, &p.s[it.m], 0, it.rt * 128, 2 * (it.kp * kStagesPerItem + j),
-                        &full[pre]);
+            tma_load_3d_hint(ring + pre * p.stage_bytes, &p.s[it.m], 0, it.rt * 128,
+                             2 * (it.kp * kStagesPerItem + j), &full[pre], wpol);
           }
         }
         know_routed();
@@ -381,16 +382,16 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
           if (it.shared) {
             if (g >= pre) {
               mbar_arrive_expect_tx(&full[s], kASlot + 2 * 16 * 128);
-              tma_load_3d(sa, &p.s[it.m], 0, it.rt * 128, 2 * kc, &full[s]);
+              tma_load_3d_hint(sa, &p.s[it.m], 0, it.rt * 128, 2 * kc, &full[s], wpol);
             }
             tma_load_3d(sb, &p.bs, 0, 0, 2 * kc, &full[s]);
           } else {
             mbar_arrive_expect_tx(&full[s], kASlot + 2 * p.N_r * 128 + kSfSlot);
-            tma_load_3d(sa, &p.w[it.m], 0, e * p.rows_r + it.rt * 128, 2 * kc, &full[s]);
+            tma_load_3d_hint(sa, &p.w[it.m], 0, e * p.rows_r + it.rt * 128, 2 * kc, &full[s], wpol);
             tma_load_3d(sb, &p.bq, 0, it.slot * p.bq_rows_per_slot, 2 * kc, &full[s]);
             const int KC = p.K_r / 128;
-            bulk_g2s(sf, p.sfa[it.m] + (((size_t)e * (p.rows_r / 128) + it.rt) * KC + 4 * kc) * kAtom, 4 * kAtom,
-                     &full[s]);
+            bulk_g2s_hint(sf, p.sfa[it.m] + (((size_t)e * (p.rows_r / 128) + it.rt) * KC + 4 * kc) * kAtom,
+                          4 * kAtom, &full[s], wpol);
             bulk_g2s(sf + 4 * kAtom, p.sfb + it.slot * p.sfb_slot_stride + (size_t)(4 * kc) * kAtom, 4 * kAtom,
                      &full[s]);
           }
@@ -615,53 +616,43 @@ __global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
     }
     if (lane == 0) *a.n_slots = count;
   }
-  // x pieces: one thread per (token, 32-block), all 8 token slots written
-  // (rows of tokens >= T are zero); piece rows t * kPieces + p
+  // x pieces: 8 threads per (token, 32-block), 4 consecutive elements each
+  // (the block maximum by three xor shuffles inside the aligned 8-lane
+  // group); piece rows t * kPieces + p
   const int nb = a.H / 32;
-  for (int w = tid; w < a.T * nb; w += gridDim.x * blockDim.x) {
-    const int t = w / nb, blk = w % nb;
-    float v[32];
+  for (int w = tid; w < a.T * nb * 8; w += gridDim.x * blockDim.x) {
+    const int grp = w >> 3, sub = w & 7;
+    const int t = grp / nb, blk = grp % nb;
+    float v[4];
     {
-      const uint4* src = reinterpret_cast<const uint4*>(a.x + (size_t)t * a.H + blk * 32);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 u = src[c];
-        const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int d = 0; d < 4; ++d) {
-          v[c * 8 + 2 * d] = __uint_as_float(wd[d] << 16);
-          v[c * 8 + 2 * d + 1] = __uint_as_float(wd[d] & 0xFFFF0000u);
-        }
-      }
+      const uint2 u = *reinterpret_cast<const uint2*>(a.x + (size_t)t * a.H + blk * 32 + sub * 4);
+      v[0] = __uint_as_float(u.x << 16);
+      v[1] = __uint_as_float(u.x & 0xFFFF0000u);
+      v[2] = __uint_as_float(u.y << 16);
+      v[3] = __uint_as_float(u.y & 0xFFFF0000u);
     }
     uint8_t* sf = a.sfx + (size_t)(blk / 4) * kAtom;
 #pragma unroll 1
     for (int pc = 0; pc < kPieces; ++pc) {
-      float am = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) am = fmaxf(am, fabsf(v[j]));
+      float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
       const int sc = e2m1_scale(am);
       const float inv = inv_scale_of(sc), scl = scale_of(sc);
-      uint32_t packed[4];
+      uint32_t half = 0;
 #pragma unroll
-      for (int wd = 0; wd < 4; ++wd) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int c = 0; c < 8; c += 2) {
-          const int j = wd * 8 + c;
-          const uint32_t b = tc5::f32x2_to_e2m1x2(v[j] * inv, v[j + 1] * inv);
-          float q0, q1;
-          tc5::e2m1x2_to_f32x2(b, q0, q1);
-          v[j] = fmaf(-q0, scl, v[j]);
-          v[j + 1] = fmaf(-q1, scl, v[j + 1]);
-          word |= b << (4 * c);
-        }
-        packed[wd] = word;
+      for (int c = 0; c < 4; c += 2) {
+        const uint32_t b = tc5::f32x2_to_e2m1x2(v[c] * inv, v[c + 1] * inv);
+        float q0, q1;
+        tc5::e2m1x2_to_f32x2(b, q0, q1);
+        v[c] = fmaf(-q0, scl, v[c]);
+        v[c + 1] = fmaf(-q1, scl, v[c + 1]);
+        half |= b << (4 * c);
       }
       const int row = t * kPieces + pc;
-      *reinterpret_cast<uint4*>(a.xq + (size_t)row * (a.H / 2) + blk * 16) =
-          make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      sf[atom_off(row, blk & 3)] = (uint8_t)sc;
+      *reinterpret_cast<uint16_t*>(a.xq + (size_t)row * (a.H / 2) + blk * 16 + sub * 2) = (uint16_t)half;
+      if (sub == 0) sf[atom_off(row, blk & 3)] = (uint8_t)sc;
     }
   }
 }
@@ -819,7 +810,7 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   pa.xq = xq;
   pa.sfx = sfx;
   pa.err = err;
-  cfg.gridDim = dim3(std::max(1, (T * (H / 32) + 255) / 256));
+  cfg.gridDim = dim3(std::max(1, (T * (H / 4) + 255) / 256));
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
   DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel, pa));

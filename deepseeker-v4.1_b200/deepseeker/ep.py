@@ -439,15 +439,15 @@ class PeerDecodeGraph:
     the library's own kernels, so the graph holds no collective call; every
     rank must replay its graphs in the same order."""
 
-    def __init__(self, layer: PeerDecodeLayer):
+    def __init__(self, layer: PeerDecodeLayer, x: torch.Tensor | None = None, logits: torch.Tensor | None = None):
         from . import moe
 
         self.layer = layer
         b, k, H = layer.rows, layer.top_k, layer.comm.hidden
         E = layer.layer.n_experts * layer.comm.world
         dev = layer.comm.device
-        self.x = torch.zeros(b, H, dtype=torch.bfloat16, device=dev)
-        self.logits = torch.zeros(b, E, dtype=torch.float32, device=dev)
+        self.x = moe._static_input(x, (b, H), torch.bfloat16, dev, "x")
+        self.logits = moe._static_input(logits, (b, E), torch.float32, dev, "logits")
         self.w = torch.empty(b, k, dtype=torch.float32, device=dev)
         self.ids = torch.empty(b, k, dtype=torch.int32, device=dev)
         self.out = torch.empty(b, H, dtype=torch.bfloat16, device=dev)

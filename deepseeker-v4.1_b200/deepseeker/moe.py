@@ -311,6 +311,14 @@ def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None
     return out.reshape(x.shape).to(x.dtype)
 
 
+def _static_input(t: torch.Tensor | None, shape, dtype, device, name: str) -> torch.Tensor:
+    if t is None:
+        return torch.zeros(shape, dtype=dtype, device=device)
+    if tuple(t.shape) != tuple(shape) or t.dtype != dtype or not t.is_contiguous() or t.device != device:
+        raise ValueError(f"{name} must be a contiguous {tuple(shape)} {dtype} tensor on {device}")
+    return t
+
+
 class DecodeGraph:
     """Softmax top-k routing + ``moe_decode`` for one resident layer and a fixed
     token count, captured once into a CUDA graph over static device buffers.
@@ -321,12 +329,15 @@ class DecodeGraph:
     router + decode launches and their host-side argument handling.
     """
 
-    def __init__(self, weights: MoEWeights, tokens: int, top_k: int, device: torch.device | str | None = None):
+    def __init__(self, weights: MoEWeights, tokens: int, top_k: int, device: torch.device | str | None = None,
+                 x: torch.Tensor | None = None, logits: torch.Tensor | None = None):
+        """``x`` [tokens, H] bf16 / ``logits`` [tokens, E] f32: input buffers to
+        read (e.g. rows of a ``GraphChain`` staging tensor); allocated here if None."""
         device = torch.device(device) if device is not None else weights.w1.data.device
         self.weights, self.tokens, self.top_k = weights, tokens, top_k
         H, E = weights.hidden, weights.n_experts
-        self.x = torch.zeros(tokens, H, dtype=torch.bfloat16, device=device)
-        self.logits = torch.zeros(tokens, E, dtype=torch.float32, device=device)
+        self.x = _static_input(x, (tokens, H), torch.bfloat16, device, "x")
+        self.logits = _static_input(logits, (tokens, E), torch.float32, device, "logits")
         self.w = torch.empty(tokens, top_k, dtype=torch.float32, device=device)
         self.ids = torch.empty(tokens, top_k, dtype=torch.int32, device=device)
         self.out = torch.empty(tokens, H, dtype=torch.bfloat16, device=device)
@@ -349,27 +360,38 @@ class DecodeGraph:
 class GraphChain:
     """Several captured layers (``DecodeGraph`` or ``ep.PeerDecodeGraph``:
     objects with static ``x``, ``logits``, ``out`` buffers and ``_step()``)
-    captured back to back into ONE CUDA graph, their inputs staged from two
-    stacked buffers: a decode step through many layers is one graph launch,
-    the way a serving loop runs its layer stack.
+    captured back to back into ONE CUDA graph: a decode step through many
+    layers is one graph launch, the way a serving loop runs its layer stack.
 
-    ``x [n, T, H]`` and ``logits [n, T, E]`` hold layer i's inputs at [i];
-    ``replay()`` runs all n layers (layer i's output in ``layers[i].out``)."""
+    ``x [n, T, H]`` and ``logits [n, T, E]`` hold layer i's inputs at [i].
+    Pass the stacked tensors whose rows the layers were built on (their
+    ``x=`` / ``logits=`` arguments) and the graph reads them in place;
+    without them the chain allocates its own and copies row i into layer i's
+    buffers inside the graph.  ``replay()`` runs all n layers (layer i's
+    output in ``layers[i].out``)."""
 
-    def __init__(self, layers):
+    def __init__(self, layers, x: torch.Tensor | None = None, logits: torch.Tensor | None = None):
         if not layers:
             raise ValueError("GraphChain needs at least one layer")
         self.layers = list(layers)
         n = len(self.layers)
         x0, l0 = self.layers[0].x, self.layers[0].logits
-        self.x = torch.zeros((n,) + tuple(x0.shape), dtype=x0.dtype, device=x0.device)
-        self.logits = torch.zeros((n,) + tuple(l0.shape), dtype=l0.dtype, device=l0.device)
+        in_place = x is not None and logits is not None
+        if in_place:
+            for i, layer in enumerate(self.layers):
+                if layer.x.data_ptr() != x[i].data_ptr() or layer.logits.data_ptr() != logits[i].data_ptr():
+                    raise ValueError(f"layer {i} does not read rows {i} of the given x / logits")
+            self.x, self.logits = x, logits
+        else:
+            self.x = torch.zeros((n,) + tuple(x0.shape), dtype=x0.dtype, device=x0.device)
+            self.logits = torch.zeros((n,) + tuple(l0.shape), dtype=l0.dtype, device=l0.device)
         torch.cuda.synchronize(x0.device)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             for i, layer in enumerate(self.layers):
-                layer.x.copy_(self.x[i])
-                layer.logits.copy_(self.logits[i])
+                if not in_place:
+                    layer.x.copy_(self.x[i])
+                    layer.logits.copy_(self.logits[i])
                 layer._step()
 
     def replay(self) -> None:
