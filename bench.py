@@ -634,7 +634,9 @@ def run_decode(args) -> dict:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     fmt = "q3" if args.config == "c3" else "fp4"
-    tokens = 1
+    tokens = args.batch
+    if not 1 <= tokens <= 8:
+        raise SystemExit("--batch must be 1..8 for the decode configs")
     L = args.layers
     layers = [synthetic.make_layer(fmt, H, I, E, seed=1000 * (rank + 1) + l, shared_inter=IS, std=0.02,
                                    device=dev) for l in range(L)]
@@ -785,7 +787,11 @@ def run_decode(args) -> dict:
     # per-step algorithmic bytes: distinct experts x expert bytes + shared + x/out/route traffic
     per_expert = sum(b.nbytes() // E for b in (layers[0].w1, layers[0].w3, layers[0].w2))
     shared_b = 3 * IS * H * 2
-    step_bytes = K_TOP * per_expert + shared_b + tokens * H * 2 * 2
+    # distinct experts of each timed step's routing (8 for B = 1)
+    timed_idx = [(i_start + s_) % n_in for s_ in range(args.steps)]
+    ids_t = torch.stack([moe.route_softmax_topk(logits[j], K_TOP)[1] for j in timed_idx]).cpu()
+    distinct = statistics.mean(len(set(r.flatten().tolist())) for r in ids_t)
+    step_bytes = int(round(distinct * per_expert)) + shared_b + tokens * H * 2 * 2
 
     ms_t = torch.tensor([ms, e2e_ms, statistics.mean(decode_ms)], device=dev)
     if dist is not None:
@@ -795,7 +801,7 @@ def run_decode(args) -> dict:
     if rank == 0:
         pk, kind = peaks()
         achieved = step_bytes / (dec_ms * 1e-3) / 1e9
-        traffic = ncu_traffic(f"decode_{fmt}_c2")
+        traffic = ncu_traffic(f"decode_{fmt}_c2") if tokens == 1 else None
         result = {
             "metric": METRIC,
             "value": round(world * tokens * args.steps / (ms * 1e-3), 2),
@@ -810,9 +816,11 @@ def run_decode(args) -> dict:
             "dtype": "fp4-e2m1 weights, bf16 activations, f32 accumulate" if fmt == "fp4"
                      else "q3-affine weights, bf16 activations, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights quantised on device; router logits N(0,1))",
-            "config": {"workload": f"BASELINE config {'2' if fmt == 'fp4' else '3'}: one MoE layer decode B=1, "
+            "config": {"workload": f"BASELINE config {'2' if fmt == 'fp4' else '3'}: one MoE layer decode "
+                                   f"B={tokens}, "
                                    "hidden 4096, 256 experts inter 2048 top-8 softmax, bf16 shared expert",
                        "format": fmt, "tokens_per_step": tokens, "layers_rotated": L,
+                       "distinct_experts_per_step": round(distinct, 3),
                        "l2": f"rotating {L} resident layers (>{L * 3.4:.0f} GB), each step streams its "
                              f"{step_bytes / 1e6:.1f} MB cold",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},

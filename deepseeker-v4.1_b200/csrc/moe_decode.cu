@@ -33,70 +33,14 @@ namespace {
 using ds::decode::DecodeArgs;
 using ds::decode::kMaxEntries;
 using ds::decode::kMaxTokens;
+using ds::decode::Slots;
+using ds::decode::build_slots;
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRowsPerWarp = 2;
 constexpr int kRowsPerItem = kWarps * kRowsPerWarp;  // 16
 constexpr int kSmemBudget = 200 * 1024;              // dynamic smem cap per CTA
-
-struct Slots {
-  int count;
-  int expert[kMaxEntries];
-  uint32_t mask[kMaxEntries];                 // bit t: token t routed here
-  float gate[kMaxEntries][kMaxTokens];
-  int ids[kMaxEntries];
-  int first[kMaxEntries];
-};
-
-// Distinct routed experts in ascending id, with each token's gate taken from
-// its first slot holding that expert (src/deepseeker/mlx_forward.py:394-404).
-__device__ void build_slots(const DecodeArgs& a, Slots& s) {
-  const int tid = threadIdx.x;
-  const int k = a.d.top_k;
-  const int n = a.tokens * k;
-  if (tid < kMaxEntries) {
-    s.mask[tid] = 0u;
-#pragma unroll
-    for (int t = 0; t < kMaxTokens; ++t) s.gate[tid][t] = 0.0f;
-  }
-  if (tid == 0) s.count = 0;
-  if (tid < n) {
-    int id = a.ids[tid];
-    if (id >= a.d.n_experts) {
-      atomicOr(a.err, 1);
-      id = -1;
-    }
-    s.ids[tid] = id < 0 ? -1 : id;
-  }
-  __syncthreads();
-  if (tid < n) {
-    const int id = s.ids[tid];
-    int first = id >= 0;
-    for (int j = 0; j < tid && first; ++j) first = (s.ids[j] != id);
-    s.first[tid] = first;
-  }
-  __syncthreads();
-  if (tid < n) {
-    const int id = s.ids[tid];
-    if (id >= 0) {
-      int rank = 0;
-      for (int j = 0; j < n; ++j) rank += (s.first[j] && s.ids[j] < id);
-      if (s.first[tid]) {
-        s.expert[rank] = id;
-        atomicAdd(&s.count, 1);
-      }
-      const int t = tid / k;
-      int first_in_row = 1;
-      for (int j = t * k; j < tid; ++j) first_in_row &= (s.ids[j] != id);
-      if (first_in_row) {
-        s.gate[rank][t] = a.gates[tid];
-        atomicOr(&s.mask[rank], 1u << t);
-      }
-    }
-  }
-  __syncthreads();
-}
 
 // ---------------------------------------------------------------- staging
 
@@ -788,6 +732,7 @@ extern "C" int ds_moe_decode_workspace_size(const DsMoeDesc* desc, int64_t token
   if (desc->w1.format == DS_FMT_FP4 && desc->w1.scales_tc && desc->w3.scales_tc && desc->w2.scales_tc &&
       tokens <= ds::decode::kMaxTokens)
     total = std::max(total, ds::decode::t5_workspace_bytes(*desc, (int)tokens));
+  if (desc->w1.format == DS_FMT_Q3) total = std::max(total, ds::decode::q3_workspace_bytes(*desc, (int)tokens));
   *bytes = total;
   return DS_OK;
 }
@@ -833,8 +778,13 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
   if (!force_generic && !no_t5 && ds::decode::t5_supported(a) &&
       workspace_bytes >= ds::decode::t5_workspace_bytes(*desc, (int)tokens))
     return ds::decode::launch_t5(a, workspace, workspace_bytes, s);
+  // Q3 banks with bf16 x take the streaming CUDA-core kernels
+  // (moe_decode_q3.cu); DEEPSEEKER_DECODE_GENERIC=1 keeps the generic ones.
+  if (!force_generic && ds::decode::q3_supported(a) &&
+      workspace_bytes >= ds::decode::q3_workspace_bytes(*desc, (int)tokens))
+    return ds::decode::launch_q3(a, workspace, workspace_bytes, s);
   DS_REQUIRE(!desc->out_f32 || x_dtype == DS_F32, DS_ENOTSUP,
-             "moe_decode: out_f32 with bf16 x needs FP4 banks with scale atoms (tensor-core kernels)");
+             "moe_decode: out_f32 with bf16 x needs FP4 banks with scale atoms or Q3 banks");
   if (!force_generic && ds::decode::tc_supported(a)) return ds::decode::launch_tc(a, s);
   return desc->w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
 }

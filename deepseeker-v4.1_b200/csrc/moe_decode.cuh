@@ -37,6 +37,67 @@ struct DecodeArgs {
   float* out_sh = nullptr;
 };
 
+// Routed slots of a decode call, built per CTA in shared memory (blockDim >=
+// tokens * top_k threads; ends with __syncthreads).
+struct Slots {
+  int count;
+  int expert[kMaxEntries];
+  uint32_t mask[kMaxEntries];                 // bit t: token t routed here
+  float gate[kMaxEntries][kMaxTokens];
+  int ids[kMaxEntries];
+  int first[kMaxEntries];
+};
+
+// Distinct routed experts in ascending id, with each token's gate taken from
+// its first slot holding that expert (src/deepseeker/mlx_forward.py:394-404).
+__device__ inline void build_slots(const DecodeArgs& a, Slots& s) {
+  const int tid = threadIdx.x;
+  const int k = a.d.top_k;
+  const int n = a.tokens * k;
+  if (tid < kMaxEntries) {
+    s.mask[tid] = 0u;
+#pragma unroll
+    for (int t = 0; t < kMaxTokens; ++t) s.gate[tid][t] = 0.0f;
+  }
+  if (tid == 0) s.count = 0;
+  if (tid < n) {
+    int id = a.ids[tid];
+    if (id >= a.d.n_experts) {
+      atomicOr(a.err, 1);
+      id = -1;
+    }
+    s.ids[tid] = id < 0 ? -1 : id;
+  }
+  __syncthreads();
+  if (tid < n) {
+    const int id = s.ids[tid];
+    int first = id >= 0;
+    for (int j = 0; j < tid && first; ++j) first = (s.ids[j] != id);
+    s.first[tid] = first;
+  }
+  __syncthreads();
+  if (tid < n) {
+    const int id = s.ids[tid];
+    if (id >= 0) {
+      int rank = 0;
+      for (int j = 0; j < n; ++j) rank += (s.first[j] && s.ids[j] < id);
+      if (s.first[tid]) {
+        s.expert[rank] = id;
+        atomicAdd(&s.count, 1);
+      }
+      const int t = tid / k;
+      int first_in_row = 1;
+      for (int j = t * k; j < tid; ++j) first_in_row &= (s.ids[j] != id);
+      if (first_in_row) {
+        s.gate[rank][t] = a.gates[tid];
+        atomicOr(&s.mask[rank], 1u << t);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+
 // Single-token tensor-core pipeline (moe_decode_tc.cu).  Returns true and
 // launches when the geometry is supported; false means "use the generic path".
 bool tc_supported(const DecodeArgs& a);
@@ -50,6 +111,12 @@ int launch_tc_uncached(const DecodeArgs& a, cudaStream_t st);
 bool t5_supported(const DecodeArgs& a);
 size_t t5_workspace_bytes(const DsMoeDesc& d, int tokens);
 int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t st);
+
+// CUDA-core pipeline for q3 routed banks, 1..8 tokens, bf16 x
+// (moe_decode_q3.cu).  Needs its own workspace size.
+bool q3_supported(const DecodeArgs& a);
+size_t q3_workspace_bytes(const DsMoeDesc& d, int tokens);
+int launch_q3(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t st);
 
 }  // namespace decode
 }  // namespace ds
