@@ -1,29 +1,30 @@
 // Decode MoE layer for 3-bit affine (q3) routed experts + the bf16 shared
-// expert, 1..8 tokens, bf16 x, on CUDA cores.
+// expert, 1..8 tokens, bf16 x, on CUDA cores with integer dot products.
 //
-// Every weight byte is read once per call and the dot products run at the
-// rate the bytes arrive:
-//   * a CTA owns 64 output rows of one matrix pair at a time (8 per warp,
+// Every weight byte is read once per call:
+//   * a CTA owns 64 output rows of one matrix (pair) at a time (8 per warp,
 //     4 lanes per row); lane j of a row takes the 128-element segments
 //     j, j+4, j+8, ... of the row (48 bytes of codes = three 16-byte loads,
-//     plus one f16x2 of scales and of biases), so a warp's loads cover whole
-//     rows and the four lanes of a row read different 512-byte stretches of
-//     the staged activations (padded by 16 bytes per 128 values: no bank
-//     conflicts);
-//   * two codes come out of the planar q3 layout per shift-and-mask into the
-//     two halves of an f16x2 whose bits are those of 1024 + q; one f16x2
-//     subtraction of 1024 leaves q exactly, widened to f32;
-//   * the group term is s * sum(q x) + b * sum(x) (sums over the 64 values of
-//     the group, the activation sums computed once per call);
+//     plus one f16x2 of scales and one of biases);
+//   * activations enter as int8 pieces per 64-value group: v ~ sx * (hi +
+//     lo / 256), sx = max|v| / 127, hi = rint(v / sx), lo = rint(256 (v - sx
+//     hi) / sx), i.e. about 15 significant bits, plus the group sum X of v;
+//   * the planar q3 layout yields two codes per shift-and-mask in the two
+//     16-bit halves of a register, which multiply two int8 pieces in one
+//     dp2a (int16 x int8 pairs into an int32); a group contributes
+//     s * sx * (Dhi + Dlo / 256) + b * X to its row;
 //   * gate/up writes h (SwiGLU clamps, route weight before the down
-//     projection) per (slot, token, row); down sums two slots per work item
-//     into f32 partials; the combine kernel adds the partials in slot order
-//     and the shared expert's output rounded to bf16 (the reference's order).
-// Three kernels chained with programmatic dependent launch.  The reference
-// computes the same layer with MLX's quantized_matmul over dequantised
-// groups (src/deepseeker/mlx_forward.py:93-101, 257-419); the group math
-// w = f32(scale) q + f32(bias) is regrouped here, which changes float
-// rounding only.
+//     projection) straight into pieces: the 64 rows of a work item are one
+//     64-value group of the down projection's input;
+//   * down sums two slots per work item into f32 partials; the combine
+//     kernel adds the partials in slot order and the shared expert's output
+//     rounded to bf16 (the reference's order).
+// The shared expert (bf16) runs on f32 FMAs in the same kernels.  Three
+// kernels chained with programmatic dependent launch.  The reference
+// computes the layer with MLX's quantized_matmul over dequantised groups
+// (src/deepseeker/mlx_forward.py:93-101, 257-419): w = f32(scale) q +
+// f32(bias); the group math is regrouped here and the activations carry
+// ~15 bits, which changes the result at the 1e-5 level.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -41,17 +42,23 @@ namespace decode {
 namespace {
 
 constexpr int kQT = 256;           // threads per CTA
-constexpr int kRowsCta = 64;       // output rows per work item (8 warps x 8 rows)
+constexpr int kRowsCta = 64;       // output rows per work item = one q3 group of the next projection
 constexpr int kChunk = 2;          // routed slots per down work item
+constexpr int kPk = 32;            // words of one (token, group) piece block: 16 hi + 16 lo
+constexpr int kPkPad = 36;         // its stride in shared memory (16 bytes of padding: no bank conflicts)
+constexpr int kShGU = 4;           // K quarters of a shared-expert gate/up item (partial g and u sums)
+constexpr int kShDn = 2;           // K halves of a shared-expert down item (partial outputs)
 
 __host__ __device__ constexpr int padded(int K) { return K + (K >> 7) * 4; }
 __device__ __forceinline__ int pidx(int k) { return k + ((k >> 7) << 2); }
 
 struct Q3Args {
   DecodeArgs a;
-  float* h;          // [max_slots + 1][T][h_stride] (row max_slots: shared expert)
-  float* part;       // [max_chunks + 1][T][H] (chunk max_chunks: shared expert)
-  int h_stride, max_chunks;
+  uint32_t* hpk;     // routed h pieces [max_slots][T][I / 64][kPk]
+  float2* hsx;       // routed h (sx, X) [max_slots][T][I / 64]
+  float* hsh;        // shared gate/up partial sums [kShGU][T][2][Is] f32 (g, u)
+  float* part;       // [max_chunks + kShDn][T][H] (chunks max_chunks..: shared expert halves)
+  int max_chunks;
 };
 
 __device__ __forceinline__ float silu_glu_q3(float g, float u, float limit) {
@@ -62,71 +69,104 @@ __device__ __forceinline__ float silu_glu_q3(float g, float u, float limit) {
   return (g / (1.0f + expf(-g))) * u;
 }
 
-// q (exact, as f32) for the 16 codes of low word wi of a group: out[j] = element
-// 16 wi + j, out[8 + j] = element 16 wi + 8 + j (planar layout of
-// oracle/q3.py).  hw = high word 4 + wi / 2, v8 = 8 (wi & 1); bits v8 + j
-// and 16 + v8 + j of hw move to bits 2 and 18 (a right or left shift by a
-// compile-time amount once unrolled).
-__device__ __forceinline__ void codes16(uint32_t lo, uint32_t hw, int v8, float (&out)[16]) {
+// Codes of elements 16 wi + j (low half) and 16 wi + 8 + j (high half) of a
+// group in the planar layout of oracle/q3.py: low word wi bits 2j / 16+2j,
+// high word hw = word 4 + wi / 2 bits v8 + j / 16 + v8 + j (v8 = 8 (wi & 1)),
+// the high bit moved to bit 2 by a compile-time shift once unrolled.
+__device__ __forceinline__ uint32_t codes2(uint32_t lo, uint32_t hw, int v8, int j) {
+  const int sh = v8 + j - 2;
+  const uint32_t hb = (sh >= 0 ? (hw >> sh) : (hw << -sh)) & 0x00040004u;
+  return ((lo >> (2 * j)) & 0x00030003u) | hb;
+}
+
+// Piece block of 16 values (one wi of a group): word p (p = 0..3) holds the
+// int8 pieces of elements [16wi + 2p, 16wi + 8 + 2p, 16wi + 2p + 1,
+// 16wi + 8 + 2p + 1], the operand order of dp2a.lo / dp2a.hi against the
+// code pairs of j = 2p and j = 2p + 1.
+__device__ __forceinline__ void make_pieces16(const float (&v)[16], float amax, uint32_t (&hi)[4], uint32_t (&lo)[4],
+                                              float& sx) {
+  sx = amax / 127.0f;
+  const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+  int qh[16], ql[16];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int sh = v8 + j - 2;
-    const uint32_t hb = sh >= 0 ? (hw >> sh) : (hw << -sh);
-    const uint32_t bits = ((lo >> (2 * j)) & 0x00030003u) | (hb & 0x00040004u) | 0x64006400u;
-    const float2 f = __half22float2(__hsub2(*reinterpret_cast<const __half2*>(&bits), __float2half2_rn(1024.0f)));
-    out[j] = f.x;
-    out[8 + j] = f.y;
+  for (int i = 0; i < 16; ++i) {
+    const int h = __float2int_rn(v[i] * inv);
+    const float r = fmaf(-(float)h, sx, v[i]);
+    const int l = __float2int_rn(r * (256.0f * inv));
+    qh[i] = h;
+    ql[i] = max(-127, min(127, l));
+  }
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int e0 = 2 * p, e1 = 8 + 2 * p, e2 = 2 * p + 1, e3 = 8 + 2 * p + 1;
+    hi[p] = (uint32_t)(qh[e0] & 0xFF) | ((uint32_t)(qh[e1] & 0xFF) << 8) | ((uint32_t)(qh[e2] & 0xFF) << 16) |
+            ((uint32_t)(qh[e3] & 0xFF) << 24);
+    lo[p] = (uint32_t)(ql[e0] & 0xFF) | ((uint32_t)(ql[e1] & 0xFF) << 8) | ((uint32_t)(ql[e2] & 0xFF) << 16) |
+            ((uint32_t)(ql[e3] & 0xFF) << 24);
   }
 }
 
-// Group of 64: S1[t] += sum q1 x_t, S3[t] += sum q3 x_t for
-// the tokens in mask; xg = group start in token 0's padded row.
-template <int NT>
-__device__ __forceinline__ void group_pair(const uint32_t (&w1)[6], const uint32_t (&w3)[6], const float* xg,
-                                           int xstride, uint32_t mask, float (&S1)[NT], float (&S3)[NT]) {
+// Pieces of T rows of K bf16 values (row stride src_stride) into blocks
+// dst[t][g] (stride kPkPad words) and (sx, X) into sxx[t][g].  A quad of
+// threads builds one group (one wi each); the loop bound is a multiple of
+// 32, so whole warps take part in the quad shuffles.
+__device__ void pieces_rows_bf16(const __nv_bfloat16* src, int T, int K, int src_stride, uint32_t* dst, float2* sxx) {
+  const int G = K / 64, n = T * G * 4;
+  for (int i = threadIdx.x; i < (n + 31) / 32 * 32; i += blockDim.x) {
+    const bool live = i < n;
+    const int wi = i & 3, tg = live ? (i >> 2) : 0, t = tg / G, g = tg % G;
+    float v[16];
+    const uint4* p = reinterpret_cast<const uint4*>(src + (size_t)t * src_stride + 64 * g + 16 * wi);
+    const uint4 a = p[0], b = p[1];
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-  for (int wi = 0; wi < 4; ++wi) {
-    float f1[16], f3[16];
-    codes16(w1[wi], w1[4 + (wi >> 1)], (wi & 1) * 8, f1);
-    codes16(w3[wi], w3[4 + (wi >> 1)], (wi & 1) * 8, f3);
+    for (int k = 0; k < 8; ++k) {
+      v[2 * k] = __uint_as_float(w[k] << 16);
+      v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+    }
+    float am = 0.0f, sum = 0.0f;
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      if (!((mask >> t) & 1u)) continue;
-      const float4* xv = reinterpret_cast<const float4*>(xg + t * xstride) + 4 * wi;
-      const float4 a = xv[0], b = xv[1], c = xv[2], d = xv[3];
-      const float x[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
-      float s1 = S1[t], s3 = S3[t];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        s1 = fmaf(f1[j], x[j], s1);
-        s3 = fmaf(f3[j], x[j], s3);
-      }
-      S1[t] = s1;
-      S3[t] = s3;
+    for (int k = 0; k < 16; ++k) {
+      am = fmaxf(am, fabsf(v[k]));
+      sum += v[k];
+    }
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    uint32_t hi[4], lo[4];
+    float sx;
+    make_pieces16(v, am, hi, lo, sx);
+    if (live) {
+      uint32_t* d = dst + (size_t)tg * kPkPad;
+      *reinterpret_cast<uint4*>(d + 4 * wi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(d + 16 + 4 * wi) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      if (wi == 0) sxx[tg] = make_float2(sx, sum);
     }
   }
 }
 
-// Group of 64: D[t] += sum q h_t (down projection).
-template <int NT>
-__device__ __forceinline__ void group_one(const uint32_t (&w)[6], const float* hg, int hstride, uint32_t mask,
-                                          float (&D)[NT]) {
+// One group of 64 codes against the pieces block pk (hi words 0..15, lo
+// 16..31): returns Dhi + Dlo / 256 (exact integers, then one f32 step).
+__device__ __forceinline__ float group_dot(const uint32_t (&w)[6], const uint32_t* pk) {
+  int dh = 0, dl = 0;
 #pragma unroll
   for (int wi = 0; wi < 4; ++wi) {
-    float f[16];
-    codes16(w[wi], w[4 + (wi >> 1)], (wi & 1) * 8, f);
+    const uint4 h = *reinterpret_cast<const uint4*>(pk + 4 * wi);
+    const uint4 l = *reinterpret_cast<const uint4*>(pk + 16 + 4 * wi);
+    const uint32_t hv[4] = {h.x, h.y, h.z, h.w}, lv[4] = {l.x, l.y, l.z, l.w};
+    const uint32_t lw = w[wi], hw = w[4 + (wi >> 1)];
+    const int v8 = (wi & 1) * 8;
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      if (!((mask >> t) & 1u)) continue;
-      const float4* hv = reinterpret_cast<const float4*>(hg + t * hstride) + 4 * wi;
-      const float4 a = hv[0], b = hv[1], c = hv[2], d = hv[3];
-      const float x[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
-      float s = D[t];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) s = fmaf(f[j], x[j], s);
-      D[t] = s;
+    for (int p = 0; p < 4; ++p) {
+      const int c0 = (int)codes2(lw, hw, v8, 2 * p), c1 = (int)codes2(lw, hw, v8, 2 * p + 1);
+      dh = __dp2a_lo(c0, (int)hv[p], dh);
+      dh = __dp2a_hi(c1, (int)hv[p], dh);
+      dl = __dp2a_lo(c0, (int)lv[p], dl);
+      dl = __dp2a_hi(c1, (int)lv[p], dl);
     }
   }
+  return (float)dh + (float)dl * (1.0f / 256.0f);
 }
 
 __device__ __forceinline__ void words_of(const uint4& u0, const uint4& u1, const uint4& u2, uint32_t (&g0)[6],
@@ -142,23 +182,22 @@ __device__ __forceinline__ float quad_sum(float v) {
   return v;
 }
 
-// T rows of K f32 values -> padded smem rows + group sums (64 per group).
-__device__ void stage_rows(const float* src, int T, int K, int src_stride, float* dst, float* gsum) {
-  const int Kp = padded(K);
-  for (int i = threadIdx.x; i < T * (K / 4); i += blockDim.x) {
-    const int t = i / (K / 4), k = (i % (K / 4)) * 4;
-    *reinterpret_cast<float4*>(dst + t * Kp + pidx(k)) =
-        *reinterpret_cast<const float4*>(src + (size_t)t * src_stride + k);
-  }
-  __syncthreads();
-  if (gsum != nullptr)
-    for (int i = threadIdx.x; i < T * (K / 64); i += blockDim.x) {
-      const int t = i / (K / 64), g = i % (K / 64);
-      const float* p = dst + t * Kp + pidx(64 * g);
-      float s = 0.0f;
-      for (int k = 0; k < 64; ++k) s += p[k];
-      gsum[i] = s;
+// bf16 row segment (32 values = four 16-byte words) dot f32 values xs[0..31]
+__device__ __forceinline__ float bf16_dot32(const uint4 (&v)[4], const float* xs) {
+  float s = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 xa = *reinterpret_cast<const float4*>(xs + 8 * c);
+    const float4 xb = *reinterpret_cast<const float4*>(xs + 8 * c + 4);
+    const uint32_t aw[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+    const float xx[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      s = fmaf(__uint_as_float(aw[k] << 16), xx[2 * k], s);
+      s = fmaf(__uint_as_float(aw[k] & 0xFFFF0000u), xx[2 * k + 1], s);
     }
+  }
+  return s;
 }
 
 // ------------------------------------------------------------------ gate/up
@@ -170,16 +209,21 @@ __global__ void __launch_bounds__(kQT, 2) q3_gate_up_kernel(const Q3Args q) {
   const DecodeArgs& a = q.a;
   extern __shared__ float4 smem4[];
   __shared__ Slots slots;
-  const int H = a.d.hidden, I = a.d.inter, T = a.tokens, Hp = padded(H);
-  float* xs = reinterpret_cast<float*>(smem4);   // [T][Hp]
-  float* xsum = xs + T * Hp;                     // [T][H / 64]
-  {
-    // bf16 x -> padded f32 rows
+  __shared__ float hrow[8][kRowsCta];            // h of the item's 64 rows per token
+  const int H = a.d.hidden, I = a.d.inter, T = a.tokens, G = H / 64;
+  const bool has_shared = a.d.shared_w1 != nullptr;
+  const int Is = has_shared ? a.d.shared_inter : 0;
+  uint32_t* xpk = reinterpret_cast<uint32_t*>(smem4);                     // [T][G][kPkPad]
+  float2* xsx = reinterpret_cast<float2*>(xpk + (size_t)T * G * kPkPad);  // [T][G]
+  float* xsf = reinterpret_cast<float*>(xsx + T * G);                     // [T][padded(H)] (shared expert)
+  const int Hp = padded(H);
+  pieces_rows_bf16(static_cast<const __nv_bfloat16*>(a.x), T, H, H, xpk, xsx);
+  if (has_shared) {
     const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(a.x);
     for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
       const int t = i / (H / 8), k = (i % (H / 8)) * 8;
       const uint4 u = *reinterpret_cast<const uint4*>(x + (size_t)t * H + k);
-      float* d = xs + t * Hp + pidx(k);
+      float* d = xsf + t * Hp + pidx(k);
       *reinterpret_cast<float4*>(d) = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
                                                   __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
       *reinterpret_cast<float4*>(d + 4) = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xFFFF0000u),
@@ -187,42 +231,34 @@ __global__ void __launch_bounds__(kQT, 2) q3_gate_up_kernel(const Q3Args q) {
     }
   }
   build_slots(a, slots);                         // ends with __syncthreads
-  for (int i = threadIdx.x; i < T * (H / 64); i += blockDim.x) {
-    const int t = i / (H / 64), g = i % (H / 64);
-    const float* p = xs + t * Hp + pidx(64 * g);
-    float s = 0.0f;
-    for (int k = 0; k < 64; ++k) s += p[k];
-    xsum[i] = s;
-  }
-  __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 3;
+  const int r_in = warp * 8 + (lane >> 2);       // row within the item
   const int D = slots.count;
-  const bool has_shared = a.d.shared_w1 != nullptr;
-  const int Is = has_shared ? a.d.shared_inter : 0;
   const int rb_r = I / kRowsCta, rb_s = Is / kRowsCta;
-  const int items = D * rb_r + rb_s;
-  const uint32_t all = (1u << T) - 1u;
+  // shared-expert items cover a quarter of K each, so that they weigh about
+  // what a routed item weighs (bf16 rows are 5.3x the bytes of q3 rows)
+  const int items = D * rb_r + rb_s * kShGU;
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
     const bool routed = item < D * rb_r;
     float acc1[NT], acc3[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc1[t] = acc3[t] = 0.0f;
-    int slot, row;
+    int slot, rb;
     uint32_t mask;
     if (routed) {
       slot = item / rb_r;
-      row = (item % rb_r) * kRowsCta + warp * 8 + (lane >> 2);
+      rb = item % rb_r;
       mask = slots.mask[slot];
       const int e = slots.expert[slot];
       const size_t rbytes = (size_t)H * 3 / 8;
-      const size_t r = (size_t)e * I + row;
+      const size_t r = (size_t)e * I + rb * kRowsCta + r_in;
       const uint8_t* w1 = static_cast<const uint8_t*>(a.d.w1.data) + r * rbytes;
       const uint8_t* w3 = static_cast<const uint8_t*>(a.d.w3.data) + r * rbytes;
-      const __half2* s1 = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w1.scales) + r * (H / 64));
-      const __half2* b1 = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w1.biases) + r * (H / 64));
-      const __half2* s3 = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w3.scales) + r * (H / 64));
-      const __half2* b3 = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w3.biases) + r * (H / 64));
+      const __half2* s1 = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w1.scales) + r * G);
+      const __half2* b1 = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w1.biases) + r * G);
+      const __half2* s3 = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w3.scales) + r * G);
+      const __half2* b3 = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w3.biases) + r * G);
       for (int seg = j; seg < H / 128; seg += 4) {
         const uint4* p1 = reinterpret_cast<const uint4*>(w1 + (size_t)seg * 48);
         const uint4* p3 = reinterpret_cast<const uint4*>(w3 + (size_t)seg * 48);
@@ -234,33 +270,34 @@ __global__ void __launch_bounds__(kQT, 2) q3_gate_up_kernel(const Q3Args q) {
         words_of(u10, u11, u12, g10, g11);
         words_of(u30, u31, u32, g30, g31);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int g = 2 * seg + h;
-          float S1[NT], S3[NT];
-#pragma unroll
-          for (int t = 0; t < NT; ++t) S1[t] = S3[t] = 0.0f;
-          group_pair<NT>(h ? g11 : g10, h ? g31 : g30, xs + pidx(64 * g), Hp, mask, S1, S3);
-          const float sa = h ? sc1.y : sc1.x, ba = h ? bi1.y : bi1.x;
-          const float sb = h ? sc3.y : sc3.x, bb = h ? bi3.y : bi3.x;
+        for (int hh = 0; hh < 2; ++hh) {
+          const int g = 2 * seg + hh;
+          const float sa = hh ? sc1.y : sc1.x, ba = hh ? bi1.y : bi1.x;
+          const float sb = hh ? sc3.y : sc3.x, bb = hh ? bi3.y : bi3.x;
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
             if (!((mask >> t) & 1u)) continue;
-            const float X = xsum[t * (H / 64) + g];
-            acc1[t] = fmaf(sa, S1[t], fmaf(ba, X, acc1[t]));
-            acc3[t] = fmaf(sb, S3[t], fmaf(bb, X, acc3[t]));
+            const uint32_t* pk = xpk + ((size_t)t * G + g) * kPkPad;
+            const float2 sxx = xsx[t * G + g];
+            const float d1 = group_dot(hh ? g11 : g10, pk), d3 = group_dot(hh ? g31 : g30, pk);
+            acc1[t] = fmaf(sa * sxx.x, d1, fmaf(ba, sxx.y, acc1[t]));
+            acc3[t] = fmaf(sb * sxx.x, d3, fmaf(bb, sxx.y, acc3[t]));
           }
         }
       }
     } else {
-      // shared expert (bf16 rows of H), all tokens
-      slot = a.max_slots;
-      row = (item - D * rb_r) * kRowsCta + warp * 8 + (lane >> 2);
-      mask = all;
+      // shared expert (bf16 rows of H), all tokens, f32 FMAs, K quarter kq
+      slot = -1;
+      rb = (item - D * rb_r) / kShGU;
+      const int kq = (item - D * rb_r) % kShGU;
+      mask = (1u << T) - 1u;
+      const int row = rb * kRowsCta + r_in;
       const uint4* w1 = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.d.shared_w1) +
                                                        (size_t)row * H);
       const uint4* w3 = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.d.shared_w3) +
                                                        (size_t)row * H);
-      for (int seg = j; seg < H / 32; seg += 4) {       // 32 values = four 16-byte loads per matrix
+      const int nseg = H / 32 / kShGU;
+      for (int seg = kq * nseg + j; seg < (kq + 1) * nseg; seg += 4) {
         uint4 v1[4], v3[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -270,24 +307,9 @@ __global__ void __launch_bounds__(kQT, 2) q3_gate_up_kernel(const Q3Args q) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           if (t >= T) continue;
-          const float4* xv = reinterpret_cast<const float4*>(xs + t * Hp + pidx(32 * seg));
-          float s1 = acc1[t], s3 = acc3[t];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float4 xa = xv[2 * c], xb = xv[2 * c + 1];
-            const uint32_t a1[4] = {v1[c].x, v1[c].y, v1[c].z, v1[c].w};
-            const uint32_t a3[4] = {v3[c].x, v3[c].y, v3[c].z, v3[c].w};
-            const float xx[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              s1 = fmaf(__uint_as_float(a1[k] << 16), xx[2 * k], s1);
-              s1 = fmaf(__uint_as_float(a1[k] & 0xFFFF0000u), xx[2 * k + 1], s1);
-              s3 = fmaf(__uint_as_float(a3[k] << 16), xx[2 * k], s3);
-              s3 = fmaf(__uint_as_float(a3[k] & 0xFFFF0000u), xx[2 * k + 1], s3);
-            }
-          }
-          acc1[t] = s1;
-          acc3[t] = s3;
+          const float* xs = xsf + t * Hp + pidx(32 * seg);
+          acc1[t] += bf16_dot32(v1, xs);
+          acc3[t] += bf16_dot32(v3, xs);
         }
       }
     }
@@ -296,18 +318,66 @@ __global__ void __launch_bounds__(kQT, 2) q3_gate_up_kernel(const Q3Args q) {
       acc1[t] = quad_sum(acc1[t]);
       acc3[t] = quad_sum(acc3[t]);
     }
+    if (!routed) {
+      // partial g and u of K quarter kq; the down kernel sums the quarters
+      // in order and applies the SwiGLU when it stages h
+      if (j == 0) {
+        const int kq = (item - D * rb_r) % kShGU;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          if (t < T) {
+            float* hp = q.hsh + ((size_t)(kq * T + t) * 2) * Is + rb * kRowsCta + r_in;
+            hp[0] = acc1[t];
+            hp[Is] = acc3[t];
+          }
+      }
+      continue;
+    }
+    // routed: h of the 64 rows -> smem -> one piece block per token (the
+    // rows are group rb of the down projection's input)
     if (j == 0) {
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         if (t >= T) continue;
         float hv = 0.0f;
         if ((mask >> t) & 1u) {
-          hv = silu_glu_q3(acc1[t], acc3[t], routed ? a.d.swiglu_limit : 10.0f);
-          if (routed && a.d.route_before_down) hv *= slots.gate[slot][t];
+          hv = silu_glu_q3(acc1[t], acc3[t], a.d.swiglu_limit);
+          if (a.d.route_before_down) hv *= slots.gate[slot][t];
         }
-        q.h[((size_t)slot * T + t) * q.h_stride + row] = hv;
+        hrow[t][r_in] = hv;
       }
     }
+    __syncthreads();
+    // T x 4 threads (quads) build the token blocks; the bound is a multiple
+    // of 32 so whole warps take part in the quad shuffles
+    for (int i = threadIdx.x; i < ((T * 4 + 31) / 32) * 32; i += blockDim.x) {
+      const bool live = i < T * 4;
+      const int t = live ? (i >> 2) : 0, wi = i & 3;
+      float v[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = hrow[t][16 * wi + k];
+      float am = 0.0f, sum = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        am = fmaxf(am, fabsf(v[k]));
+        sum += v[k];
+      }
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      uint32_t hi[4], lo[4];
+      float sx;
+      make_pieces16(v, am, hi, lo, sx);
+      if (live) {
+        const size_t blk = ((size_t)slot * T + t) * (I / 64) + rb;
+        uint32_t* d = q.hpk + blk * kPk;
+        *reinterpret_cast<uint4*>(d + 4 * wi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(d + 16 + 4 * wi) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        if (wi == 0) q.hsx[blk] = make_float2(sx, sum);
+      }
+    }
+    __syncthreads();                             // hrow is rewritten by the next item
   }
 }
 
@@ -321,31 +391,53 @@ __global__ void __launch_bounds__(kQT, 2) q3_down_kernel(const Q3Args q) {
   extern __shared__ float4 smem4[];
   __shared__ Slots slots;
   build_slots(a, slots);
-  const int H = a.d.hidden, I = a.d.inter, T = a.tokens;
+  const int H = a.d.hidden, I = a.d.inter, T = a.tokens, G = I / 64;
   const bool has_shared = a.d.shared_w2 != nullptr;
   const int Is = has_shared ? a.d.shared_inter : 0;
-  const int Ip = padded(I), Isp = padded(Is);
-  float* hs = reinterpret_cast<float*>(smem4);   // routed: [kChunk][T][Ip]; shared: [T][Isp]
-  float* ysum = hs + kChunk * T * Ip;            // [kChunk][T][I / 64]
+  const int Isp = padded(Is);
+  uint32_t* hpk = reinterpret_cast<uint32_t*>(smem4);                              // [kChunk][T][G][kPkPad]
+  float2* hsx = reinterpret_cast<float2*>(hpk + (size_t)kChunk * T * G * kPkPad);  // [kChunk][T][G]
+  float* hs = reinterpret_cast<float*>(smem4);                                     // shared items: [T][Isp]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 3;
   const int D = slots.count;
   const int n_chunks = (D + kChunk - 1) / kChunk;
   const int n_rb = H / kRowsCta;
-  const int items = (n_chunks + (has_shared ? 1 : 0)) * n_rb;
+  const int items = (n_chunks + (has_shared ? kShDn : 0)) * n_rb;
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
     const int c = item / n_rb, rb = item % n_rb;
     const bool routed = c < n_chunks;
+    const int hf = routed ? 0 : c - n_chunks;    // shared expert: K half
     const int row = rb * kRowsCta + warp * 8 + (lane >> 2);
     float acc[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-    __syncthreads();                             // previous item's readers are done with hs
+    __syncthreads();                             // previous item's readers are done with the staging area
     if (routed) {
-      for (int ci = 0; ci < kChunk && c * kChunk + ci < D; ++ci)
-        stage_rows(q.h + (size_t)(c * kChunk + ci) * T * q.h_stride, T, I, q.h_stride, hs + ci * T * Ip,
-                   ysum + ci * T * (I / 64));
+      const int nsl = min(kChunk, D - c * kChunk);
+      const int nblk = nsl * T * G;
+      const uint32_t* src = q.hpk + (size_t)c * kChunk * T * G * kPk;
+      for (int i = threadIdx.x; i < nblk * (kPk / 4); i += blockDim.x) {
+        const int blk = i / (kPk / 4), w4 = i % (kPk / 4);
+        *reinterpret_cast<uint4*>(hpk + (size_t)blk * kPkPad + 4 * w4) =
+            *reinterpret_cast<const uint4*>(src + (size_t)blk * kPk + 4 * w4);
+      }
+      for (int i = threadIdx.x; i < nblk; i += blockDim.x) hsx[i] = q.hsx[(size_t)c * kChunk * T * G + i];
     } else {
-      stage_rows(q.h + (size_t)a.max_slots * T * q.h_stride, T, Is, q.h_stride, hs, nullptr);
+      // h of the shared expert = SwiGLU of the K-quarter sums (in order)
+      for (int i = threadIdx.x; i < T * (Is / 4); i += blockDim.x) {
+        const int t = i / (Is / 4), k = (i % (Is / 4)) * 4;
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+        for (int kq = 0; kq < kShGU; ++kq) {
+          const float* hp = q.hsh + ((size_t)(kq * T + t) * 2) * Is + k;
+          const float4 gg = *reinterpret_cast<const float4*>(hp);
+          const float4 uu = *reinterpret_cast<const float4*>(hp + Is);
+          g.x += gg.x; g.y += gg.y; g.z += gg.z; g.w += gg.w;
+          u.x += uu.x; u.y += uu.y; u.z += uu.z; u.w += uu.w;
+        }
+        *reinterpret_cast<float4*>(hs + t * Isp + pidx(k)) =
+            make_float4(silu_glu_q3(g.x, u.x, 10.0f), silu_glu_q3(g.y, u.y, 10.0f), silu_glu_q3(g.z, u.z, 10.0f),
+                        silu_glu_q3(g.w, u.w, 10.0f));
+      }
     }
     __syncthreads();
     if (routed) {
@@ -355,10 +447,8 @@ __global__ void __launch_bounds__(kQT, 2) q3_down_kernel(const Q3Args q) {
         const int e = slots.expert[slot];
         const size_t r = (size_t)e * H + row;
         const uint8_t* w = static_cast<const uint8_t*>(a.d.w2.data) + r * ((size_t)I * 3 / 8);
-        const __half2* sc = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w2.scales) + r * (I / 64));
-        const __half2* bi = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w2.biases) + r * (I / 64));
-        const float* hsl = hs + ci * T * Ip;
-        const float* ysl = ysum + ci * T * (I / 64);
+        const __half2* sc = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w2.scales) + r * G);
+        const __half2* bi = reinterpret_cast<const __half2*>(static_cast<const __half*>(a.d.w2.biases) + r * G);
         float part[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) part[t] = 0.0f;
@@ -371,14 +461,15 @@ __global__ void __launch_bounds__(kQT, 2) q3_down_kernel(const Q3Args q) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int g = 2 * seg + hh;
-            float Dq[NT];
-#pragma unroll
-            for (int t = 0; t < NT; ++t) Dq[t] = 0.0f;
-            group_one<NT>(hh ? g1 : g0, hsl + pidx(64 * g), Ip, mask, Dq);
             const float s = hh ? s2.y : s2.x, b = hh ? b2.y : b2.x;
 #pragma unroll
-            for (int t = 0; t < NT; ++t)
-              if ((mask >> t) & 1u) part[t] = fmaf(s, Dq[t], fmaf(b, ysl[t * (I / 64) + g], part[t]));
+            for (int t = 0; t < NT; ++t) {
+              if (!((mask >> t) & 1u)) continue;
+              const size_t blk = ((size_t)ci * T + t) * G + g;
+              const float2 sxy = hsx[blk];
+              const float d = group_dot(hh ? g1 : g0, hpk + blk * kPkPad);
+              part[t] = fmaf(s * sxy.x, d, fmaf(b, sxy.y, part[t]));
+            }
           }
         }
 #pragma unroll
@@ -391,34 +482,20 @@ __global__ void __launch_bounds__(kQT, 2) q3_down_kernel(const Q3Args q) {
     } else {
       const uint4* w = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.d.shared_w2) +
                                                       (size_t)row * Is);
-      for (int seg = j; seg < Is / 32; seg += 4) {
+      const int nseg = Is / 32 / kShDn;
+      for (int seg = hf * nseg + j; seg < (hf + 1) * nseg; seg += 4) {
         uint4 v[4];
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) v[cc] = __ldcs(w + seg * 4 + cc);
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (t >= T) continue;
-          const float4* hv = reinterpret_cast<const float4*>(hs + t * Isp + pidx(32 * seg));
-          float s = acc[t];
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const float4 xa = hv[2 * cc], xb = hv[2 * cc + 1];
-            const uint32_t aw[4] = {v[cc].x, v[cc].y, v[cc].z, v[cc].w};
-            const float xx[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              s = fmaf(__uint_as_float(aw[k] << 16), xx[2 * k], s);
-              s = fmaf(__uint_as_float(aw[k] & 0xFFFF0000u), xx[2 * k + 1], s);
-            }
-          }
-          acc[t] = s;
-        }
+        for (int t = 0; t < NT; ++t)
+          if (t < T) acc[t] += bf16_dot32(v, hs + t * Isp + pidx(32 * seg));
       }
     }
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t] = quad_sum(acc[t]);
     if (j == 0) {
-      const int cc = routed ? c : q.max_chunks;
+      const int cc = routed ? c : q.max_chunks + hf;
 #pragma unroll
       for (int t = 0; t < NT; ++t)
         if (t < T) q.part[((size_t)cc * T + t) * H + row] = acc[t];
@@ -442,37 +519,47 @@ __global__ void __launch_bounds__(kQT) q3_combine_kernel(const Q3Args q) {
   const int t = i / H, n = i % H;
   float acc = 0.0f;
   for (int c = 0; c < n_chunks; ++c) acc += q.part[((size_t)c * T + t) * H + n];
-  if (has_shared)
-    acc += __bfloat162float(__float2bfloat16_rn(q.part[((size_t)q.max_chunks * T + t) * H + n]));
+  if (has_shared) {
+    float sh = 0.0f;
+    for (int hf = 0; hf < kShDn; ++hf) sh += q.part[((size_t)(q.max_chunks + hf) * T + t) * H + n];
+    acc += __bfloat162float(__float2bfloat16_rn(sh));
+  }
   if (a.d.out_f32) static_cast<float*>(a.out)[i] = acc;
   else static_cast<__nv_bfloat16*>(a.out)[i] = __float2bfloat16_rn(acc);
 }
 
 struct Q3Layout {
-  size_t h, part, total;
-  int h_stride, max_chunks;
+  size_t hpk, hsx, hsh, part, total;
+  int max_chunks;
 };
+
+size_t up256(size_t v) { return (v + 255) / 256 * 256; }
 
 Q3Layout q3_layout(const DsMoeDesc& d, int T) {
   Q3Layout L;
   const int S = std::min(T * d.top_k, d.n_experts);
   const int Is = d.shared_w1 ? d.shared_inter : 0;
-  L.h_stride = std::max(d.inter, Is);
   L.max_chunks = (S + kChunk - 1) / kChunk;
-  size_t o = 256;                                 // error word etc.
-  L.h = o;
-  o += ((size_t)(S + 1) * T * L.h_stride * 4 + 255) / 256 * 256;
-  L.part = o;
-  o += ((size_t)(L.max_chunks + 1) * T * d.hidden * 4 + 255) / 256 * 256;
+  const size_t blocks = (size_t)L.max_chunks * kChunk * T * (d.inter / 64);
+  size_t o = 256;                                 // error word
+  L.hpk = o;  o += up256(blocks * kPk * 4);
+  L.hsx = o;  o += up256(blocks * sizeof(float2));
+  L.hsh = o;  o += up256((size_t)kShGU * T * 2 * Is * 4);
+  L.part = o; o += up256((size_t)(L.max_chunks + kShDn) * T * d.hidden * 4);
   L.total = o;
   return L;
 }
 
-size_t smem_gate_up(const DsMoeDesc& d, int T) { return (size_t)T * padded(d.hidden) * 4 + (size_t)T * (d.hidden / 64) * 4; }
+size_t smem_gate_up(const DsMoeDesc& d, int T) {
+  const int G = d.hidden / 64;
+  const size_t pk = (size_t)T * G * kPkPad * 4 + (size_t)T * G * sizeof(float2);
+  return pk + (d.shared_w1 ? (size_t)T * padded(d.hidden) * 4 : 0);
+}
 
 size_t smem_down(const DsMoeDesc& d, int T) {
   const int Is = d.shared_w1 ? d.shared_inter : 0;
-  const size_t routed = (size_t)kChunk * T * padded(d.inter) * 4 + (size_t)kChunk * T * (d.inter / 64) * 4;
+  const int G = d.inter / 64;
+  const size_t routed = (size_t)kChunk * T * G * kPkPad * 4 + (size_t)kChunk * T * G * sizeof(float2);
   return std::max(routed, (size_t)T * padded(Is) * 4);
 }
 
@@ -528,7 +615,7 @@ int launch_nt(const Q3Args& q, cudaStream_t st) {
 bool q3_supported(const DecodeArgs& a) {
   const DsMoeDesc& d = a.d;
   if (a.x_f32 || d.w1.format != DS_FMT_Q3 || a.tokens < 1 || a.tokens > 8) return false;
-  if (d.hidden % 128 != 0 || d.inter % 128 != 0 || d.hidden % kRowsCta != 0 || d.inter % kRowsCta != 0) return false;
+  if (d.hidden % 128 != 0 || d.inter % 128 != 0) return false;
   const bool sh = d.shared_w1 != nullptr;
   if (sh && (d.shared_inter % 128 != 0)) return false;
   if (!ds::aligned(a.x, 16) || !ds::aligned(d.w1.data, 16) || !ds::aligned(d.w3.data, 16) ||
@@ -548,13 +635,15 @@ int launch_q3(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   const Q3Layout L = q3_layout(a.d, a.tokens);
   DS_REQUIRE(workspace_bytes >= L.total, DS_EINVAL, "moe_decode: workspace %zu bytes < %zu (q3 path)",
              workspace_bytes, L.total);
+  char* ws = static_cast<char*>(workspace);
   Q3Args q;
   q.a = a;
-  q.a.err = static_cast<int*>(workspace);
+  q.a.err = reinterpret_cast<int*>(ws);
   q.a.max_slots = std::min(a.tokens * a.d.top_k, a.d.n_experts);
-  q.h = reinterpret_cast<float*>(static_cast<char*>(workspace) + L.h);
-  q.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + L.part);
-  q.h_stride = L.h_stride;
+  q.hpk = reinterpret_cast<uint32_t*>(ws + L.hpk);
+  q.hsx = reinterpret_cast<float2*>(ws + L.hsx);
+  q.hsh = reinterpret_cast<float*>(ws + L.hsh);
+  q.part = reinterpret_cast<float*>(ws + L.part);
   q.max_chunks = L.max_chunks;
   if (a.tokens == 1) return launch_nt<1>(q, st);
   if (a.tokens == 2) return launch_nt<2>(q, st);

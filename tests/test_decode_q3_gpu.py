@@ -2,8 +2,11 @@
 CUDA-core dot products) vs the torch fp32 oracle of moe_layer
 (mlx_forward.py:388-419) with the q3 groups dequantised by oracle/q3.py.
 Shapes are chosen so that ds_moe_decode takes this path (hidden, inter and
-the shared inter multiples of 128).  Tolerance: relative L2 <= 1e-3; f32
-output without a shared expert <= 1e-5.
+the shared inter multiples of 128).  Tolerance: relative L2 <= 1e-3 (the
+north-star bar).  The path multiplies the 3-bit codes with int8 pieces of the
+activations (hi + lo / 256 per 64-value group: ~15 significant bits relative
+to the group maximum; x and h are each cut once), so an f32 output sits near
+1e-4 of the oracle; those cases are held to 5e-4.
 """
 from __future__ import annotations
 
@@ -41,7 +44,7 @@ def test_q3_path_dropped_repeated_slots_f32_out(cuda):
     out = moe.moe_decode(x.cuda(), layer, ids.cuda(), wts.cuda(), out_f32=True)
     ref = oracle_out(x.float(), ids, wts, layer, None)
     assert out.dtype == torch.float32
-    assert rel_l2(out, ref) < 1e-5, rel_l2(out, ref)
+    assert rel_l2(out, ref) < 5e-4, rel_l2(out, ref)
 
 
 def test_q3_path_gate_after_down(cuda):
@@ -53,7 +56,7 @@ def test_q3_path_gate_after_down(cuda):
     x = torch.randn(2, H, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
     out = moe.moe_decode(x.cuda(), layer, ids.cuda(), wts.cuda(), out_f32=True)
     ref = oracle_out(x.float(), ids, wts, layer, None)
-    assert rel_l2(out, ref) < 1e-5, rel_l2(out, ref)
+    assert rel_l2(out, ref) < 5e-4, rel_l2(out, ref)
 
 
 def test_q3_path_expert_id_out_of_range_sets_error(cuda):
