@@ -228,6 +228,8 @@ def time_reference(steps: int, warmup: int, budget_s: float | None = None) -> tu
 def run_ours(args) -> dict:
     if args.config == "c4":
         return run_grouped(args)
+    if args.config == "c5":
+        return run_stack(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         return run_ep(args)
     return run_decode(args)
@@ -463,6 +465,244 @@ def run_ep(args) -> dict:
         comm.close()
     dist.barrier()
     dist.destroy_process_group()
+    return result
+
+
+def run_stack(args) -> dict:
+    """a decode step through a 40-layer stack (layers 0-19
+    FP4, 20-39 q3, each a config-2 layer), --batch tokens per GPU per step,
+    each layer's output feeding the next.  N = 1: all 256 experts of every
+    layer on the GPU (131 GB resident), the whole step one CUDA graph.
+    N > 1: rank g holds experts [g E/N, (g+1) E/N) of every layer; with
+    N * batch <= 8 the layers exchange through ds_ep_decode (NVLink peer
+    memory, one CUDA graph per step), otherwise through NCCL all-to-all."""
+    import datetime
+
+    import torch
+
+    from deepseeker import ep, moe, synthetic
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    NL = args.stack_layers
+    b = args.batch
+    El = E // world
+    fmts = ["fp4" if l < NL // 2 else "q3" for l in range(NL)]
+    layers = []
+    for l in range(NL):
+        layer = synthetic.make_layer(fmts[l], H, I, El, seed=1000 * l + 1, shared_inter=IS, std=0.02, device=dev,
+                                     expert_offset=rank * El)
+        layers.append(layer.prepare_tc())
+    torch.cuda.synchronize(dev)
+    peer = world > 1 and world * b <= 8
+    if world > 1 and not peer:
+        eps = [ep.gpu_layer(layer, E, K_TOP) for layer in layers]
+    n_in = 64                                     # distinct step inputs, cycled
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    x_pool = torch.randn(n_in, b, H, generator=g, device=dev).to(torch.bfloat16)
+    l_pool = torch.randn(n_in, NL, b, E, generator=g, device=dev)
+    stage_x = torch.zeros(b, H, dtype=torch.bfloat16, device=dev)
+    stage_l = torch.zeros(NL, b, E, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    graph = None
+    comm = None
+    if world == 1:
+        # one graph: for every layer, routing + the decode kernels over
+        # chunks of 8 tokens, ping-pong activation buffers
+        bufs = [torch.zeros(b, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        wbuf = torch.empty(b, K_TOP, dtype=torch.float32, device=dev)
+        ibuf = torch.empty(b, K_TOP, dtype=torch.int32, device=dev)
+        ws_bytes = max(max(layer.decode_workspace_bytes(min(8, b), K_TOP) for layer in layers[::NL // 2]), 1 << 20)
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+
+        def body():
+            cur = stage_x
+            for l, layer in enumerate(layers):
+                nxt = bufs[l % 2]
+                moe.route_softmax_topk(stage_l[l], K_TOP, out=(wbuf, ibuf))
+                for r0 in range(0, b, 8):
+                    r1 = min(b, r0 + 8)
+                    moe.moe_decode(cur[r0:r1], layer, ibuf[r0:r1], wbuf[r0:r1], out=nxt[r0:r1], workspace=ws)
+                cur = nxt
+            return cur
+        out_buf = body()                          # eager once: attributes, caches
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out_buf = body()
+    elif peer:
+        comm = ep.PeerComm(b, H, K_TOP, timeout_ms=30000)
+        pgs = []
+        for l, layer in enumerate(layers):
+            pl = ep.PeerDecodeLayer(comm, layer, E, K_TOP, rows=b)
+            pgs.append(ep.PeerDecodeGraph(pl, x=stage_x if l == 0 else pgs[-1].out, logits=stage_l[l]))
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for pg in pgs:
+                pg._step()
+        out_buf = pgs[-1].out
+
+    def step(i):
+        j = i % n_in
+        stage_x.copy_(x_pool[j])
+        stage_l.copy_(l_pool[j])
+        if graph is not None:
+            graph.replay()
+            return out_buf
+        cur = stage_x
+        for l in range(NL):
+            w, ids = moe.route_softmax_topk(stage_l[l], K_TOP)
+            cur = eps[l](cur, ids, w)
+        return cur
+
+    def agreed(n: int) -> int:
+        if dist is None:
+            return n
+        t = torch.tensor([n], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return int(t.item())
+
+    with ClockSampler(local) as clk:
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")
+        start.record(stream)
+        for s_ in range(args.steps):
+            step(args.warmup + s_)
+        end.record(stream)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ms = start.elapsed_time(end)
+        if not args.quick:
+            extra = agreed(int(500.0 / max(ms / args.steps, 1e-3)))
+            for i in range(min(extra, 2000)):
+                step(i)
+            torch.cuda.synchronize(dev)
+    clocks = clk.summary()
+
+    # e2e: the step's x and logits from pinned host memory, output back
+    e2e_steps = 0 if args.quick else min(args.steps, 20)
+    pin_x = x_pool[:max(e2e_steps, 1)].cpu().pin_memory()
+    pin_l = l_pool[:max(e2e_steps, 1)].cpu().pin_memory()
+    pin_o = torch.empty(b, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(s_):
+        stage_x.copy_(pin_x[s_], non_blocking=True)
+        stage_l.copy_(pin_l[s_], non_blocking=True)
+        if graph is not None:
+            graph.replay()
+            o = out_buf
+        else:
+            cur = stage_x
+            for l in range(NL):
+                w, ids = moe.route_softmax_topk(stage_l[l], K_TOP)
+                cur = eps[l](cur, ids, w)
+            o = cur
+        pin_o.copy_(o, non_blocking=True)
+        stream.synchronize()
+    for s_ in range(min(2, e2e_steps)):
+        e2e_step(s_)
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s_ in range(e2e_steps):
+        e2e_step(s_)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max(e0.elapsed_time(e1), 1e-9)
+
+    # bytes one GPU streams per step: per layer, its distinct local experts of
+    # the step's routing (all ranks' tokens) + the shared expert (split over
+    # the ranks on the peer path) + activations
+    per_exp = {f: sum(bk.nbytes() // El for bk in (layers[i].w1, layers[i].w3, layers[i].w2))
+               for f, i in (("fp4", 0), ("q3", NL - 1))}
+    steps_idx = [(args.warmup + s_) % n_in for s_ in range(args.steps)]
+    ids_all = torch.stack([torch.stack([moe.route_softmax_topk(l_pool[j][l], K_TOP)[1] for l in range(NL)])
+                           for j in steps_idx])                               # [steps, NL, b, k]
+    if dist is not None:
+        gathered = torch.empty((world,) + tuple(ids_all.shape), dtype=ids_all.dtype, device=dev)
+        dist.all_gather_into_tensor(gathered, ids_all.contiguous())
+        ids_all = gathered.permute(1, 2, 0, 3, 4).reshape(args.steps, NL, -1)
+    ids_all = ids_all.reshape(args.steps, NL, -1).cpu()
+    shared_b = 3 * IS * H * 2 // world if (peer and IS % (256 * world) == 0) else 3 * IS * H * 2 * ((b + 7) // 8)
+    tot = 0.0
+    for st_ in range(args.steps):
+        for l in range(NL):
+            mine = {int(e) for e in ids_all[st_, l].tolist() if rank * El <= e < (rank + 1) * El}
+            tot += len(mine) * per_exp[fmts[l]] + shared_b + 2 * b * H * 2
+    step_bytes = tot / args.steps
+    ms_t = torch.tensor([ms, e2e_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = (float(v) for v in ms_t.cpu())
+    result = None
+    if rank == 0:
+        pk, kind = peaks()
+        gbs = step_bytes / (ms / args.steps * 1e-3) / 1e9
+        result = {
+            "metric": METRIC,
+            "value": round(world * b * args.steps / (ms * 1e-3), 2),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp4-e2m1 (layers 0-19) and q3-affine (20-39) weights, bf16 activations, f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights quantised on device, seed 1000*layer+1; router logits "
+                    "N(0,1) per layer and step)",
+            "config": {"workload": f"BASELINE config 5: {NL}-layer MoE stack decode, {b} token(s) per GPU per step, "
+                                   "hidden 4096, 256 experts inter 2048 top-8 softmax, bf16 shared expert per layer",
+                       "layers": NL, "tokens_per_step_per_gpu": b,
+                       "resident_gb_per_gpu": round(sum(sum(bk.nbytes() for bk in (ly.w1, ly.w3, ly.w2)) +
+                                                        3 * IS * H * 2 for ly in layers) / 1e9, 1),
+                       "l2": "each step streams every layer's experts once (the stack is far above L2)",
+                       "parallelism": ("single GPU, the step in one CUDA graph" if world == 1 else
+                                       f"ep{world} over NVLink peer memory (ds_ep_decode), the step in one CUDA graph"
+                                       if peer else f"ep{world} over NCCL all_to_all_single")},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None,
+                         "kernel": "whole stack step per GPU (40 layers: router + decode kernels)",
+                         "bytes_per_launch": int(step_bytes), "peak_kind": kind},
+            "e2e": {"value": round(world * b * max(e2e_steps, 1) / (e2e_ms * 1e-3), 2) if e2e_steps else None,
+                    "unit": "tokens/s", "h2d_bytes_per_step": b * (H * 2 + NL * E * 4),
+                    "d2h_bytes_per_step": b * H * 2},
+            # ours per layer: router + prep/gemm/h/gemm/combine (FP4, tcgen05) or
+            # gate_up/down/combine (q3) per 8-token chunk, + 2 exchange kernels (peer)
+            "gpu_launches": args.steps * sum(
+                1 + (5 if f == "fp4" else 3) * (((b + 7) // 8) if world == 1 else 1) + (2 if peer else 0)
+                for f in fmts) if (world == 1 or peer) else None,
+            "clocks": clocks,
+        }
+    graph = None
+    torch.cuda.synchronize(dev)
+    if comm is not None:
+        if dist is not None:
+            dist.barrier()
+        comm.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
     return result
 
 
@@ -851,7 +1091,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c2")
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--stack-layers", type=int, default=40, help="config 5: layers in the stack (half FP4, half q3)")
     ap.add_argument("--layers", type=int, default=8, help="distinct resident layers rotated (L2-cold)")
     ap.add_argument("--batch", type=int, default=1, help="decode tokens per GPU per step (N > 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -898,6 +1139,14 @@ def main() -> int:
                 value, cores, sample = time_reference_grouped(budget_s=20.0)
                 result["cpu_baseline"] = {"value": round(value, 6), "unit": "TFLOP/s", "cores": cores,
                                           "kind": "port", "sample": sample}
+            elif args.config == "c5":
+                # one layer of the reference CPU path, timed; a stack step is
+                # args.stack_layers such layers in sequence
+                value, cores, sample = time_reference(steps=1000, warmup=1, budget_s=15.0)
+                result["cpu_baseline"] = {"value": round(value / args.stack_layers, 5), "unit": "tokens/s",
+                                          "cores": cores, "kind": "port",
+                                          "sample": sample + f"; divided by the {args.stack_layers} layers of a "
+                                                             "stack step"}
             else:
                 value, cores, sample = time_reference(steps=1000, warmup=1, budget_s=15.0)
                 result["cpu_baseline"] = {"value": round(value, 4), "unit": "tokens/s", "cores": cores,

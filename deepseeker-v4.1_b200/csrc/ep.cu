@@ -9,7 +9,8 @@
 //      NVLink into memory opened with CUDA IPC), raises a flag there, waits
 //      for all G flags of its own area and rewrites the gathered ids to local
 //      expert ids (-1 where another rank owns the expert).
-//   2. the tcgen05 decode kernels (moe_decode_t5.cu) over the G*b gathered
+//   2. the decode kernels (tcgen05 for FP4 banks, moe_decode_t5.cu; CUDA-core
+//      for q3 banks, moe_decode_q3.cu) over the G*b gathered
 //      rows: this rank's routed experts for every row and slice `rank` of
 //      the shared expert's intermediate features for every row (when the
 //      shared inter splits into G slices of 256; otherwise the whole shared
@@ -421,7 +422,9 @@ extern "C" int ds_ep_decode_workspace_size(DsEp* ep, const DsMoeDesc* desc, int6
   DS_REQUIRE(ep != nullptr && desc != nullptr && bytes != nullptr, DS_EINVAL, "ep_decode_workspace_size: null");
   DS_REQUIRE(rows >= 1 && rows <= ep->max_rows, DS_EINVAL, "ep_decode_workspace_size: rows %lld outside 1..%d",
              (long long)rows, ep->max_rows);
-  *bytes = ds::decode::t5_workspace_bytes(*desc, (int)(ep->world * rows));
+  const int T = (int)(ep->world * rows);
+  *bytes = desc->w1.format == DS_FMT_Q3 ? ds::decode::q3_workspace_bytes(*desc, T)
+                                        : ds::decode::t5_workspace_bytes(*desc, T);
   return DS_OK;
 }
 
@@ -484,7 +487,7 @@ extern "C" int ds_ep_decode(DsEp* ep, const DsMoeDesc* desc, int32_t first_exper
   // the ranks in the combine); otherwise each rank evaluates all of it for
   // its own rows
   const bool sh = desc->shared_w1 != nullptr;
-  a.split = sh && desc->shared_inter % (256 * G) == 0;
+  a.split = sh && desc->shared_inter % (256 * G) == 0;     // slices of 256 suit both decode paths
   if (a.split) {
     const int Is = desc->shared_inter, Isl = Is / G, r = ep->rank;
     d.d.shared_inter = Isl;
@@ -494,9 +497,11 @@ extern "C" int ds_ep_decode(DsEp* ep, const DsMoeDesc* desc, int32_t first_exper
     d.sh_w2_ld = Is;
     d.out_sh = reinterpret_cast<float*>(ep->own + ep->L.part_sh);
   }
-  DS_REQUIRE(ds::decode::t5_supported(d), DS_ENOTSUP,
-             "ep_decode: needs FP4 banks with scale atoms, hidden and inter multiples of 1024 (tensor-core "
-             "decode kernels)");
+  const bool t5 = ds::decode::t5_supported(d);
+  const bool q3 = !t5 && ds::decode::q3_supported(d);
+  DS_REQUIRE(t5 || q3, DS_ENOTSUP,
+             "ep_decode: needs FP4 banks with scale atoms (hidden and inter multiples of 1024) or Q3 banks "
+             "(multiples of 128)");
 
   // programmatic dependent launches: each kernel starts while its
   // predecessor drains and waits for it (griddepcontrol.wait) before it
@@ -511,7 +516,8 @@ extern "C" int ds_ep_decode(DsEp* ep, const DsMoeDesc* desc, int32_t first_exper
   cfg.blockDim = dim3(kEpThreads);
   cfg.gridDim = dim3(G * kDispatchBlocks);
   DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, ep_dispatch_kernel, a));
-  int rc = ds::decode::launch_t5(d, workspace, workspace_bytes, st);
+  int rc = t5 ? ds::decode::launch_t5(d, workspace, workspace_bytes, st)
+              : ds::decode::launch_q3(d, workspace, workspace_bytes, st);
   if (rc != DS_OK) return rc;
   cfg.gridDim = dim3(G * kCombineBlocks);
   DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, ep_combine_kernel, a));

@@ -26,13 +26,14 @@ struct DecodeArgs {
   int max_slots;      // routed slots reserved = min(T*k, E)
   int h_stride;       // max(I, shared_inter), multiple of 4
   int* err;           // device error word
-  // tcgen05 path only: the shared expert is added to output rows
+  // tcgen05 and q3 paths only: the shared expert is added to output rows
   // [sh_row0, sh_row1) (expert-parallel ranks add it to their own rows)
   int sh_row0 = 0, sh_row1 = 1 << 30;
-  // tcgen05 path only: row stride (elements) of shared_w2 when the shared
-  // expert is a column slice of a wider one (0: shared_inter), and an f32
-  // [T, H] output that receives the shared expert's sum unrounded instead
-  // of adding it to `out` (expert-parallel ranks that each hold a slice)
+  // tcgen05 and q3 paths only: row stride (elements) of shared_w2 when the
+  // shared expert is a column slice of a wider one (0: shared_inter), and an
+  // f32 [T, H] output that receives the shared expert's sum unrounded
+  // instead of adding it to `out` (expert-parallel ranks that each hold a
+  // slice)
   int sh_w2_ld = 0;
   float* out_sh = nullptr;
 };

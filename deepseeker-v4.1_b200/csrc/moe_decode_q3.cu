@@ -480,8 +480,10 @@ __global__ void __launch_bounds__(kQT, 2) q3_down_kernel(const Q3Args q) {
         }
       }
     } else {
-      const uint4* w = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.d.shared_w2) +
-                                                      (size_t)row * Is);
+      // row stride of W2: the full shared inter when this call holds a
+      // column slice of it (expert-parallel ranks), else Is
+      const size_t ld = a.sh_w2_ld > 0 ? (size_t)a.sh_w2_ld : (size_t)Is;
+      const uint4* w = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.d.shared_w2) + row * ld);
       const int nseg = Is / 32 / kShDn;
       for (int seg = hf * nseg + j; seg < (hf + 1) * nseg; seg += 4) {
         uint4 v[4];
@@ -522,7 +524,8 @@ __global__ void __launch_bounds__(kQT) q3_combine_kernel(const Q3Args q) {
   if (has_shared) {
     float sh = 0.0f;
     for (int hf = 0; hf < kShDn; ++hf) sh += q.part[((size_t)(q.max_chunks + hf) * T + t) * H + n];
-    acc += __bfloat162float(__float2bfloat16_rn(sh));
+    if (a.out_sh != nullptr) a.out_sh[i] = sh;                  // summed over ranks by the caller
+    else if (t >= a.sh_row0 && t < a.sh_row1) acc += __bfloat162float(__float2bfloat16_rn(sh));
   }
   if (a.d.out_f32) static_cast<float*>(a.out)[i] = acc;
   else static_cast<__nv_bfloat16*>(a.out)[i] = __float2bfloat16_rn(acc);

@@ -384,8 +384,8 @@ class PeerComm:
 
 class PeerDecodeLayer:
     """One layer of expert-parallel decode on ``PeerComm``: this rank's FP4
-    shard ``local_layer`` (global experts [rank * E_l, (rank + 1) * E_l),
-    scale atoms prepared here), ``rows`` tokens per rank and step.
+    (scale atoms prepared here) or q3 shard ``local_layer`` (global experts
+    [rank * E_l, (rank + 1) * E_l)), ``rows`` tokens per rank and step.
 
     ``layer(x [rows, H] bf16, ids [rows, k] int32 global, gates [rows, k] f32)``
     -> [rows, H] bf16: all ranks' routed experts plus the shared expert, the

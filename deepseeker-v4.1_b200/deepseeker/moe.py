@@ -169,7 +169,10 @@ class MoEWeights:
         return self.w1.cols
 
     def prepare_tc(self) -> "MoEWeights":
-        """FP4 layers: prepare the scale atoms the tcgen05 decode kernels read."""
+        """FP4 layers: prepare the scale atoms the tcgen05 decode kernels read
+        (q3 layers need no preparation: a no-op)."""
+        if self.w1.fmt != _abi.DS_FMT_FP4:
+            return self
         for b in (self.w1, self.w3, self.w2):
             b.prepare_atoms()
         self._descs.clear()

@@ -299,8 +299,9 @@ int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x_dtype, int
  * with the same `rows`.  Device waits give up after `timeout_ms`; the error
  * word then holds bit 2 (ds_ep_status), and later calls of that
  * communicator return without exchanging (outputs undefined).
- * Limits: world <= 8, world * max_rows <= 8, FP4 banks with scale atoms,
- * hidden and inter multiples of 1024 (the tcgen05 decode kernels). */
+ * Limits: world <= 8, world * max_rows <= 8; FP4 banks with scale atoms,
+ * hidden and inter multiples of 1024 (the tcgen05 decode kernels), or Q3
+ * banks, hidden and inter multiples of 128 (the CUDA-core q3 kernels). */
 #define DS_EP_HANDLE_BYTES 64
 typedef struct DsEp DsEp;
 int ds_ep_create(int world, int rank, int max_rows, int hidden, int top_k, int timeout_ms, DsEp** ep);

@@ -112,14 +112,14 @@ def rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
         q.put((rank, f"exception: {e!r}"))
 
 
-def gpu_problem(rank: int, world: int, shared_inter: int = 512):
+def gpu_problem(rank: int, world: int, shared_inter: int = 512, fmt: str = "fp4"):
     from deepseeker import synthetic
     from oracle import moe as omoe
 
     dev = torch.device("cuda", rank)
     Hg, Ig, Eg, Kg, Bg = 1024, 1024, 16, 4, 6
     El = Eg // world
-    layer = synthetic.make_layer("fp4", Hg, Ig, El, seed=5, shared_inter=shared_inter, device=dev,
+    layer = synthetic.make_layer(fmt, Hg, Ig, El, seed=5, shared_inter=shared_inter, device=dev,
                                  expert_offset=rank * El)
     g = torch.Generator().manual_seed(77)
     x = torch.randn(Bg, Hg, generator=g).to(torch.bfloat16).to(dev)
@@ -167,8 +167,12 @@ def run_gpu_peer_rank(rank: int, world: int, q) -> None:
     layer2 = gpu_problem(rank, world, shared_inter=256)[0]
     pl2 = ep.PeerDecodeLayer(comm, layer2, Eg, Kg, rows=4)
     eager2 = pl2(x[:4].contiguous(), ids[:4].contiguous(), w[:4].contiguous())
+    # q3 layer through the same communicator
+    layer3 = gpu_problem(rank, world, fmt="q3")[0]
+    pl3 = ep.PeerDecodeLayer(comm, layer3, Eg, Kg, rows=4)
+    eager3 = pl3(x[:4].contiguous(), ids[:4].contiguous(), w[:4].contiguous())
     torch.cuda.synchronize()
     status = comm.status()
     del gr
     comm.close()
-    q.put((rank, (eager.cpu(), out_g.cpu(), logits.cpu(), status, eager2.cpu())))
+    q.put((rank, (eager.cpu(), out_g.cpu(), logits.cpu(), status, eager2.cpu(), eager3.cpu())))

@@ -49,6 +49,21 @@ def test_peer_single_rank_equals_decode(cuda):
     comm.close()
 
 
+def test_peer_single_rank_q3_equals_decode(cuda):
+    """q3 banks take the CUDA-core decode kernels inside the exchange."""
+    from deepseeker import ep, moe
+
+    layer, x, ids, w, E, K = ep_worker.gpu_problem(0, 1, fmt="q3")
+    comm = ep.PeerComm(4, layer.hidden, K)
+    x4, i4, w4 = x[:4].contiguous(), ids[:4].contiguous(), w[:4].contiguous()
+    out = ep.PeerDecodeLayer(comm, layer, E, K, rows=4)(x4, i4, w4)
+    ref = moe.moe_decode(x4, layer, i4, w4)
+    torch.cuda.synchronize()
+    assert comm.status() == 0
+    assert torch.equal(out, ref), rel_l2(out, ref)
+    comm.close()
+
+
 def test_peer_graph_replays_match_eager(cuda):
     from deepseeker import ep, moe
 
@@ -105,6 +120,8 @@ def test_peer_two_ranks(cuda):
     single = moe.moe_decode(x4, layer, i4, w4).cpu()
     layer2 = ep_worker.gpu_problem(0, 1, shared_inter=256)[0].prepare_tc()
     single2 = moe.moe_decode(x4, layer2, i4, w4).cpu()
+    layer3 = ep_worker.gpu_problem(0, 1, fmt="q3")[0]
+    single3 = moe.moe_decode(x4, layer3, i4, w4).cpu()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
@@ -125,7 +142,8 @@ def test_peer_two_ranks(cuda):
                 p.kill()
     for r in (0, 1):
         assert isinstance(res[r], tuple), res[r]
-        eager, out_g, logits, status, eager2 = res[r]
+        eager, out_g, logits, status, eager2, eager3 = res[r]
+        assert rel_l2(eager3, single3) <= 1e-3, rel_l2(eager3, single3)      # q3 banks
         assert status == 0
         assert rel_l2(eager, single) <= 1e-3, rel_l2(eager, single)            # shared expert split 2 ways
         assert rel_l2(eager2, single2) <= 1e-3, rel_l2(eager2, single2)        # shared expert per own rows
