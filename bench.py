@@ -38,7 +38,9 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
-os.environ.setdefault("NCCL_DEBUG", "WARN")   # keep stdout to the one JSON line
+# stdout carries the one JSON line: NCCL's messages (when NCCL_DEBUG is set)
+# go to stderr
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 sys.path.insert(0, str(ROOT / "deepseeker-v4.1_b200"))
 sys.path.insert(0, str(ROOT))
 

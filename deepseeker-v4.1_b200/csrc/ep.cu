@@ -5,31 +5,33 @@
 // One ds_ep_decode call per layer and rank:
 //
 //   1. ep_dispatch_kernel: every rank stores its b token rows (x, global ids,
-//      gates) into slot `rank` of every rank's receive area (P2P stores over
-//      NVLink into memory opened with CUDA IPC), raises a flag there, waits
-//      for all G flags of its own area and rewrites the gathered ids to local
+//      gates) into slot `rank` of every rank's dispatch area (P2P stores over
+//      NVLink into memory opened with CUDA IPC), then reads the G slots of
+//      its own area into local buffers, rewriting the gathered ids to local
 //      expert ids (-1 where another rank owns the expert).
 //   2. the decode kernels (tcgen05 for FP4 banks, moe_decode_t5.cu; CUDA-core
-//      for q3 banks, moe_decode_q3.cu) over the G*b gathered
-//      rows: this rank's routed experts for every row and slice `rank` of
-//      the shared expert's intermediate features for every row (when the
-//      shared inter splits into G slices of 256; otherwise the whole shared
-//      expert for its own rows), f32 partial rows out.
+//      for q3 banks, moe_decode_q3.cu) over the G*b gathered rows: this
+//      rank's routed experts for every row and slice `rank` of the shared
+//      expert's intermediate features for every row (when the shared inter
+//      splits into G slices of 256; otherwise the whole shared expert for its
+//      own rows), f32 partial rows out.
 //   3. ep_combine_kernel: every rank stores the partial rows of rank q's
-//      tokens into slot `rank` of q's reduce areas, raises a flag there,
-//      waits for all G flags of its own area and sums the G slots in rank
-//      order into its bf16 output: routed partials, plus the shared sum
-//      rounded to bf16 first (the reference adds the shared expert's output
-//      in the activation dtype, src/deepseeker/mlx_runner.py:776-781).
+//      tokens into slot `rank` of q's combine area, then sums the G slots of
+//      its own area in rank order into its bf16 output: routed partials,
+//      plus the shared sum rounded to bf16 first (the reference adds the
+//      shared expert's output in the activation dtype,
+//      src/deepseeker/mlx_runner.py:776-781).
 //
-// Nothing on the path calls NCCL, so a step of many layers captures into one
-// CUDA graph.  Flags carry epochs: each kernel block keeps a counter in local
-// device memory and adds 1 to the flag it raises, so a flag reaches
-// epoch * blocks-per-peer when every block of that peer has stored its part.
-// Flags are never reset; graph replays keep counting.  A receive area is
-// written again only after its owner has moved past the step that reads it
-// (the next dispatch of a peer needs this rank's own next dispatch, which
-// follows this rank's combine), so one buffer of each kind suffices.
+// Exchange format: every 4-byte data word travels with the call's epoch in
+// one 8-byte store; a reader polls each word until it carries the epoch it
+// expects, so the data needs no fence and no separate flag.  The epoch is a
+// per-block counter in local device memory (every block of every rank runs
+// once per call, so the counters agree); nothing is ever reset and graph
+// replays keep counting.  Nothing on the path calls NCCL, so a step of many
+// layers captures into one CUDA graph.  An area is written again only after
+// its owner has moved past the step that reads it (a peer's next dispatch
+// follows its combine, which needs this rank's combine push, which follows
+// this rank's reads), so one area of each kind suffices.
 //
 // Every wait is bounded by %globaltimer (the communicator's timeout); a
 // timeout sets the error word and an abort flag, and later kernels of an
@@ -60,28 +62,28 @@ constexpr int kErrTimeout = 2;
 
 size_t up256(size_t v) { return (v + 255) / 256 * 256; }
 
-// Byte offsets inside one rank's region (identical on every rank).  The
-// first part (flags, receive and reduce areas) is written by peers; the rest
-// is local.
+// Byte offsets inside one rank's region (identical on every rank).  The two
+// exchange areas are written by peers in the low-latency word format (8-byte
+// stores of {data word, epoch}); the rest is local.
 struct EpLayout {
-  size_t flags_g, flags_r, recv_x, recv_ids, recv_w, rbuf, rbuf_sh;   // peer-visible
-  size_t ctr, err, ids_local, part, part_sh;                           // local
+  size_t ll_g, ll_r;                                   // peer-written
+  size_t ctr, err, recv_x, recv_w, ids_local, part, part_sh;   // local
   size_t total;
+  int slot_g, slot_r;                                  // words per sender slot in ll_g / ll_r
 };
 
 EpLayout ep_layout(int world, int max_rows, int H, int k) {
   EpLayout L;
   const size_t R = (size_t)world * max_rows;
+  L.slot_g = max_rows * (H / 2 + 2 * k);               // x as u32 words, ids, gates
+  L.slot_r = 2 * max_rows * H;                         // routed partials, shared partials
   size_t o = 0;
-  L.flags_g = o;   o += 256;
-  L.flags_r = o;   o += 256;
-  L.recv_x = o;    o += up256(R * H * 2);
-  L.recv_ids = o;  o += up256(R * k * 4);
-  L.recv_w = o;    o += up256(R * k * 4);
-  L.rbuf = o;      o += up256(R * H * 4);
-  L.rbuf_sh = o;   o += up256(R * H * 4);
+  L.ll_g = o;      o += up256((size_t)world * L.slot_g * 8);
+  L.ll_r = o;      o += up256((size_t)world * L.slot_r * 8);
   L.ctr = o;       o += 512;
   L.err = o;       o += 256;
+  L.recv_x = o;    o += up256(R * H * 2);
+  L.recv_w = o;    o += up256(R * k * 4);
   L.ids_local = o; o += up256(R * k * 4);
   L.part = o;      o += up256(R * H * 4);
   L.part_sh = o;   o += up256(R * H * 4);
@@ -94,7 +96,7 @@ struct EpArgs {
   EpLayout L;
   int world, rank, rows, H, k;
   int first_expert, local_experts;
-  int split;               // 1: the shared expert's partial sums travel in their own area (rbuf_sh)
+  int split;               // 1: the shared expert's partial sums travel too (second half of a slot)
   const void* x;           // [rows, H] bf16 (dispatch)
   const int32_t* ids;      // [rows, k] global ids
   const float* gates;      // [rows, k]
@@ -102,51 +104,58 @@ struct EpArgs {
   uint64_t timeout_ns;
 };
 
-__device__ __forceinline__ void red_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// One exchange word: 4 data bytes and the call's epoch in a single 8-byte
+// store, so a reader that sees the epoch sees the data (no fence, no flag).
+__device__ __forceinline__ void st_ll(uint2* p, uint32_t v, uint32_t epoch) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v), "r"(epoch) : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ uint2 ld_ll(const uint2* p) {
+  uint2 r;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+  return r;
 }
 
-// Thread 0 of the block waits until every flag in flags[0..n) reaches
-// `target` (or the timeout passes, or another block aborted); returns the
-// block-wide verdict (all threads call it).
-__device__ bool block_wait_flags(const uint32_t* flags, int n, uint32_t target, uint64_t timeout_ns,
-                                 int* err, volatile int* abort) {
-  __shared__ int ok;
+// Poll one word until it carries `epoch` (bounded by the communicator's
+// timeout from t0, or an abort raised elsewhere); returns its data word.
+__device__ __forceinline__ uint32_t wait_ll(const uint2* p, uint32_t epoch, uint64_t t0, uint64_t timeout_ns,
+                                            volatile int* abort, bool& ok) {
+  if (!ok) return 0u;
+  for (uint32_t it = 0;; ++it) {
+    const uint2 v = ld_ll(p);
+    if (v.y == epoch) return v.x;
+    if ((it & 255u) == 255u && (*abort || ds::ptx::globaltimer_ns() - t0 > timeout_ns)) {
+      ok = false;
+      return 0u;
+    }
+  }
+}
+
+__device__ __forceinline__ void report_timeout(int* err, volatile int* abort) {
+  atomicOr(err, kErrTimeout);
+  *abort = 1;
+}
+
+// This block's epoch: its own counter + 1 (every block of every rank runs
+// once per call, so the counters agree across blocks and ranks).
+__device__ __forceinline__ bool block_epoch(char* own, const EpLayout& L, int slot, uint32_t& epoch) {
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_abort;
   if (threadIdx.x == 0) {
-    int good = 1;
-    const uint64_t t0 = ds::ptx::globaltimer_ns();
-    for (int j = 0; j < n && good; ++j) {
-      for (uint32_t it = 0;; ++it) {
-        // wrap-safe "flag >= target"
-        if ((int32_t)(ld_acquire_sys(flags + j) - target) >= 0) break;
-        if ((it & 63u) == 63u) {
-          if (*abort || ds::ptx::globaltimer_ns() - t0 > timeout_ns) {
-            good = 0;
-            break;
-          }
-        }
-        __nanosleep(64);
-      }
-    }
-    if (!good) {
-      atomicOr(err, kErrTimeout);
-      *abort = 1;
-    }
-    ok = good;
+    uint32_t* ctr = reinterpret_cast<uint32_t*>(own + L.ctr) + slot;
+    s_epoch = *ctr + 1;
+    *ctr = s_epoch;
+    s_abort = *reinterpret_cast<volatile int*>(own + L.err + 4);
   }
   __syncthreads();
-  return ok != 0;
+  epoch = s_epoch;
+  return s_abort == 0;
 }
 
-// Block (q, part): push this rank's rows into slot `rank` of rank q's
-// receive area, raise q's flag, wait for q's rows in our own area, rewrite
-// their ids to local ids.
+// Block (q, part): push this rank's rows (x words, global ids, gates) into
+// slot `rank` of rank q's dispatch area, then take q's rows from slot q of
+// our own area into the local buffers the decode kernels read (ids rewritten
+// to local expert ids, -1 where another rank owns the expert).
 __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const __grid_constant__ EpArgs a) {
   ds::ptx::wait_prior_grid();        // x / ids / gates come from the previous kernel (router)
   ds::ptx::launch_dependents();
@@ -154,56 +163,41 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(const __grid_co
   int* err = reinterpret_cast<int*>(own + a.L.err);
   volatile int* abort = err + 1;
   const int q = blockIdx.x / kDispatchBlocks, part = blockIdx.x % kDispatchBlocks;
-  __shared__ uint32_t s_epoch;
-  __shared__ int s_abort;
-  if (threadIdx.x == 0) {
-    uint32_t* ctr = reinterpret_cast<uint32_t*>(own + a.L.ctr) + blockIdx.x;
-    s_epoch = *ctr + 1;
-    *ctr = s_epoch;
-    s_abort = *abort;
-  }
-  __syncthreads();
-  if (s_abort) return;
-  const uint32_t epoch = s_epoch;
+  uint32_t epoch;
+  if (!block_epoch(own, a.L, blockIdx.x, epoch)) return;
   const int b = a.rows, H = a.H, k = a.k;
-  char* dst = a.base[q];
-  {
-    // x rows: b * H bf16 as 16-byte vectors, split over the blocks of this peer
-    const uint4* src = static_cast<const uint4*>(a.x);
-    uint4* to = reinterpret_cast<uint4*>(dst + a.L.recv_x + (size_t)a.rank * b * H * 2);
-    const int nv = b * H / 8;
-    for (int i = part * kEpThreads + threadIdx.x; i < nv; i += kDispatchBlocks * kEpThreads) to[i] = src[i];
-    if (part == 0) {
-      int32_t* ti = reinterpret_cast<int32_t*>(dst + a.L.recv_ids) + (size_t)a.rank * b * k;
-      float* tw = reinterpret_cast<float*>(dst + a.L.recv_w) + (size_t)a.rank * b * k;
-      for (int i = threadIdx.x; i < b * k; i += kEpThreads) {
-        ti[i] = a.ids[i];
-        tw[i] = a.gates[i];
-      }
+  const int nx = b * H / 2, n = nx + 2 * b * k;
+  const uint32_t* xw = static_cast<const uint32_t*>(a.x);
+  const uint32_t* iw = reinterpret_cast<const uint32_t*>(a.ids);
+  const uint32_t* gw = reinterpret_cast<const uint32_t*>(a.gates);
+  uint2* dst = reinterpret_cast<uint2*>(a.base[q] + a.L.ll_g) + (size_t)a.rank * a.L.slot_g;
+  for (int w = part * kEpThreads + threadIdx.x; w < n; w += kDispatchBlocks * kEpThreads) {
+    const uint32_t v = w < nx ? xw[w] : (w < nx + b * k ? iw[w - nx] : gw[w - nx - b * k]);
+    st_ll(dst + w, v, epoch);
+  }
+  const uint2* src = reinterpret_cast<const uint2*>(own + a.L.ll_g) + (size_t)q * a.L.slot_g;
+  uint32_t* rx = reinterpret_cast<uint32_t*>(own + a.L.recv_x) + (size_t)q * nx;
+  int32_t* li = reinterpret_cast<int32_t*>(own + a.L.ids_local) + (size_t)q * b * k;
+  uint32_t* rw = reinterpret_cast<uint32_t*>(own + a.L.recv_w) + (size_t)q * b * k;
+  const uint64_t t0 = ds::ptx::globaltimer_ns();
+  bool ok = true;
+  for (int w = part * kEpThreads + threadIdx.x; w < n; w += kDispatchBlocks * kEpThreads) {
+    const uint32_t v = wait_ll(src + w, epoch, t0, a.timeout_ns, abort, ok);
+    if (w < nx) {
+      rx[w] = v;
+    } else if (w < nx + b * k) {
+      const int32_t e = (int32_t)v;
+      li[w - nx] = (ok && e >= a.first_expert && e < a.first_expert + a.local_experts) ? e - a.first_expert : -1;
+    } else {
+      rw[w - nx - b * k] = v;
     }
   }
-  // every thread's stores precede thread 0's system-scope fence (barrier),
-  // which precedes the flag (release): a peer that acquires the flag sees
-  // the rows
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    red_release_sys(reinterpret_cast<uint32_t*>(dst + a.L.flags_g) + a.rank, 1u);
-  }
-  const uint32_t* flags = reinterpret_cast<const uint32_t*>(own + a.L.flags_g) + q;
-  if (!block_wait_flags(flags, 1, epoch * kDispatchBlocks, a.timeout_ns, err, abort)) return;
-  // slot q arrived: local ids (L2 reads: the rows were written over NVLink)
-  const int32_t* gi = reinterpret_cast<const int32_t*>(own + a.L.recv_ids) + (size_t)q * b * k;
-  int32_t* li = reinterpret_cast<int32_t*>(own + a.L.ids_local) + (size_t)q * b * k;
-  for (int i = part * kEpThreads + threadIdx.x; i < b * k; i += kDispatchBlocks * kEpThreads) {
-    const int32_t e = __ldcg(gi + i);
-    li[i] = (e >= a.first_expert && e < a.first_expert + a.local_experts) ? e - a.first_expert : -1;
-  }
+  if (!ok) report_timeout(err, abort);
 }
 
-// Block (q, part): push the partial rows of rank q's tokens into slot
-// `rank` of q's reduce area, raise q's flag, wait for every rank's slot in
-// our own area, sum the slots in rank order into the bf16 output.
+// Block (q, part): push the partial rows of rank q's tokens (and, split, the
+// shared expert's) into slot `rank` of q's combine area; then every block
+// sums its share of our b * H outputs over the G slots in rank order.
 __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const __grid_constant__ EpArgs a) {
   ds::ptx::wait_prior_grid();        // partial rows come from the decode kernels
   ds::ptx::launch_dependents();
@@ -211,74 +205,37 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(const __grid_con
   int* err = reinterpret_cast<int*>(own + a.L.err);
   volatile int* abort = err + 1;
   const int q = blockIdx.x / kCombineBlocks, part = blockIdx.x % kCombineBlocks;
-  __shared__ uint32_t s_epoch;
-  __shared__ int s_abort;
-  if (threadIdx.x == 0) {
-    uint32_t* ctr = reinterpret_cast<uint32_t*>(own + a.L.ctr) + 64 + blockIdx.x;
-    s_epoch = *ctr + 1;
-    *ctr = s_epoch;
-    s_abort = *abort;
-  }
-  __syncthreads();
-  if (s_abort) return;
-  const uint32_t epoch = s_epoch;
+  uint32_t epoch;
+  if (!block_epoch(own, a.L, 64 + blockIdx.x, epoch)) return;
   const int b = a.rows, H = a.H, G = a.world;
-  const size_t slot_elems = (size_t)b * H;
+  const int ne = b * H;
   {
-    const float4* src = reinterpret_cast<const float4*>(own + a.L.part) + (size_t)q * slot_elems / 4;
-    float4* to = reinterpret_cast<float4*>(a.base[q] + a.L.rbuf) + (size_t)a.rank * slot_elems / 4;
-    const int nv = (int)(slot_elems / 4);
-    for (int i = part * kEpThreads + threadIdx.x; i < nv; i += kCombineBlocks * kEpThreads) to[i] = src[i];
+    const uint32_t* pr = reinterpret_cast<const uint32_t*>(own + a.L.part) + (size_t)q * ne;
+    const uint32_t* ps = reinterpret_cast<const uint32_t*>(own + a.L.part_sh) + (size_t)q * ne;
+    uint2* dst = reinterpret_cast<uint2*>(a.base[q] + a.L.ll_r) + (size_t)a.rank * a.L.slot_r;
+    const int n = a.split ? 2 * ne : ne;
+    for (int w = part * kEpThreads + threadIdx.x; w < n; w += kCombineBlocks * kEpThreads)
+      st_ll(dst + w, w < ne ? pr[w] : ps[w - ne], epoch);
+  }
+  const uint2* src = reinterpret_cast<const uint2*>(own + a.L.ll_r);
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
+  const uint64_t t0 = ds::ptx::globaltimer_ns();
+  bool ok = true;
+  for (int i = blockIdx.x * kEpThreads + threadIdx.x; i < ne; i += gridDim.x * kEpThreads) {
+    float acc = 0.0f;
+    for (int j = 0; j < G; ++j)
+      acc += __uint_as_float(wait_ll(src + (size_t)j * a.L.slot_r + i, epoch, t0, a.timeout_ns, abort, ok));
     if (a.split) {
-      const float4* ssrc = reinterpret_cast<const float4*>(own + a.L.part_sh) + (size_t)q * slot_elems / 4;
-      float4* sto = reinterpret_cast<float4*>(a.base[q] + a.L.rbuf_sh) + (size_t)a.rank * slot_elems / 4;
-      for (int i = part * kEpThreads + threadIdx.x; i < nv; i += kCombineBlocks * kEpThreads) sto[i] = ssrc[i];
+      // the shared expert's sum over the ranks, rounded to bf16 before it is
+      // added, as the unsplit layer does
+      float sh = 0.0f;
+      for (int j = 0; j < G; ++j)
+        sh += __uint_as_float(wait_ll(src + (size_t)j * a.L.slot_r + ne + i, epoch, t0, a.timeout_ns, abort, ok));
+      acc += __bfloat162float(__float2bfloat16_rn(sh));
     }
+    out[i] = __float2bfloat16_rn(acc);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    red_release_sys(reinterpret_cast<uint32_t*>(a.base[q] + a.L.flags_r) + a.rank, 1u);
-  }
-  const uint32_t* flags = reinterpret_cast<const uint32_t*>(own + a.L.flags_r);
-  if (!block_wait_flags(flags, G, epoch * kCombineBlocks, a.timeout_ns, err, abort)) return;
-  // sum: this block's share of the b * H outputs, 4 at a time; routed
-  // partials in rank order, then (split) the shared expert's sum rounded to
-  // bf16 before it is added, as the unsplit layer does
-  const float4* rb = reinterpret_cast<const float4*>(own + a.L.rbuf);
-  const float4* rs = reinterpret_cast<const float4*>(own + a.L.rbuf_sh);
-  const int nv = (int)(slot_elems / 4);
-  uint2* out = static_cast<uint2*>(a.out);
-  for (int i = blockIdx.x * kEpThreads + threadIdx.x; i < nv; i += gridDim.x * kEpThreads) {
-    float4 acc = __ldcg(rb + i);
-    for (int j = 1; j < G; ++j) {
-      const float4 v = __ldcg(rb + (size_t)j * nv + i);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
-    }
-    if (a.split) {
-      float4 sh = __ldcg(rs + i);
-      for (int j = 1; j < G; ++j) {
-        const float4 v = __ldcg(rs + (size_t)j * nv + i);
-        sh.x += v.x;
-        sh.y += v.y;
-        sh.z += v.z;
-        sh.w += v.w;
-      }
-      acc.x += __bfloat162float(__float2bfloat16_rn(sh.x));
-      acc.y += __bfloat162float(__float2bfloat16_rn(sh.y));
-      acc.z += __bfloat162float(__float2bfloat16_rn(sh.z));
-      acc.w += __bfloat162float(__float2bfloat16_rn(sh.w));
-    }
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-    const __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&lo);
-    o.y = *reinterpret_cast<const uint32_t*>(&hi);
-    out[i] = o;
-  }
+  if (!ok) report_timeout(err, abort);
 }
 
 }  // namespace
