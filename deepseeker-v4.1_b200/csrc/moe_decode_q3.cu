@@ -182,6 +182,24 @@ __device__ __forceinline__ float quad_sum(float v) {
   return v;
 }
 
+// bf16 row segment (32 values = four 16-byte words) dot bf16 values (four
+// 16-byte words, read through L1)
+__device__ __forceinline__ float bf16_dot32_bf16(const uint4 (&v)[4], const uint4* xg) {
+  float s = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 xv = __ldg(xg + c);
+    const uint32_t aw[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      s = fmaf(__uint_as_float(aw[k] << 16), __uint_as_float(xw[k] << 16), s);
+      s = fmaf(__uint_as_float(aw[k] & 0xFFFF0000u), __uint_as_float(xw[k] & 0xFFFF0000u), s);
+    }
+  }
+  return s;
+}
+
 // bf16 row segment (32 values = four 16-byte words) dot f32 values xs[0..31]
 __device__ __forceinline__ float bf16_dot32(const uint4 (&v)[4], const float* xs) {
   float s = 0.0f;
@@ -215,21 +233,7 @@ __global__ void __launch_bounds__(kQT, 2) q3_gate_up_kernel(const Q3Args q) {
   const int Is = has_shared ? a.d.shared_inter : 0;
   uint32_t* xpk = reinterpret_cast<uint32_t*>(smem4);                     // [T][G][kPkPad]
   float2* xsx = reinterpret_cast<float2*>(xpk + (size_t)T * G * kPkPad);  // [T][G]
-  float* xsf = reinterpret_cast<float*>(xsx + T * G);                     // [T][padded(H)] (shared expert)
-  const int Hp = padded(H);
   pieces_rows_bf16(static_cast<const __nv_bfloat16*>(a.x), T, H, H, xpk, xsx);
-  if (has_shared) {
-    const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(a.x);
-    for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
-      const int t = i / (H / 8), k = (i % (H / 8)) * 8;
-      const uint4 u = *reinterpret_cast<const uint4*>(x + (size_t)t * H + k);
-      float* d = xsf + t * Hp + pidx(k);
-      *reinterpret_cast<float4*>(d) = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
-                                                  __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
-      *reinterpret_cast<float4*>(d + 4) = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xFFFF0000u),
-                                                      __uint_as_float(u.w << 16), __uint_as_float(u.w & 0xFFFF0000u));
-    }
-  }
   build_slots(a, slots);                         // ends with __syncthreads
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 3;
@@ -307,9 +311,10 @@ __global__ void __launch_bounds__(kQT, 2) q3_gate_up_kernel(const Q3Args q) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           if (t >= T) continue;
-          const float* xs = xsf + t * Hp + pidx(32 * seg);
-          acc1[t] += bf16_dot32(v1, xs);
-          acc3[t] += bf16_dot32(v3, xs);
+          const uint4* xg = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.x) + (size_t)t * H) +
+                            seg * 4;
+          acc1[t] += bf16_dot32_bf16(v1, xg);
+          acc3[t] += bf16_dot32_bf16(v3, xg);
         }
       }
     }
@@ -555,8 +560,7 @@ Q3Layout q3_layout(const DsMoeDesc& d, int T) {
 
 size_t smem_gate_up(const DsMoeDesc& d, int T) {
   const int G = d.hidden / 64;
-  const size_t pk = (size_t)T * G * kPkPad * 4 + (size_t)T * G * sizeof(float2);
-  return pk + (d.shared_w1 ? (size_t)T * padded(d.hidden) * 4 : 0);
+  return (size_t)T * G * kPkPad * 4 + (size_t)T * G * sizeof(float2);
 }
 
 size_t smem_down(const DsMoeDesc& d, int T) {

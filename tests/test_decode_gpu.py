@@ -127,7 +127,7 @@ def test_config1_single_expert_f32(cuda):
     assert rel_l2(out, ref) < 1e-5
 
 
-@pytest.mark.parametrize("fmt,T", [("fp4", 1), ("q3", 1), ("q3", 4)])
+@pytest.mark.parametrize("fmt,T", [("fp4", 1), ("q3", 1), ("q3", 4), ("q3", 8)])
 def test_config2_3_full_layer(fmt, T, cuda):
     """BASELINE configs 2/3: hidden 4096, 256 experts (inter 2048), top-8 softmax,
     bf16 shared expert, bf16 activations; all experts resident."""
