@@ -38,9 +38,27 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
-# stdout carries the one JSON line: NCCL's messages (when NCCL_DEBUG is set)
-# go to stderr
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
+
+def init_nccl(dev, seconds: int):
+    """torch.distributed over NCCL for this rank's device, communicator built
+    eagerly; NCCL's start-up banner is written to stdout by the library, so
+    fd 1 points at stderr meanwhile (stdout carries the one JSON line)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    sys.stdout.flush()
+    saved = os.dup(1)
+    try:
+        os.dup2(2, 1)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=seconds), device_id=dev)
+        dist.barrier()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+    return dist
 sys.path.insert(0, str(ROOT / "deepseeker-v4.1_b200"))
 sys.path.insert(0, str(ROOT))
 
@@ -256,7 +274,7 @@ def run_ep(args) -> dict:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    init_nccl(dev, 120)
     fmt = "q3" if args.config == "c3" else "fp4"
     El = E // world
     L = args.layers
@@ -492,7 +510,7 @@ def run_stack(args) -> dict:
     dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        init_nccl(dev, 300)
     NL = args.stack_layers
     b = args.batch
     El = E // world
@@ -724,7 +742,7 @@ def run_grouped(args) -> dict:
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        init_nccl(dev, 120)
     T = C4_TOKENS
     layer = synthetic.make_layer("fp4", H, I, E, seed=1000 * (rank + 1), shared_inter=None, std=0.02, device=dev)
     ffn = grouped.GroupedFFN(layer, K_TOP)
@@ -873,7 +891,7 @@ def run_decode(args) -> dict:
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        init_nccl(dev, 120)
 
     fmt = "q3" if args.config == "c3" else "fp4"
     tokens = args.batch
