@@ -1061,7 +1061,7 @@ def run_decode(args) -> dict:
     if rank == 0:
         pk, kind = peaks()
         achieved = step_bytes / (dec_ms * 1e-3) / 1e9
-        traffic = ncu_traffic(f"decode_{fmt}_c2") if tokens == 1 else None
+        traffic = ncu_traffic(f"decode_{fmt}_{args.config}") if tokens == 1 else None
         result = {
             "metric": METRIC,
             "value": round(world * tokens * args.steps / (ms * 1e-3), 2),
