@@ -293,7 +293,8 @@ def run_ep(args) -> dict:
         if os.environ.get("DEEPSEEKER_BENCH_NO_GRAPH") != "1":
             stage_x = torch.zeros(L, b, H, dtype=torch.bfloat16, device=dev)
             stage_l = torch.zeros(L, b, E, dtype=torch.float32, device=dev)
-            graphs = [ep.PeerDecodeGraph(pl, x=stage_x[l], logits=stage_l[l]) for l, pl in enumerate(eps)]
+            graphs = [ep.PeerDecodeGraph(pl, x=stage_x[l], logits=stage_l[l], host_io=True)
+                      for l, pl in enumerate(eps)]
     else:
         eps = [ep.gpu_layer(layer, E, K_TOP) for layer in layers]
     # graph mode: the L layers back to back in one CUDA graph (no collective
@@ -400,10 +401,12 @@ def run_ep(args) -> dict:
 
     def e2e_step(s_):
         if graphs is not None:
+            # host in -> one graph launch (copies, router, exchange, decode) -> host out
             gr = graphs[s_ % L]
-            gr.x.copy_(pin_x[s_], non_blocking=True)
-            gr.logits.copy_(pin_l[s_], non_blocking=True)
-            out = gr.replay()
+            gr.x_host.copy_(pin_x[s_])
+            gr.logits_host.copy_(pin_l[s_])
+            pin_o.copy_(gr.replay_host())
+            return
         else:
             dx.copy_(pin_x[s_], non_blocking=True)
             dl.copy_(pin_l[s_], non_blocking=True)
@@ -743,7 +746,7 @@ def run_grouped(args) -> dict:
 
         import torch.distributed as dist
         init_nccl(dev, 120)
-    T = C4_TOKENS
+    T = args.tokens or C4_TOKENS
     layer = synthetic.make_layer("fp4", H, I, E, seed=1000 * (rank + 1), shared_inter=None, std=0.02, device=dev)
     ffn = grouped.GroupedFFN(layer, K_TOP)
     R = 4  # distinct routings / inputs rotated
@@ -850,14 +853,14 @@ def run_grouped(args) -> dict:
             "vs_baseline": None,
             "dtype": "fp4-e2m1 weights x e4m3 activation pieces (bf16-exact x, ~14-bit h), f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights quantised on device; Zipf(1.1) top-8 routing)",
-            "config": {"workload": "BASELINE config 4: batched grouped expert FFN, 2048 tokens, hidden 4096, "
+            "config": {"workload": f"BASELINE config 4: batched grouped expert FFN, {T} tokens, hidden 4096, "
                                    "256 FP4 experts inter 2048, top-8 Zipf(1.1), bf16 out",
                        "tokens_per_step": T, "pairs_per_step": T * K_TOP, "experts_touched": touched,
                        "l2": f"each step streams {step_bytes / 1e9:.2f} GB of expert weights (> 126 MB L2)",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "tokens_per_s": round(world * T * args.steps / (ms * 1e-3), 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": ncu_traffic("grouped_fp4_c4"),
+                         "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": ncu_traffic("grouped_fp4_c4") if T == C4_TOKENS else None,
                          "kernel": "ds_grouped_ffn: align + xquant + gemm<gate/up> + gemm<down> + combine",
                          "bytes_per_launch": int(step_bytes), "peak_kind": kind},
             "tensor": {"achieved_tflops": round(flops / (step_ms * 1e-3) / 1e12, 1),
@@ -922,7 +925,7 @@ def run_decode(args) -> dict:
     use_graph = os.environ.get("DEEPSEEKER_BENCH_NO_GRAPH") != "1"
     stage_x = torch.zeros(L, tokens, H, dtype=torch.bfloat16, device=dev)
     stage_l = torch.zeros(L, tokens, E, dtype=torch.float32, device=dev)
-    graphs = [moe.DecodeGraph(layer, tokens, K_TOP, dev, x=stage_x[l], logits=stage_l[l])
+    graphs = [moe.DecodeGraph(layer, tokens, K_TOP, dev, x=stage_x[l], logits=stage_l[l], host_io=True)
               for l, layer in enumerate(layers)] if use_graph else None
     chain = moe.GraphChain(graphs, x=stage_x, logits=stage_l) \
         if use_graph and os.environ.get("DEEPSEEKER_BENCH_NO_CHAIN") != "1" else None
@@ -1020,10 +1023,12 @@ def run_decode(args) -> dict:
 
     def e2e_step(s):
         if use_graph:
+            # host in -> one graph launch (H2D copies, router, decode, D2H copy) -> host out
             gr = graphs[s % L]
-            gr.x.copy_(pin_x[s], non_blocking=True)
-            gr.logits.copy_(pin_l[s], non_blocking=True)
-            pin_o[s].copy_(gr.replay(), non_blocking=True)
+            gr.x_host.copy_(pin_x[s])
+            gr.logits_host.copy_(pin_l[s])
+            pin_o[s].copy_(gr.replay_host())
+            return
         else:
             dx.copy_(pin_x[s], non_blocking=True)
             dl.copy_(pin_l[s], non_blocking=True)
@@ -1115,6 +1120,7 @@ def main() -> int:
     ap.add_argument("--stack-layers", type=int, default=40, help="config 5: layers in the stack (half FP4, half q3)")
     ap.add_argument("--layers", type=int, default=8, help="distinct resident layers rotated (L2-cold)")
     ap.add_argument("--batch", type=int, default=1, help="decode tokens per GPU per step (N > 1)")
+    ap.add_argument("--tokens", type=int, default=0, help="config 4: tokens per step (default 2048)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="profiling runs: no time-based warm-up, no e2e / CPU-baseline legs")

@@ -439,7 +439,8 @@ class PeerDecodeGraph:
     the library's own kernels, so the graph holds no collective call; every
     rank must replay its graphs in the same order."""
 
-    def __init__(self, layer: PeerDecodeLayer, x: torch.Tensor | None = None, logits: torch.Tensor | None = None):
+    def __init__(self, layer: PeerDecodeLayer, x: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+                 host_io: bool = False):
         from . import moe
 
         self.layer = layer
@@ -448,6 +449,11 @@ class PeerDecodeGraph:
         dev = layer.comm.device
         self.x = moe._static_input(x, (b, H), torch.bfloat16, dev, "x")
         self.logits = moe._static_input(logits, (b, E), torch.float32, dev, "logits")
+        self.host_io = host_io
+        if host_io:
+            self.x_host = torch.zeros(b, H, dtype=torch.bfloat16).pin_memory()
+            self.logits_host = torch.zeros(b, E, dtype=torch.float32).pin_memory()
+            self.out_host = torch.zeros(b, H, dtype=torch.bfloat16).pin_memory()
         self.w = torch.empty(b, k, dtype=torch.float32, device=dev)
         self.ids = torch.empty(b, k, dtype=torch.int32, device=dev)
         self.out = torch.empty(b, H, dtype=torch.bfloat16, device=dev)
@@ -457,6 +463,13 @@ class PeerDecodeGraph:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._step()
+        if host_io:
+            self.graph_host = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph_host):
+                self.x.copy_(self.x_host, non_blocking=True)
+                self.logits.copy_(self.logits_host, non_blocking=True)
+                self._step()
+                self.out_host.copy_(self.out, non_blocking=True)
 
     def _step(self) -> None:
         self._route()
@@ -465,3 +478,14 @@ class PeerDecodeGraph:
     def replay(self) -> torch.Tensor:
         self.graph.replay()
         return self.out
+
+    def replay_host(self) -> torch.Tensor:
+        """x_host / logits_host -> out_host in one graph launch (host_io=True),
+        waited for; returns ``out_host``."""
+        from . import moe
+
+        if not self.host_io:
+            raise ValueError("PeerDecodeGraph was built without host_io")
+        self.graph_host.replay()
+        moe.wait_stream(self.x.device)
+        return self.out_host

@@ -322,6 +322,15 @@ def _static_input(t: torch.Tensor | None, shape, dtype, device, name: str) -> to
     return t
 
 
+def wait_stream(device) -> None:
+    """Wait for the current stream by polling an event (a decode step is tens
+    of microseconds: a blocking synchronisation adds its own wake-up time)."""
+    ev = torch.cuda.Event()
+    ev.record(torch.cuda.current_stream(device))
+    while not ev.query():
+        pass
+
+
 class DecodeGraph:
     """Softmax top-k routing + ``moe_decode`` for one resident layer and a fixed
     token count, captured once into a CUDA graph over static device buffers.
@@ -333,14 +342,23 @@ class DecodeGraph:
     """
 
     def __init__(self, weights: MoEWeights, tokens: int, top_k: int, device: torch.device | str | None = None,
-                 x: torch.Tensor | None = None, logits: torch.Tensor | None = None):
+                 x: torch.Tensor | None = None, logits: torch.Tensor | None = None, host_io: bool = False):
         """``x`` [tokens, H] bf16 / ``logits`` [tokens, E] f32: input buffers to
-        read (e.g. rows of a ``GraphChain`` staging tensor); allocated here if None."""
+        read (e.g. rows of a ``GraphChain`` staging tensor); allocated here if None.
+
+        ``host_io``: pinned host buffers ``x_host``, ``logits_host`` and
+        ``out_host``, copied in and out inside the graph: ``replay_host()`` is
+        then one launch per token step, host data in, host data out."""
         device = torch.device(device) if device is not None else weights.w1.data.device
         self.weights, self.tokens, self.top_k = weights, tokens, top_k
         H, E = weights.hidden, weights.n_experts
         self.x = _static_input(x, (tokens, H), torch.bfloat16, device, "x")
         self.logits = _static_input(logits, (tokens, E), torch.float32, device, "logits")
+        self.host_io = host_io
+        if host_io:
+            self.x_host = torch.zeros(tokens, H, dtype=torch.bfloat16).pin_memory()
+            self.logits_host = torch.zeros(tokens, E, dtype=torch.float32).pin_memory()
+            self.out_host = torch.zeros(tokens, H, dtype=torch.bfloat16).pin_memory()
         self.w = torch.empty(tokens, top_k, dtype=torch.float32, device=device)
         self.ids = torch.empty(tokens, top_k, dtype=torch.int32, device=device)
         self.out = torch.empty(tokens, H, dtype=torch.bfloat16, device=device)
@@ -350,6 +368,13 @@ class DecodeGraph:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._step()
+        if host_io:
+            self.graph_host = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph_host):
+                self.x.copy_(self.x_host, non_blocking=True)
+                self.logits.copy_(self.logits_host, non_blocking=True)
+                self._step()
+                self.out_host.copy_(self.out, non_blocking=True)
 
     def _step(self) -> None:
         route_softmax_topk(self.logits, self.top_k, out=(self.w, self.ids))
@@ -358,6 +383,15 @@ class DecodeGraph:
     def replay(self) -> torch.Tensor:
         self.graph.replay()
         return self.out
+
+    def replay_host(self) -> torch.Tensor:
+        """x_host / logits_host -> out_host in one graph launch (host_io=True);
+        synchronises the stream and returns ``out_host``."""
+        if not self.host_io:
+            raise ValueError("DecodeGraph was built without host_io")
+        self.graph_host.replay()
+        wait_stream(self.x.device)
+        return self.out_host
 
 
 class GraphChain:

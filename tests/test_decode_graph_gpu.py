@@ -63,3 +63,18 @@ def test_graph_chain_rejects_foreign_buffers(cuda):
     with pytest.raises(ValueError):
         moe.GraphChain([g], x=torch.zeros(1, 1, 1024, dtype=torch.bfloat16, device=cuda),
                        logits=torch.zeros(1, 1, 16, device=cuda))
+
+
+def test_graph_host_io_matches_eager(cuda):
+    """host_io: pinned host in, one graph launch (copies inside), pinned host out."""
+    layer = synthetic.make_layer("fp4", 4096, 2048, 64, seed=35, shared_inter=2048, device=cuda).prepare_tc()
+    g = moe.DecodeGraph(layer, 1, 8, host_io=True)
+    for step in range(3):
+        x = torch.randn(1, 4096).to(torch.bfloat16)
+        logits = torch.randn(1, 64)
+        g.x_host.copy_(x)
+        g.logits_host.copy_(logits)
+        got = g.replay_host().clone()
+        w, ids = moe.route_softmax_topk(logits.to(cuda), 8)
+        ref = moe.moe_decode(x.to(cuda), layer, ids, w).cpu()
+        assert torch.equal(got, ref), step

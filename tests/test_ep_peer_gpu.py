@@ -84,6 +84,18 @@ def test_peer_graph_replays_match_eager(cuda):
         assert torch.equal(out_g, ref), (step, rel_l2(out_g, ref))
     assert comm.status() == 0
     del gr
+    # host in / host out through one graph launch
+    gh = ep.PeerDecodeGraph(pl, host_io=True)
+    xs = torch.randn(2, layer.hidden).to(torch.bfloat16)
+    lg = torch.randn(2, E)
+    gh.x_host.copy_(xs)
+    gh.logits_host.copy_(lg)
+    got = gh.replay_host().clone()
+    wr, ir = moe.route_softmax_topk(lg.to(x.device), K)
+    ref = moe.moe_decode(xs.to(x.device), layer, ir, wr).cpu()
+    assert torch.equal(got, ref), rel_l2(got, ref)
+    assert comm.status() == 0
+    del gh
     comm.close()
 
 
