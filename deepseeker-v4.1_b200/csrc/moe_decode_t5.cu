@@ -52,8 +52,10 @@ namespace {
 
 using namespace ds::ptx;
 
-constexpr int kThreads = 320;                  // 10 warps
+constexpr int kThreads = 352;                  // 11 warps
 constexpr int kMaxStages = 8;
+constexpr int kAcc = 4;                        // accumulator buffers (64 tensor-memory columns each)
+static_assert(64 * kAcc + 32 * kMaxStages <= 512, "accumulators + scale ring exceed tensor memory");
 constexpr int kASlot = 32768;                  // 2 chunks x 128 rows x 128 B (FP4 K = 512 packed, or bf16 K = 128)
 constexpr int kSfSlot = 4096;                  // 4 weight atoms + 4 activation atoms
 constexpr int kAtom = 512;
@@ -181,33 +183,54 @@ __device__ __forceinline__ float scale_of(int sfb) { return __uint_as_float((uin
 __device__ __forceinline__ float inv_scale_of(int sfb) { return __uint_as_float((uint32_t)(254 - sfb) << 23); }
 __device__ __forceinline__ int atom_off(int r, int kb) { return (r & 31) * 16 + (r >> 5) * 4 + kb; }
 
-// ------------------------------------------------------------------ fused tails (one warp, 32 rows)
-// The partial sums of a row are independent loads; they are issued in
-// batches so that many are in flight per lane.
+// ------------------------------------------------------------------ tails (one warp, 32 rows, kT tokens)
+// Partial sums live in L2 ([...][rows][kT] f32); they are read with .cg loads
+// in batches so that up to 32 are in flight per lane (one L2 round trip for
+// the usual slice counts), and summed in slice order starting from 0.
+
+// sa = sum_j a[j * stride + 0..kT), sb likewise, j < n.
+template <int kT>
+__device__ __forceinline__ void sum_two(const float* a, const float* b, size_t stride, int n, float (&sa)[kT],
+                                        float (&sb)[kT]) {
+  constexpr int kC = kT >= 16 ? 1 : 16 / kT;
+#pragma unroll
+  for (int t = 0; t < kT; ++t) sa[t] = sb[t] = 0.0f;
+  for (int j0 = 0; j0 < n; j0 += kC) {
+    float va[kC][kT], vb[kC][kT];
+#pragma unroll
+    for (int c = 0; c < kC; ++c)
+#pragma unroll
+      for (int t = 0; t < kT; ++t) {
+        const bool ok = j0 + c < n;
+        va[c][t] = ok ? __ldcg(a + (size_t)(j0 + c) * stride + t) : 0.0f;
+        vb[c][t] = ok ? __ldcg(b + (size_t)(j0 + c) * stride + t) : 0.0f;
+      }
+#pragma unroll
+    for (int c = 0; c < kC; ++c)
+      if (j0 + c < n) {
+#pragma unroll
+        for (int t = 0; t < kT; ++t) {
+          sa[t] += va[c][t];
+          sb[t] += vb[c][t];
+        }
+      }
+  }
+}
 
 // h of one routed slot for rows r0 + lane of I (one 32-row block) as e2m1
 // pieces: sums the K slices of the gate/up partials, SiLU/clamp, route gate.
+template <int kT>
 __device__ void tail_h_routed(const T5Params& p, int slot, int r0, int lane) {
-  const int I = p.rows_r, T = p.T, KP = p.KP_r;
+  const int I = p.rows_r, KP = p.KP_r;
   const int i = r0 + lane;
+  float g[kT], u[kT];
+  sum_two<kT>(p.part + (((size_t)slot * 2 + 0) * KP * I + i) * kT, p.part + (((size_t)slot * 2 + 1) * KP * I + i) * kT,
+              (size_t)I * kT, KP, g, u);
   uint8_t* hq = p.hq + (size_t)slot * kPieceRows * (I / 2);
   uint8_t* sf = p.sfh + ((size_t)slot * (I / 128) + r0 / 128) * kAtom;
-  const float* pg = p.part + (((size_t)slot * 2 + 0) * KP * I + i) * T;
-  const float* pu = p.part + (((size_t)slot * 2 + 1) * KP * I + i) * T;
-  for (int t = 0; t < T; ++t) {
-    float gs[8], us[8];
-#pragma unroll
-    for (int kp = 0; kp < 8; ++kp) {
-      gs[kp] = kp < KP ? __ldcg(pg + (size_t)kp * I * T + t) : 0.0f;
-      us[kp] = kp < KP ? __ldcg(pu + (size_t)kp * I * T + t) : 0.0f;
-    }
-    float g = 0.0f, u = 0.0f;
-#pragma unroll
-    for (int kp = 0; kp < 8; ++kp) {
-      g += gs[kp];
-      u += us[kp];
-    }
-    float r = silu_glu(g, u, p.limit) * p.slot_gate[slot * kMaxT + t];
+#pragma unroll 1
+  for (int t = 0; t < kT; ++t) {
+    float r = silu_glu(g[t], u[t], p.limit) * p.slot_gate[slot * kMaxT + t];
 #pragma unroll 1
     for (int pc = 0; pc < kPieces; ++pc) {
       float am = fabsf(r);
@@ -227,25 +250,15 @@ __device__ void tail_h_routed(const T5Params& p, int slot, int r0, int lane) {
 }
 
 // Shared-expert h for rows r0 + lane of Is as bf16 hi/lo (rows 2t, 2t+1).
+template <int kT>
 __device__ void tail_h_shared(const T5Params& p, int r0, int lane) {
-  const int Is = p.rows_s, T = p.T, KP = p.KP_s;
+  const int Is = p.rows_s, KP = p.KP_s;
   const int i = r0 + lane;
-  for (int t = 0; t < T; ++t) {
-    float g = 0.0f, u = 0.0f;
-    for (int k0 = 0; k0 < KP; k0 += 8) {
-      float gs[8], us[8];
+  float g[kT], u[kT];
+  sum_two<kT>(p.part_sh + (size_t)i * kT, p.part_sh + ((size_t)KP * Is + i) * kT, (size_t)Is * kT, KP, g, u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        gs[k] = k0 + k < KP ? __ldcg(p.part_sh + (((size_t)0 * KP + k0 + k) * Is + i) * T + t) : 0.0f;
-        us[k] = k0 + k < KP ? __ldcg(p.part_sh + (((size_t)1 * KP + k0 + k) * Is + i) * T + t) : 0.0f;
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        g += gs[k];
-        u += us[k];
-      }
-    }
-    const float h = silu_glu(g, u, p.limit);
+  for (int t = 0; t < kT; ++t) {
+    const float h = silu_glu(g[t], u[t], p.limit);
     const __nv_bfloat16 hi = __float2bfloat16_rn(h);
     p.hb[(size_t)(2 * t) * Is + i] = hi;
     p.hb[(size_t)(2 * t + 1) * Is + i] = __float2bfloat16_rn(h - __bfloat162float(hi));
@@ -253,47 +266,72 @@ __device__ void tail_h_shared(const T5Params& p, int r0, int lane) {
 }
 
 // Output rows r0 + lane of H: routed slots in ascending expert order (each
-// slot's K slices in order), then the shared expert rounded to bf16.
+// slot's K slices summed in order, then added), then the shared expert's K
+// slices summed and rounded to bf16.
+template <int kT>
 __device__ void tail_combine(const T5Params& p, int r0, int lane) {
-  const int H = p.rows_r, T = p.T, ns = *p.n_slots, KP = p.KP_r;
+  const int H = p.rows_r, KP = p.KP_r, KPs = p.n_sh_items ? p.KP_s : 0;
   const int h = r0 + lane;
-  for (int t = 0; t < T; ++t) {
-    float acc = 0.0f;
-    for (int s0 = 0; s0 < ns; s0 += 4) {
-      float e[4][4];
+  const int nr = *p.n_slots * KP, n = nr + KPs;
+  // partial j: routed (slot j / KP, K slice j % KP) for j < nr, then the
+  // shared K slices; both arrays have H * kT floats per slice
+  const size_t stride = (size_t)H * kT;
+  const float* pr = p.part + (size_t)h * kT;
+  const float* ps = p.part_sh + (size_t)h * kT;
+  constexpr int kC = kT >= 32 ? 1 : 32 / kT;
+  float acc[kT], es[kT], sh[kT];
 #pragma unroll
-      for (int ds = 0; ds < 4; ++ds)
+  for (int t = 0; t < kT; ++t) acc[t] = es[t] = sh[t] = 0.0f;
+  int kp = 0;
+  for (int j0 = 0; j0 < n; j0 += kC) {
+    float v[kC][kT];
 #pragma unroll
-        for (int kp = 0; kp < 4; ++kp)
-          e[ds][kp] = (s0 + ds < ns && kp < KP)
-                          ? __ldcg(p.part + (((size_t)(s0 + ds) * KP + kp) * H + h) * T + t)
-                          : 0.0f;
+    for (int c = 0; c < kC; ++c) {
+      const int j = j0 + c;
+      const float* src = j < nr ? pr + (size_t)j * stride : ps + (size_t)(j - nr) * stride;
 #pragma unroll
-      for (int ds = 0; ds < 4; ++ds) {
-        float es = 0.0f;
-#pragma unroll
-        for (int kp = 0; kp < 4; ++kp) es += e[ds][kp];
-        if (s0 + ds < ns) acc += es;
-      }
-      for (int kp = 4; kp < KP; ++kp)   // K slices beyond 4 (inter > 4096): rare, added in order
-        for (int ds = 0; ds < 4 && s0 + ds < ns; ++ds) acc += __ldcg(p.part + (((size_t)(s0 + ds) * KP + kp) * H + h) * T + t);
+      for (int t = 0; t < kT; ++t) v[c][t] = j < n ? __ldcg(src + t) : 0.0f;
     }
-    if (p.n_sh_items && (p.out_sh != nullptr || (t >= p.sh_t0 && t < p.sh_t1))) {
-      float sh = 0.0f;
-      for (int k0 = 0; k0 < p.KP_s; k0 += 8) {
-        float v[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = k0 + k < p.KP_s ? __ldcg(p.part_sh + ((size_t)(k0 + k) * H + h) * T + t) : 0.0f;
+    for (int c = 0; c < kC; ++c) {
+      const int j = j0 + c;
+      if (j < nr) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) sh += v[k];
+        for (int t = 0; t < kT; ++t) es[t] = (kp == 0 ? 0.0f : es[t]) + v[c][t];
+        if (++kp == KP) {
+          kp = 0;
+#pragma unroll
+          for (int t = 0; t < kT; ++t) acc[t] += es[t];
+        }
+      } else if (j < n) {
+#pragma unroll
+        for (int t = 0; t < kT; ++t) sh[t] += v[c][t];
       }
-      if (p.out_sh != nullptr) p.out_sh[(size_t)t * H + h] = sh;
-      else acc += __bfloat162float(__float2bfloat16_rn(sh));
     }
-    if (p.out_f32) static_cast<float*>(p.out)[(size_t)t * H + h] = acc;
-    else static_cast<__nv_bfloat16*>(p.out)[(size_t)t * H + h] = __float2bfloat16_rn(acc);
+  }
+#pragma unroll
+  for (int t = 0; t < kT; ++t) {
+    if (KPs && (p.out_sh != nullptr || (t >= p.sh_t0 && t < p.sh_t1))) {
+      if (p.out_sh != nullptr) p.out_sh[(size_t)t * H + h] = sh[t];
+      else acc[t] += __bfloat162float(__float2bfloat16_rn(sh[t]));
+    }
+    if (p.out_f32) static_cast<float*>(p.out)[(size_t)t * H + h] = acc[t];
+    else static_cast<__nv_bfloat16*>(p.out)[(size_t)t * H + h] = __float2bfloat16_rn(acc[t]);
   }
 }
+
+// CALL(K) with K = the token count as a compile-time constant (1..8).
+#define DS_T5_FOR_T(T, CALL)  \
+  switch (T) {                \
+    case 1: CALL(1); break;   \
+    case 2: CALL(2); break;   \
+    case 3: CALL(3); break;   \
+    case 4: CALL(4); break;   \
+    case 5: CALL(5); break;   \
+    case 6: CALL(6); break;   \
+    case 7: CALL(7); break;   \
+    default: CALL(8); break;  \
+  }
 
 // ------------------------------------------------------------------ gate/up and down GEMM kernel
 
@@ -301,8 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* ring = smem;                          // nst x [A 32 KB][B b_slot][SF 4 KB]
-  __shared__ __align__(8) uint64_t full[kMaxStages], staged[kMaxStages], empty[kMaxStages], accfull[2], accempty[2],
-      done;
+  __shared__ __align__(8) uint64_t full[kMaxStages], staged[kMaxStages], empty[kMaxStages], accfull[kAcc], accempty[kAcc],
+      done[2];
   const int S = p.nst;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -314,19 +352,20 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
       mbar_init(&staged[s], 4);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAcc; ++b) {
       mbar_init(&accfull[b], 1);
       mbar_init(&accempty[b], 4);
     }
-    mbar_init(&done, 1);
+    mbar_init(&done[0], 1);
+    mbar_init(&done[1], 1);
     abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) tc5::alloc(&tmem_base, 512);
   __syncthreads();
   tc5::fence_after();
-  const uint32_t tb = tmem_base;                 // D buffers at columns 0 and 64; scale ring from 128
-  const uint32_t tsf0 = tb + 128;                // 32 columns per stage
+  const uint32_t tb = tmem_base;                 // D buffers at columns 0, 64, 128, 192; scale ring from 256
+  const uint32_t tsf0 = tb + 64 * kAcc;          // 32 columns per stage
   volatile int* abort = &abort_flag;
   // the down phase consumes what the gate/up launch produced; its producer
   // first prefetches weight tiles, every other role waits right away
@@ -400,12 +439,19 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
     drain:
       for (int j = g - S < 0 ? 0 : g - S; j < g; ++j) mbar_wait_bounded(&full[j % S], (j / S) & 1, 200000000ull);
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == 10) {
+    // ---------------------------------------------------------------- MMA issuers
+    // Two threads issue the MMAs, alternating items (warp 1: even local
+    // items, warp 10: odd), so that one thread's waits and issue latency
+    // overlap the other's MMAs in the tensor pipe.  Each item has its own
+    // accumulator buffer (item % kAcc) and ring stages g = item * 2 + j.  A
+    // thread starts waiting on stage g only after it has seen stage g - 3
+    // staged (its previous item), and the stagers stage in ring order, so
+    // with S >= 3 the slot's previous phase (stage g - S) has completed and
+    // the parity wait cannot alias.
     if (lane == 0) {
-      // ring position kept incrementally (no division in the issue loop);
-      // the stagers arrive on staged[s] only after observing full[s]
-      int s = 0, ph = 0, li = 0;
+      const int par = warp == 1 ? 0 : 1;
+      int li = 0;
       const uint32_t ring0 = smem_u32(ring);
       const uint32_t idesc_sh = tc5::idesc_bf16(16);
       uint32_t idesc_r[2];
@@ -417,11 +463,13 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
           know_routed();
           if (item >= n_items) break;
         }
+        if ((li & 1) != par) continue;
         const bool shared = item < p.n_sh_items;
-        const int b = li & 1;
-        if (li >= 2 && !wait_or_abort(&accempty[b], ((li >> 1) - 1) & 1, abort, p.err)) break;
+        const int b = li % kAcc;
+        if (li >= kAcc && !wait_or_abort(&accempty[b], ((li / kAcc) - 1) & 1, abort, p.err)) break;
         const uint32_t dacc = tb + b * 64;
         for (int j = 0; j < kStagesPerItem; ++j) {
+          const int g = li * kStagesPerItem + j, s = g % S, ph = (g / S) & 1;
           if (!wait_or_abort(&staged[s], ph, abort, p.err)) goto mma_out;
           tc5::fence_after();
           const uint32_t sa = ring0 + s * p.stage_bytes, sb = sa + kASlot;
@@ -444,16 +492,12 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
                               tsf + 4 * (2 * c + (kk >> 1)), tsf + 16 + 4 * (2 * c + (kk >> 1)), (j | c | kk) != 0);
           }
           tc5::commit(&empty[s]);
-          if (++s == S) {
-            s = 0;
-            ph ^= 1;
-          }
         }
         tc5::commit(&accfull[b]);
       }
     mma_out:
-      tc5::commit(&done);
-      mbar_wait_bounded(&done, 0, 1000000000ull);
+      tc5::commit(&done[par]);
+      mbar_wait_bounded(&done[par], 0, 1000000000ull);
     }
   } else if (warp < 6) {
     // ---------------------------------------------------------------- stagers
@@ -487,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
       }
     }
   st_out:;
-  } else {
+  } else if (warp < 10) {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;
     int li = 0;
@@ -497,8 +541,8 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
         if (item >= n_items) break;
       }
       const Item it = decode_item(p, item);
-      const int b = li & 1;
-      if (!warp_wait(&accfull[b], (li >> 1) & 1, abort, p.err)) break;
+      const int b = li % kAcc;
+      if (!warp_wait(&accfull[b], (li / kAcc) & 1, abort, p.err)) break;
       tc5::fence_after();
       const uint32_t dacc = tc5::lane_quarter(tb + b * 64, q);
       float v[48];
@@ -539,23 +583,36 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
 }
 
 // h between the two GEMM launches: one CTA per 128-row tile of one slot
-// (the last grid row is the shared expert), one row per thread.
+// (the last grid row is the shared expert), one row per thread.  The down
+// launch may be scheduled right away: it waits for this grid before it reads
+// h, and its producer streams weights meanwhile.
 __global__ void __launch_bounds__(128) t5_h_kernel(const __grid_constant__ T5Params p) {
-  wait_prior_grid();
   launch_dependents();
+  wait_prior_grid();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * 128 + warp * 32;
   if (blockIdx.y == gridDim.y - 1) {
-    if (p.n_sh_items && r0 < p.rows_s) tail_h_shared(p, r0, lane);
+    if (p.n_sh_items && r0 < p.rows_s) {
+#define DS_T5_CALL(K) tail_h_shared<K>(p, r0, lane)
+      DS_T5_FOR_T(p.T, DS_T5_CALL)
+#undef DS_T5_CALL
+    }
   } else if ((int)blockIdx.y < *p.n_slots && r0 < p.rows_r) {
-    tail_h_routed(p, blockIdx.y, r0, lane);
+    const int slot = blockIdx.y;
+#define DS_T5_CALL(K) tail_h_routed<K>(p, slot, r0, lane)
+    DS_T5_FOR_T(p.T, DS_T5_CALL)
+#undef DS_T5_CALL
   }
 }
 
 // Output rows after the down launch: one row per thread.
 __global__ void __launch_bounds__(128) t5_combine_kernel(const __grid_constant__ T5Params p) {
+  launch_dependents();
   wait_prior_grid();
-  tail_combine(p, blockIdx.x * 128 + (threadIdx.x >> 5) * 32, threadIdx.x & 31);
+  const int r0 = blockIdx.x * 128 + (threadIdx.x >> 5) * 32, lane = threadIdx.x & 31;
+#define DS_T5_CALL(K) tail_combine<K>(p, r0, lane)
+  DS_T5_FOR_T(p.T, DS_T5_CALL)
+#undef DS_T5_CALL
 }
 
 // ------------------------------------------------------------------ prep: slots, gates, x pieces
@@ -883,6 +940,7 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   p.b_slot = std::max(4096, NB * 2 * 128);
   p.stage_bytes = kASlot + p.b_slot + kSfSlot;
   p.nst = std::min<int>(kMaxStages, (int)((kSmemMax - 1024) / p.stage_bytes));
+  DS_REQUIRE(p.nst >= 3, DS_ENOTSUP, "moe_decode: ring of %d stages (needs 3)", p.nst);
   const size_t smem = 1024 + (size_t)p.nst * p.stage_bytes;
   p.n_sh_items = sh ? 2 * (Is / 128) * L.KPas : 0;
   p.slot_gate = slot_gate;

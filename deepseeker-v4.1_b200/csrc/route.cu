@@ -58,6 +58,10 @@ route_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bi
                   int top_k, int kind, float route_scale, int32_t* __restrict__ ids,
                   float* __restrict__ weights) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // launched with programmatic stream serialisation: the logits may come from
+  // the previous kernel, so wait for it (a no-op after a kernel that did not
+  // trigger early)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ uint32_t scode[kMaxExperts];
   __shared__ float sval[kMaxExperts];
   __shared__ float red[kRouteThreads / 32];
@@ -173,21 +177,29 @@ extern "C" int ds_route_topk(const float* logits, const float* bias, int64_t row
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned g = (unsigned)rows;
   const int per = (n_experts + 31) / 32;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g);
+  cfg.blockDim = dim3(kRouteThreads);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t rc;
   if (per <= 2)
-    route_topk_kernel<2><<<g, kRouteThreads, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids,
-                                                      weights);
+    rc = cudaLaunchKernelEx(&cfg, route_topk_kernel<2>, logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
   else if (per <= 4)
-    route_topk_kernel<4><<<g, kRouteThreads, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids,
-                                                      weights);
+    rc = cudaLaunchKernelEx(&cfg, route_topk_kernel<4>, logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
   else if (per <= 8)
-    route_topk_kernel<8><<<g, kRouteThreads, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids,
-                                                      weights);
+    rc = cudaLaunchKernelEx(&cfg, route_topk_kernel<8>, logits, bias, n_experts, top_k, kind, route_scale, ids, weights);
   else if (per <= 16)
-    route_topk_kernel<16><<<g, kRouteThreads, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids,
-                                                       weights);
+    rc = cudaLaunchKernelEx(&cfg, route_topk_kernel<16>, logits, bias, n_experts, top_k, kind, route_scale, ids,
+                            weights);
   else
-    route_topk_kernel<32><<<g, kRouteThreads, 0, st>>>(logits, bias, n_experts, top_k, kind, route_scale, ids,
-                                                       weights);
+    rc = cudaLaunchKernelEx(&cfg, route_topk_kernel<32>, logits, bias, n_experts, top_k, kind, route_scale, ids,
+                            weights);
+  DS_CHECK_CUDA(rc);
   DS_CHECK_LAUNCH("route_topk_kernel");
   return DS_OK;
 }

@@ -67,9 +67,14 @@ def test_q3_path_expert_id_out_of_range_sets_error(cuda):
     ws = torch.zeros(layer.decode_workspace_bytes(1, k), dtype=torch.uint8, device="cuda")
     ids = torch.tensor([[3, 99]], dtype=torch.int32, device="cuda")
     wts = torch.tensor([[0.5, 0.5]], device="cuda")
-    x = torch.randn(1, H, device="cuda").to(torch.bfloat16)
+    x = torch.randn(1, H, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).cuda()
     out = moe.moe_decode(x, layer, ids, wts, workspace=ws)
     torch.cuda.synchronize()
     assert int(ws[:4].view(torch.int32)[0]) & 1
+    # the dropped id behaves exactly like an empty routing entry
+    same = moe.moe_decode(x, layer, torch.tensor([[3, -1]], dtype=torch.int32, device="cuda"), wts)
+    assert torch.equal(out, same)
+    # 256 bf16 outputs: a few one-ulp rounding flips (2^-8 relative each)
+    # already reach 1e-3 rel-L2, so the oracle bound here is 2e-3
     ref = oracle_out(x, torch.tensor([[3, -1]], dtype=torch.int32), wts, layer, 10.0)
-    assert rel_l2(out, ref) < TOL
+    assert rel_l2(out, ref) < 2e-3, rel_l2(out, ref)
