@@ -9,8 +9,9 @@ Modules mirror the reference package's hot-path surface:
   grouped      `plan_groups` and the grouped expert FFN
   moe_align    device sort-and-pad alignment
   ep           expert-parallel dispatch / combine over torch.distributed
+  loader       checkpoint manifest / shards -> resident expert banks
 
 All compute runs in libdeepseeker_b200.so (CUDA, sm_100a), loaded lazily on the
 first operator call; there is no CPU fallback.
 """
-__all__ = ["metal_fp4", "mlx_weights", "requant", "variant_q3", "moe", "grouped", "moe_align", "ep"]
+__all__ = ["metal_fp4", "mlx_weights", "requant", "variant_q3", "moe", "grouped", "moe_align", "ep", "loader"]
