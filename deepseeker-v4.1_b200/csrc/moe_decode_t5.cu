@@ -20,7 +20,8 @@
 //             every item is 128 weight rows x a K slice, its f32 partial sum
 //             goes to a workspace slot;
 //   h       : sums the K slices, applies SiLU/clamp/gate, writes h as six
-//             e2m1 pieces (routed) or bf16 hi/lo (shared);
+//             e2m1 pieces (routed) or bf16 hi/lo (shared); it lets the down
+//             launch be scheduled before it waits for gate/up;
 //   down    : the same kernel over W2 tiles (its producer prefetches weight
 //             stages before waiting for the previous grid);
 //   combine : adds the slots in ascending expert order and the shared expert
@@ -29,12 +30,14 @@
 // kind::mxf4 reads FP4 operands packed (two codes per byte) with the 128-byte
 // swizzle, so the weights go from HBM to shared memory unchanged (128-byte
 // TMA rows: 256 codes) and a stage of shared memory holds exactly its HBM
-// bytes; nine stages keep ~144 KB of weights in flight per SM, which is what
-// the ~3 us TMA + MMA-commit round trip needs to stream at HBM rate.  Roles
-// per CTA: TMA producer, single-thread MMA issuer, four stager warps (scale
-// atoms into tensor memory, one warp per lane quarter), four epilogue warps.
-// Every wait is bounded; a timeout sets kErrWaitTimeout and an abort flag
-// that ends every role.
+// bytes; the ring holds as many 40 KB stages as fit (5 for up to 2 tokens:
+// 160 KB of weights in flight per SM).  A stage is freed only when its MMAs
+// complete, so the ring's turnaround (TMA landing, scale staging, MMA issue
+// and completion) sets the per-SM stream rate.  Roles per CTA: TMA producer,
+// two single-thread MMA issuers (even / odd items, four accumulator buffers
+// in tensor memory), four stager warps (scale atoms into tensor memory, one
+// warp per lane quarter), four epilogue warps.  Every wait is bounded; a
+// timeout sets kErrWaitTimeout and an abort flag that ends every role.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
