@@ -814,7 +814,8 @@ std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
 
 // Device address of the scratch array on the current device, resolved once
-// per device (the first call on a device does this setup).
+// per device (the first call on a device does this setup, which is why that
+// first call should come before any stream capture).
 int noalloc_scratch(void** out) {
   int dev = 0;
   DS_CHECK_CUDA(cudaGetDevice(&dev));

@@ -266,8 +266,9 @@ int ds_dense_swiglu(const float* x, int64_t tokens, int hidden, int inter, int n
  * array of ds_moe_decode_noalloc_max_scratch() bytes (8 MiB) per device;
  * a layer whose ds_moe_decode_workspace_size() exceeds it is rejected with
  * DS_ERANGE.  Same arguments, kernels and results as ds_moe_decode.
- *   - The first call on each device resolves the array's address (setup);
- *     make it before any latency-sensitive or otherwise restricted phase.
+ *   - The first call on each device resolves the array's address (setup,
+ *     cudaGetSymbolAddress with that device current); make that first call
+ *     before any stream capture and before any latency-sensitive phase.
  *   - Each call clears the array's error word on `stream` (cudaMemsetAsync);
  *     nothing else has to start at zero.
  *   - All calls on one device share the array: two calls that may overlap
