@@ -282,14 +282,18 @@ class ExpertLoader:
             self.bytes_read += len(data)
         return res["w1"], res["w3"], res["w2"]
 
+    def layer_experts(self, layer: int, prefix: str = "layers") -> list[int]:
+        """Expert ids of a layer that the manifest names, ascending."""
+        head = f"{prefix}.{layer}.ffn.experts."
+        return sorted({int(n[len(head):].split(".", 1)[0]) for n in self._by_name if n.startswith(head)})
+
     def load_layer(self, layer: int, experts: list[int] | None = None, shared: bool = True,
                    device: torch.device | str | None = None, prefix: str = "layers") -> MoEWeights:
         """One decode layer resident on the device: routed banks of ``experts``
         (default: every expert of the layer in the manifest, ascending) and,
         when present, the shared expert; FP4 banks come with their scale atoms."""
         if experts is None:
-            head = f"{prefix}.{layer}.ffn.experts."
-            experts = sorted({int(n[len(head):].split(".", 1)[0]) for n in self._by_name if n.startswith(head)})
+            experts = self.layer_experts(layer, prefix)
         banks = self.load_expert_banks([(layer, e, prefix) for e in experts], device)[layer]["banks"]
         sw = (None, None, None)
         if shared and f"{prefix}.{layer}.ffn.shared_experts.w1.weight" in self._by_name:

@@ -159,6 +159,16 @@ def test_read_banks_host_q3_payload(tmp_path):
     ld.close()
 
 
+def test_layer_experts_and_runs_cache(tmp_path):
+    root, _ = make_fp4_checkpoint(tmp_path)
+    man = loader.manifest_from_shards(root, ["a.safetensors", "b.safetensors"])
+    ld = loader.ExpertLoader(root, man)
+    assert ld.layer_experts(LAYER) == list(range(E))
+    assert ld.layer_experts(LAYER + 1) == []
+    assert ld.expert_runs("layers", LAYER, 1) is ld.expert_runs("layers", LAYER, 1)
+    ld.close()
+
+
 def test_layout_errors(tmp_path):
     root, _ = make_fp4_checkpoint(tmp_path)
     man = loader.manifest_from_shards(root, ["a.safetensors", "b.safetensors"])
