@@ -184,6 +184,20 @@ def test_layout_errors(tmp_path):
     ld.close()
 
 
+def test_read_into_buffer(tmp_path):
+    root, src = make_fp4_checkpoint(tmp_path)
+    man = loader.manifest_from_shards(root, ["a.safetensors", "b.safetensors"])
+    ent = {t["name"]: t for t in man["tensors"]}[f"layers.{LAYER}.ffn.experts.3.w1.weight"]
+    buf = np.zeros(ent["bytes"], dtype=np.uint8)
+    assert loader.read_into(root, ent["shard"], ent["file_range"][0], buf) == ent["bytes"]
+    assert buf.tobytes() == src[f"layers.{LAYER}.ffn.experts.3.w1.weight"].tobytes()
+    with pytest.raises(ValueError):
+        loader.read_into(root, ent["shard"], ent["file_range"][0], bytes(4))   # read-only target
+    with pytest.raises(RuntimeError):
+        loader.read_bytes(root, ent["shard"], (root / ent["shard"]).stat().st_size - 2,
+                          (root / ent["shard"]).stat().st_size + 2)   # past the end: short read
+
+
 def test_not_safetensors(tmp_path):
     p = tmp_path / "x.safetensors"
     p.write_bytes(b"\x01\x02")
