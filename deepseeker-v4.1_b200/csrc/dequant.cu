@@ -142,8 +142,10 @@ fp8_block_dequant_kernel(const uint8_t* __restrict__ packed, int64_t rows, int64
 
 // ---------------------------------------------------------------- 3-bit affine
 
-// Decode the 64 codes of one group (layout documented in the header of
-// oracle/q3.py and in DESIGN): low words 0..3, high words 4..5.
+// Decode code e (0..63) of one group.  Group layout (six u32 words): word w
+// in 0..3 holds the low two bits of element 16w+i at bits [2i, 2i+2); word
+// 4+h holds bit 2: element 16(2h+v)+j at bit 8v+j and element 16(2h+v)+8+j at
+// bit 16+8v+j (v in {0,1}, j < 8).
 __device__ __forceinline__ uint32_t q3_code(const uint32_t (&w)[6], int e) {
   const int wi = e >> 4, j = e & 7, upper = (e >> 3) & 1;
   const int lo_shift = upper * 16 + 2 * j;

@@ -612,6 +612,68 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(const DecodeArgs 
   }
 }
 
+// ============================================================== qmm
+
+// out[r, n] = sum_k x[r, k] * W[n, k] for one compressed matrix W (FP4 or Q3),
+// f32 accumulate, f32 out.  Block = 8 warps x 2 output rows = 16 rows of W
+// (blockIdx.x) for up to 8 rows of x (blockIdx.y), x staged in shared memory
+// as swizzled f32 (plus the 64-group sums for Q3).
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kThreads) qmm_kernel(const DsExpertBank w, const void* x, int x_f32,
+                                                        int64_t rows, float* out) {
+  extern __shared__ float4 smem4[];
+  const int K = w.cols, N = w.rows;
+  const int64_t r0 = (int64_t)blockIdx.y * NT;
+  const int T = (rows - r0 < (int64_t)NT) ? (int)(rows - r0) : NT;
+  float* xs = reinterpret_cast<float*>(smem4);  // [T][K]
+  float* xg = xs + (size_t)NT * K;              // [T][K/64] (Q3)
+  if (x_f32)
+    stage_f32(static_cast<const float*>(x) + r0 * K, T, K, K, xs);
+  else
+    stage_bf16(static_cast<const __nv_bfloat16*>(x) + r0 * K, T, K, xs);
+  __syncthreads();
+  if (FMT == DS_FMT_Q3) {
+    stage_group_sums(xs, T, K, xg);
+    __syncthreads();
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kRowsPerItem + warp * kRowsPerWarp;
+  const uint32_t tmask = (T >= 32) ? 0xffffffffu : ((1u << T) - 1u);
+  float acc[kRowsPerWarp][NT];
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+  const uint8_t* data[kRowsPerWarp];
+  const uint8_t* sc[kRowsPerWarp];
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
+    const RowPtr p = bank_row(w, 0, row0 + r);
+    data[r] = row0 + r < N ? p.data : nullptr;
+    sc[r] = p.sc;
+  }
+  if (FMT == DS_FMT_FP4) {
+    RowDot<DS_FMT_FP4, kRowsPerWarp, NT>::run(data, sc, K, xs, K, tmask, acc);
+  } else {
+    const __half* scq[kRowsPerWarp];
+    const __half* biq[kRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) {
+      const RowPtr p = bank_row(w, 0, row0 + r);
+      scq[r] = reinterpret_cast<const __half*>(p.sc);
+      biq[r] = reinterpret_cast<const __half*>(p.bi);
+    }
+    RowDotQ3<kRowsPerWarp, NT>::run(data, scq, biq, K, xs, K, xg, tmask, acc);
+  }
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float v = warp_sum(acc[r][t]);
+      if (lane == 0 && t < T && row0 + r < N) out[(r0 + t) * N + row0 + r] = v;
+    }
+}
+
 // ============================================================== host side
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -722,6 +784,28 @@ int dispatch_tokens(const DecodeArgs& a, cudaStream_t st) {
   return launch_decode<FMT, 8>(a, st);
 }
 
+// Kernel choice of one call, made from the descriptor and the scratch the
+// caller provides (workspace_bytes); ds_moe_decode and ds_moe_decode_noalloc
+// both come through here, so a given (layer, tokens, scratch size) always runs
+// the same kernels:
+//   FP4 banks with scale atoms, bf16 x  -> tcgen05 kernels (moe_decode_t5.cu)
+//   Q3 banks, bf16 x                    -> dp2a CUDA-core kernels (moe_decode_q3.cu)
+//   single-token FP4 without atoms      -> mma.sync kernels (moe_decode_tc.cu)
+//   anything else (f32 x, ...)          -> the generic kernels above
+// A path whose scratch does not fit in workspace_bytes is skipped.
+// `uncached`: encode tensor maps on the stack for this call only.
+int dispatch(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t s, bool uncached) {
+  if (ds::decode::t5_supported(a) && workspace_bytes >= ds::decode::t5_workspace_bytes(a.d, a.tokens))
+    return ds::decode::launch_t5(a, workspace, workspace_bytes, s);
+  if (ds::decode::q3_supported(a) && workspace_bytes >= ds::decode::q3_workspace_bytes(a.d, a.tokens))
+    return ds::decode::launch_q3(a, workspace, workspace_bytes, s);
+  DS_REQUIRE(!a.d.out_f32 || a.x_f32, DS_ENOTSUP,
+             "moe_decode: out_f32 with bf16 x needs FP4 banks with scale atoms or Q3 banks");
+  if (ds::decode::tc_supported(a))
+    return uncached ? ds::decode::launch_tc_uncached(a, s) : ds::decode::launch_tc(a, s);
+  return a.d.w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
+}
+
 }  // namespace
 
 extern "C" int ds_moe_decode_workspace_size(const DsMoeDesc* desc, int64_t tokens, size_t* bytes) {
@@ -761,32 +845,60 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
   a.max_slots = w.max_slots;
   a.h_stride = w.h_stride;
   a.err = reinterpret_cast<int*>(static_cast<char*>(workspace) + w.err_off);
+  return dispatch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), false);
+}
+
+// ============================================================== qmm host side
+
+namespace {
+
+template <int FMT, int NT>
+int launch_qmm(const DsExpertBank& w, const void* x, int x_f32, int64_t rows, float* out, cudaStream_t s) {
+  const size_t smem = (size_t)NT * w.cols * 4 + (FMT == DS_FMT_Q3 ? (size_t)NT * (w.cols / 64) * 4 : 0);
+  DS_REQUIRE(smem <= (size_t)kSmemBudget, DS_EINVAL, "qmm: K = %d too large (x rows staged in shared memory)",
+             w.cols);
+  DS_CHECK_CUDA(cudaFuncSetAttribute(qmm_kernel<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBudget + 16 * 1024));
+  const dim3 grid((w.rows + kRowsPerItem - 1) / kRowsPerItem, (unsigned)((rows + NT - 1) / NT));
+  qmm_kernel<FMT, NT><<<grid, kThreads, smem, s>>>(w, x, x_f32, rows, out);
+  DS_CHECK_LAUNCH("qmm_kernel");
+  return DS_OK;
+}
+
+template <int FMT>
+int qmm_rows(const DsExpertBank& w, const void* x, int x_f32, int64_t rows, float* out, cudaStream_t s) {
+  if (rows == 1) return launch_qmm<FMT, 1>(w, x, x_f32, rows, out, s);
+  if (rows == 2) return launch_qmm<FMT, 2>(w, x, x_f32, rows, out, s);
+  if (rows <= 4) return launch_qmm<FMT, 4>(w, x, x_f32, rows, out, s);
+  return launch_qmm<FMT, 8>(w, x, x_f32, rows, out, s);
+}
+
+}  // namespace
+
+extern "C" int ds_qmm(const DsExpertBank* w, const void* x, int x_dtype, int64_t rows, float* out, void* stream) {
+  DS_REQUIRE(w != nullptr, DS_EINVAL, "qmm: null matrix");
+  DS_REQUIRE(w->format == DS_FMT_FP4 || w->format == DS_FMT_Q3, DS_ENOTSUP, "qmm: format must be FP4 or Q3");
+  DS_REQUIRE(w->n_experts == 1, DS_EINVAL, "qmm: one matrix (n_experts == 1), got %d", w->n_experts);
+  DS_REQUIRE(w->rows > 0 && w->cols > 0, DS_EINVAL, "qmm: bad matrix geometry [%d, %d]", w->rows, w->cols);
+  DS_REQUIRE(rows >= 0 && rows <= (int64_t)65535 * 8, DS_EINVAL, "qmm: rows must be in [0, %d]", 65535 * 8);
+  DS_REQUIRE(x_dtype == DS_F32 || x_dtype == DS_BF16, DS_EINVAL, "qmm: x_dtype must be DS_F32 or DS_BF16");
+  DS_REQUIRE(w->data && w->scales && x && out, DS_EINVAL, "qmm: null pointer");
+  if (w->format == DS_FMT_FP4) {
+    DS_REQUIRE(w->cols % 32 == 0, DS_EINVAL, "qmm: FP4 K = %d not a multiple of 32", w->cols);
+    DS_REQUIRE(ds::aligned(w->data, 16), DS_EALIGN, "qmm: FP4 data must be 16-byte aligned");
+  } else {
+    DS_REQUIRE(w->cols % 64 == 0, DS_EINVAL, "qmm: Q3 K = %d not a multiple of 64", w->cols);
+    DS_REQUIRE(w->biases != nullptr, DS_EINVAL, "qmm: Q3 matrix needs biases");
+    DS_REQUIRE(ds::aligned(w->data, 8) && ds::aligned(w->scales, 2) && ds::aligned(w->biases, 2), DS_EALIGN,
+               "qmm: Q3 words 8-byte aligned, scales/biases 2-byte");
+  }
+  DS_REQUIRE(ds::aligned(x, 16) && ds::aligned(out, 4), DS_EALIGN, "qmm: x 16-byte and out 4-byte aligned");
+  DS_REQUIRE(w->cols % 4 == 0, DS_EINVAL, "qmm: K must be a multiple of 4");
+  if (rows == 0) return DS_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Single-token FP4 layers take the pipelined tensor-core kernels; the
-  // environment variable DEEPSEEKER_DECODE_GENERIC=1 forces the generic
-  // kernels (used by the tests to cross-check the two implementations).
-  static const bool force_generic = [] {
-    const char* v = getenv("DEEPSEEKER_DECODE_GENERIC");
-    return v != nullptr && v[0] == '1';
-  }();
-  // FP4 banks with prepared scale atoms take the tcgen05 kernels (1..8
-  // tokens); DEEPSEEKER_DECODE_NO_T5=1 keeps them on the older kernels.
-  static const bool no_t5 = [] {
-    const char* v = getenv("DEEPSEEKER_DECODE_NO_T5");
-    return v != nullptr && v[0] == '1';
-  }();
-  if (!force_generic && !no_t5 && ds::decode::t5_supported(a) &&
-      workspace_bytes >= ds::decode::t5_workspace_bytes(*desc, (int)tokens))
-    return ds::decode::launch_t5(a, workspace, workspace_bytes, s);
-  // Q3 banks with bf16 x take the streaming CUDA-core kernels
-  // (moe_decode_q3.cu); DEEPSEEKER_DECODE_GENERIC=1 keeps the generic ones.
-  if (!force_generic && ds::decode::q3_supported(a) &&
-      workspace_bytes >= ds::decode::q3_workspace_bytes(*desc, (int)tokens))
-    return ds::decode::launch_q3(a, workspace, workspace_bytes, s);
-  DS_REQUIRE(!desc->out_f32 || x_dtype == DS_F32, DS_ENOTSUP,
-             "moe_decode: out_f32 with bf16 x needs FP4 banks with scale atoms or Q3 banks");
-  if (!force_generic && ds::decode::tc_supported(a)) return ds::decode::launch_tc(a, s);
-  return desc->w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
+  const int xf = x_dtype == DS_F32;
+  return w->format == DS_FMT_FP4 ? qmm_rows<DS_FMT_FP4>(*w, x, xf, rows, out, s)
+                                 : qmm_rows<DS_FMT_Q3>(*w, x, xf, rows, out, s);
 }
 
 // ============================================================== no-allocation variant
@@ -797,15 +909,17 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
 // between stream-ordered allocator phases and must not trigger an
 // allocation, implicit or not.  ds_moe_decode_noalloc takes its scratch
 // from a file-scope __device__ array instead: the CUDA runtime reserves it
-// when the module is loaded, so the call itself allocates nothing on the
-// device or the host heap (tensor maps are encoded on the stack per call).
+// when the module is loaded, so the call itself allocates no device memory
+// (tensor maps live in fixed static tables or on the stack).
 
 namespace {
 
-// Scratch limit: 8 MiB.  A call needs 256 + (slots + 1) * tokens * stride * 4
-// bytes (slots = min(tokens * k, experts), stride = max(inter, shared_inter)):
-// one token fits for any k <= 32 with stride <= 8192, eight tokens of a top-8
-// layer fit with stride <= 4032.
+// Scratch limit: 8 MiB.  The call runs the kernels ds_moe_decode would run
+// with a workspace of this size (dispatch() above): the fastest path whose
+// scratch fits.  The generic kernels need 256 + (slots + 1) * tokens * stride
+// * 4 bytes (slots = min(tokens * k, experts), stride = max(inter,
+// shared_inter)); config 2's layer (hidden 4096, inter 2048, top-8) fits every
+// path at one token.
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -815,7 +929,8 @@ void* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
 
 // Device address of the scratch array on the current device, resolved once
 // per device (the first call on a device does this setup, which is why that
-// first call should come before any stream capture).
+// first call should come before any stream capture).  Every path keeps its
+// error word in the first 4 bytes of its scratch.
 int noalloc_scratch(void** out) {
   int dev = 0;
   DS_CHECK_CUDA(cudaGetDevice(&dev));
@@ -845,20 +960,19 @@ extern "C" int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x
              "moe_decode_noalloc: x_dtype must be DS_BF16 or DS_F32");
   DS_REQUIRE(ds::aligned(x, 16) && ds::aligned(out, 4), DS_EALIGN,
              "moe_decode_noalloc: x 16-byte and out 4-byte aligned");
+  // The generic kernels are the fallback of every call: their scratch must fit.
   const WsLayout w = ws_layout(desc, tokens);
   DS_REQUIRE(w.total <= kNoAllocScratchBytes, DS_ERANGE,
              "moe_decode_noalloc: this layer needs %zu bytes of scratch, the static limit is %zu "
              "(use ds_moe_decode with a workspace)",
              w.total, kNoAllocScratchBytes);
-  DS_REQUIRE(!desc->out_f32 || x_dtype == DS_F32, DS_ENOTSUP,
-             "moe_decode_noalloc: out_f32 with bf16 x is not supported here (use ds_moe_decode)");
   void* scratch = nullptr;
   if ((st = noalloc_scratch(&scratch)) != DS_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The error word is the only scratch that must start at zero (every h row
-  // the kernels read is written earlier in the same call); clear it on the
-  // stream so that it reports this call alone.
-  DS_CHECK_CUDA(cudaMemsetAsync(static_cast<char*>(scratch) + w.err_off, 0, sizeof(int), s));
+  // The error word is the only scratch that must start at zero (every other
+  // byte the kernels read is written earlier in the same call); clear it on
+  // the stream so that it reports this call alone.
+  DS_CHECK_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int), s));
   DecodeArgs a;
   a.d = *desc;
   a.x = x;
@@ -870,7 +984,15 @@ extern "C" int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x
   a.h = reinterpret_cast<float*>(static_cast<char*>(scratch) + w.h_off);
   a.max_slots = w.max_slots;
   a.h_stride = w.h_stride;
-  a.err = reinterpret_cast<int*>(static_cast<char*>(scratch) + w.err_off);
-  if (ds::decode::tc_supported(a)) return ds::decode::launch_tc_uncached(a, s);
-  return desc->w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
+  a.err = static_cast<int*>(scratch);
+  return dispatch(a, scratch, kNoAllocScratchBytes, s, true);
+}
+
+extern "C" int ds_moe_decode_noalloc_status(int32_t* err, void* stream) {
+  DS_REQUIRE(err != nullptr, DS_EINVAL, "moe_decode_noalloc_status: null output");
+  void* scratch = nullptr;
+  int st = noalloc_scratch(&scratch);
+  if (st != DS_OK) return st;
+  DS_CHECK_CUDA(cudaMemcpyAsync(err, scratch, sizeof(int32_t), cudaMemcpyDefault, static_cast<cudaStream_t>(stream)));
+  return DS_OK;
 }

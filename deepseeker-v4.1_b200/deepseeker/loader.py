@@ -231,9 +231,17 @@ class ExpertLoader:
                           ) -> dict[int, dict]:
         """Experts given as (layer, expert, prefix) -> {layer: {"banks": {role:
         ExpertBank}, "slots": {expert: slot}}}, one resident bank per projection
-        and layer (slots in the order the experts were given)."""
+        and layer (slots in the order the experts were given).
+
+        The result is keyed by layer index alone (as the reference's
+        load_expert_banks, mlx_weights.py:576-649), so one call takes one
+        prefix: specs that mix "layers" and "mtp" raise ValueError instead of
+        letting equal layer indices overwrite each other."""
         if not specs:
             return {}
+        prefixes = {prefix for _, _, prefix in specs}
+        if len(prefixes) > 1:
+            raise ValueError(f"load_expert_banks: one prefix per call, got {sorted(prefixes)}")
         device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         grouped: dict[tuple[int, str], list[int]] = {}
         for layer, expert, prefix in specs:

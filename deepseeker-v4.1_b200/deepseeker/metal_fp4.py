@@ -8,9 +8,11 @@ ue8m0 power-of-two scale per 32 elements (2^(b-127), 0xFF -> NaN).
 f32 out, ValueError on a scale-count mismatch; metal_fp4.py:139-155) but runs
 the sm_100a kernel ``ds_fp4_dequant``.  ``dequant`` is the device-resident form
 (replaces the bf16/u8-scale Metal path used by the expert loader,
-mlx_weights.py:340-360).  Results are bit-exact with the reference's CPU
-references (``reference_dequant`` / ``torch_reference``, which live with the
-test oracle, not in this package).
+mlx_weights.py:340-360).  ``reference_dequant`` (numpy) and
+``torch_reference`` (torch CPU) keep the reference's two host-side
+references of the same math (metal_fp4.py:122-131, 158-168), so callers and
+tests that cross-check the device result against them work unchanged; the
+device kernel is bit-exact with both.
 """
 from __future__ import annotations
 
@@ -73,3 +75,26 @@ def metal_dequant(packed: np.ndarray, scales_f32: np.ndarray) -> np.ndarray:
     s = to_device(np.ascontiguousarray(scales_f32, dtype=np.float32).reshape(-1))
     out = dequant(p, s, torch.float32)
     return out.cpu().numpy()
+
+
+def reference_dequant(packed: np.ndarray, scales_f32: np.ndarray) -> np.ndarray:
+    """Host numpy form of the dequant (metal_fp4.py:122-131): FP4_TABLE[nibble]
+    (low nibble = even element) times the block's f32 scale, one f32 multiply
+    per element; ``scales_f32`` must hold n/32 entries."""
+    raw = np.frombuffer(np.ascontiguousarray(packed).tobytes(), dtype=np.uint8)
+    vals = np.empty(raw.size * 2, dtype=np.float32)
+    vals[0::2] = FP4_TABLE[raw & 0x0F]
+    vals[1::2] = FP4_TABLE[raw >> 4]
+    return vals * np.repeat(np.asarray(scales_f32, dtype=np.float32).reshape(-1), BLOCK)
+
+
+def torch_reference(packed: np.ndarray, scales_f32: np.ndarray) -> torch.Tensor:
+    """Host torch form of the same dequant (metal_fp4.py:158-168), an
+    independent cross-check of ``reference_dequant``; returns a CPU tensor."""
+    table = torch.from_numpy(FP4_TABLE.copy())
+    raw = torch.frombuffer(bytearray(np.ascontiguousarray(packed).tobytes()), dtype=torch.uint8)
+    vals = torch.empty(raw.numel() * 2, dtype=torch.float32)
+    vals[0::2] = table[(raw & 0x0F).long()]
+    vals[1::2] = table[(raw >> 4).long()]
+    rep = torch.from_numpy(np.ascontiguousarray(scales_f32, dtype=np.float32).reshape(-1)).repeat_interleave(BLOCK)
+    return vals * rep

@@ -1,11 +1,15 @@
 """Routed-expert MoE layer on B200 -- the MoE subset of the reference's ``deepseeker.mlx_forward``.
 
-Reference: src/deepseeker/mlx_forward.py:62-419 (router, qmm, moe_layer) and
-src/deepseeker/mlx_runner.py:765-783 (shared expert).  Experts are held
-resident in HBM as stacked banks (``ExpertBank``: [E, N, ...] in the
-checkpoint's FP4 layout, or the build's 3-bit layout) instead of being
-streamed from SSD through a cache, so ``expert_fn`` / prefetch / pipeline /
-union-cap arguments of the reference have no counterpart here.
+Reference: src/deepseeker/mlx_forward.py:62-419 (router, qmm, gate/up
+stacking, banked gather, union cap, moe_layer) and
+src/deepseeker/mlx_runner.py:765-783 (shared expert).  ``moe_layer`` keeps the
+reference's signature (``expert_fn`` / ``shared_fn`` callables, trace and
+prefetch hooks, union cap); experts are best held resident in HBM as stacked
+banks (``ExpertBank``: [E, N, ...] in the checkpoint's FP4 layout, or the
+build's 3-bit layout; ``MoEWeights.resident()`` / ``shared_expert()``), which
+lets the whole routed loop run as one fused decode call.  The reference's
+SSD read pipeline (``pipeline=True`` with its submit / finalize hooks) is
+accepted and gives the same result as the plain path.
 
 Semantics kept from the reference:
   * router: sqrt(softplus(x Wg^T)), top-k of scores + bias, gates = scores /
@@ -219,6 +223,16 @@ class MoEWeights:
         d.route_before_down = 1 if self.route_before_down else 0
         return d
 
+    def resident(self) -> "ResidentExperts":
+        """The routed banks in the role of moe_layer's ``expert_fn``."""
+        return ResidentExperts(self)
+
+    def shared_expert(self) -> "SharedExpert | None":
+        """The bf16 shared expert in the role of moe_layer's ``shared_fn`` (None without one)."""
+        if self.shared_w1 is None:
+            return None
+        return SharedExpert(self.shared_w1, self.shared_w3, self.shared_w2)
+
     def streamed_bytes(self, n_distinct: int) -> int:
         """Algorithmic HBM bytes of one decode step touching `n_distinct` experts."""
         per_expert = sum(b.nbytes() // b.n_experts for b in (self.w1, self.w3, self.w2))
@@ -283,35 +297,333 @@ def moe_decode(x: torch.Tensor, weights: MoEWeights, topk_ids: torch.Tensor, top
     return out
 
 
-def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None, weights: MoEWeights,
-              top_k: int = 6, limit: float = 10.0, trace_hook=None, layer_id: int = 0,
-              route_scale: float = 1.5, **unsupported) -> torch.Tensor:
-    """MoE layer: sqrt-softplus router (exact), routed experts, shared expert add.
+# ------------------------------------------------------------------ qmm (mlx_forward.py:84-156)
 
-    Mirrors ``moe_layer`` (mlx_forward.py:257-419) with resident banks in place
-    of ``expert_fn``; ``trace_hook(layer, indices, weights)`` receives the
-    routing like the reference.  Token counts above the fused decode limit are
-    processed in groups of 8 rows (the grouped tensor-core path serves large
-    batches through ``grouped``).
+def _matrix_bank(w: tuple) -> ExpertBank:
+    """One compressed matrix as a one-expert bank view: (packed, scales) FP4
+    (packed u8 [N, K/2] or the u32 view [N, K/8] of pack_fp4_mxfp4, scales u8
+    [N, K/32]) or (words, scales, biases) Q3 (words u32/int32 [N, K*3/32],
+    f16 [N, K/64] scales and biases)."""
+    if not isinstance(w, (tuple, list)) or len(w) not in (2, 3):
+        raise ValueError("qmm operands must be (packed, scales) mxfp4 or (words, scales, biases) q3")
+    if len(w) == 2:
+        packed, scales = w
+        packed = require_cuda(packed, "packed", (torch.uint8, torch.int32, torch.uint32))
+        if packed.dtype != torch.uint8:
+            packed = packed.view(torch.uint8)
+        scales = require_cuda(scales, "scales", torch.uint8)
+        if packed.dim() != 2 or scales.dim() != 2:
+            raise ValueError("mxfp4 operands must be 2-D [N, K/2] (or u32 [N, K/8]) and [N, K/32]")
+        return ExpertBank.fp4(packed.unsqueeze(0), scales.unsqueeze(0))
+    words, scales, biases = w
+    if words.dim() != 2 or scales.dim() != 2:
+        raise ValueError("q3 operands must be 2-D [N, K*3/32], [N, K/64], [N, K/64]")
+    return ExpertBank.q3(words.unsqueeze(0), scales.unsqueeze(0), biases.unsqueeze(0))
+
+
+def qmm(x: torch.Tensor, w: tuple) -> torch.Tensor:
+    """x @ W.T with W held compressed: arity 2 = mxfp4 (packed, ue8m0 scales),
+    arity 3 = q3 affine (words, f16 scales, f16 biases), group 64
+    (mlx_forward.py:84-103).  x [..., K] f32 (or bf16) -> [..., N] f32; the
+    weights are dequantised in registers, never materialised."""
+    bank = _matrix_bank(w)
+    x = require_cuda(x, "x", (torch.float32, torch.bfloat16))
+    K = bank.cols
+    if x.shape[-1] != K:
+        raise ValueError(f"x has {x.shape[-1]} features, the matrix {K}")
+    x2 = x.reshape(-1, K)
+    out = torch.empty((x2.shape[0], bank.rows), dtype=torch.float32, device=x.device)
+    if x2.shape[0]:
+        wb = bank.c_struct()
+        xdt = _abi.DS_F32 if x2.dtype == torch.float32 else _abi.DS_BF16
+        with torch.cuda.device(x.device):
+            _abi.call("ds_qmm", ctypes.byref(wb), ptr(x2), xdt, x2.shape[0], ptr(out), stream_handle(x.device))
+    return out.reshape(*x.shape[:-1], bank.rows)
+
+
+def stack_gate_up_expert(weights: dict) -> dict:
+    """w1 / w3 operands concatenated along the output rows into one "w13"
+    (mlx_forward.py:106-120); a dict that already holds w13 is returned as is."""
+    if "w13" in weights:
+        return weights
+    w1, w3 = weights["w1"], weights["w3"]
+    if len(w1) != len(w3) or len(w1) not in (2, 3):
+        raise ValueError("w1/w3 operand arity must be 2 (mxfp4) or 3 (q3)")
+    for a, b in zip(w1, w3):
+        if a.shape[1:] != b.shape[1:] or a.shape[0] != b.shape[0]:
+            raise ValueError("gate/up packed shapes must agree")
+    return {"w13": tuple(torch.cat((a, b), dim=0) for a, b in zip(w1, w3)), "w2": weights["w2"]}
+
+
+def split_gate_up_expert(weights: dict) -> dict:
+    """w1 / w3 views of a stacked "w13" without copying (mlx_forward.py:123-140)."""
+    if "w13" not in weights:
+        return weights
+    parts = weights["w13"]
+    halves: dict[str, list] = {"w1": [], "w3": []}
+    for part in parts:
+        if part.shape[0] % 2:
+            raise ValueError("stacked gate/up operand rows must divide evenly")
+        n = part.shape[0] // 2
+        halves["w1"].append(part[:n])
+        halves["w3"].append(part[n:])
+    return {"w1": tuple(halves["w1"]), "w3": tuple(halves["w3"]), "w2": weights["w2"]}
+
+
+def gate_up_qmm(x: torch.Tensor, weights, *, stack_single_row: bool = False
+                ) -> tuple[torch.Tensor, torch.Tensor, tuple]:
+    """(gate, up, w2 operands) for rows x; with stack_single_row and one row,
+    gate and up come from one qmm over the stacked w13 (mlx_forward.py:143-156)."""
+    if isinstance(weights, dict):
+        expert = weights
+    else:
+        w1, w3, w2 = weights
+        expert = {"w1": w1, "w3": w3, "w2": w2}
+    single = stack_single_row and x.shape[0] == 1
+    if "w13" not in expert and single:
+        expert = stack_gate_up_expert(expert)
+    if "w13" in expert and single:
+        gate, up = torch.chunk(qmm(x, expert["w13"]), 2, dim=-1)
+    else:
+        sep = split_gate_up_expert(expert)
+        gate, up = qmm(x, sep["w1"]), qmm(x, sep["w3"])
+    return gate, up, expert["w2"]
+
+
+def gather_pinned_contributions(x: torch.Tensor, indices, weights, banks: dict[str, tuple],
+                                slots: dict[int, int], limit: float = 10.0) -> dict[int, tuple]:
+    """Per-expert weighted outputs of the (expert, row, column) pairs whose
+    expert sits in a resident bank (mlx_forward.py:159-210): banks[role] holds
+    stacked operands [E_b, N, ...], slots maps expert -> bank index.  Pairs in
+    (expert, row) order; every matching column counts (duplicates included);
+    the route weight multiplies h before the down projection.  Returns
+    {expert: (rows int32 numpy, contributions [n, H] f32)}."""
+    import numpy as np
+
+    idx = np.asarray(indices)
+    wts = np.asarray(weights, dtype=np.float32)
+    out = {}
+    for expert in sorted(slots):
+        rr, cc = np.nonzero(idx == int(expert))
+        if rr.size == 0:
+            continue
+        order = np.lexsort((cc, rr))
+        rr, cc = rr[order], cc[order]
+        b = slots[expert]
+        ops = {role: tuple(part[b] for part in banks[role]) for role in ("w1", "w3", "w2")}
+        xr = x[torch.as_tensor(rr, device=x.device)].float()
+        g = torch.clamp(qmm(xr, ops["w1"]), max=limit)
+        u = torch.clamp(qmm(xr, ops["w3"]), -limit, limit)
+        h = g / (1.0 + torch.exp(-g)) * u
+        rw = torch.as_tensor(wts[rr, cc], device=x.device).reshape(-1, 1)
+        out[int(expert)] = (rr.astype(np.int32), qmm(h * rw, ops["w2"]))
+    return out
+
+
+def cap_union(idx, w, n_experts: int, budget: int, *, scores=None, strict: bool = False):
+    """Cap the batch's expert union at ``budget`` experts (mlx_forward.py:213-254):
+    keep the experts with the largest summed gate weight (or summed raw score
+    when ``scores`` is given), drop the others' slots (index -1, weight 0),
+    renormalise each row to its original weight sum; unless ``strict``, a row
+    that would lose every slot keeps its heaviest one.  Returns (indices
+    int64, weights f32, share of the total weight kept before renormalising)."""
+    import numpy as np
+
+    idx = np.asarray(idx)
+    w = np.asarray(w, dtype=np.float32)
+    if np.unique(idx).size <= budget:
+        return idx, w, 1.0
+    mass = np.zeros(n_experts, dtype=np.float32)
+    if scores is not None:
+        np.add.at(mass, idx.ravel(), np.asarray(scores)[np.arange(idx.shape[0])[:, None], idx].ravel())
+    else:
+        np.add.at(mass, idx.ravel(), w.ravel())
+    keep = np.zeros(n_experts, dtype=bool)
+    keep[np.argpartition(mass, -budget)[-budget:]] = True
+    kept = keep[idx]
+    lost = ~kept.any(axis=1)
+    if lost.any() and not strict:
+        kept[np.nonzero(lost)[0], w[lost].argmax(axis=1)] = True
+    kept_w = np.where(kept, w, 0.0)
+    total, kept_total = float(w.sum()), float(kept_w.sum())
+    rescale = w.sum(axis=1, keepdims=True) / (kept_w.sum(axis=1, keepdims=True) + 1e-20)
+    return (np.where(kept, idx, -1).astype(np.int64), (kept_w * rescale).astype(np.float32),
+            kept_total / total if total > 0 else 1.0)
+
+
+# ------------------------------------------------------------------ moe_layer (mlx_forward.py:257-419)
+
+class ResidentExperts:
+    """A layer's routed experts held resident as banks (``MoEWeights``), in the
+    role of the reference's ``expert_fn``: calling it with an expert id gives
+    that expert's (w1, w3, w2) operand tuples (views into the banks), and
+    ``moe_layer`` runs the whole routed loop as one fused kernel when it gets
+    one of these."""
+
+    def __init__(self, weights: "MoEWeights"):
+        self.weights = weights
+
+    def __call__(self, expert: int) -> tuple:
+        e = int(expert)
+        out = []
+        for b in (self.weights.w1, self.weights.w3, self.weights.w2):
+            out.append((b.data[e], b.scales[e]) if b.biases is None else (b.data[e], b.scales[e], b.biases[e]))
+        return tuple(out)
+
+
+class SharedExpert:
+    """A resident bf16 shared expert in the role of the reference's
+    ``shared_fn`` (mlx_runner.py:765-783): f32 SwiGLU with g <= 10 and u in
+    [-10, 10], output cast to x.dtype.  ``moe_layer`` folds it into the fused
+    decode kernel when the routed experts are resident too."""
+
+    def __init__(self, w1: torch.Tensor, w3: torch.Tensor, w2: torch.Tensor, limit: float = 10.0):
+        self.w1, self.w3, self.w2, self.limit = w1, w3, w2, limit
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        g = torch.clamp(xf @ self.w1.float().T, max=self.limit)
+        u = torch.clamp(xf @ self.w3.float().T, -self.limit, self.limit)
+        return ((g / (1.0 + torch.exp(-g)) * u) @ self.w2.float().T).to(x.dtype)
+
+
+def _routed_only(weights: "MoEWeights", shared: SharedExpert | None, limit: float) -> "MoEWeights":
+    sw = (shared.w1, shared.w3, shared.w2) if shared is not None else (None, None, None)
+    return MoEWeights(weights.w1, weights.w3, weights.w2, *sw, limit, True)
+
+
+def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None, expert_fn, shared_fn,
+              top_k: int = 6, limit: float = 10.0, trace_hook=None, layer_id: int = 0, prefetch_fn=None,
+              union_budget: int = 0, route_stats: dict | None = None, union_strict: bool = False,
+              pipeline: bool = False, async_submit_fn=None, async_finalize_fn=None, pinned_gather_fn=None,
+              stack_gateup: bool = False, route_scale: float = 1.5) -> torch.Tensor:
+    """Route (exact), routed experts, shared expert add (mlx_forward.py:257-419).
+
+    Same arguments and semantics as the reference:
+      * router: s = sqrt(softplus(x Wg^T)), top-k of s + gate_b, gates =
+        s / (sum + 1e-20) * 1.5; ``trace_hook(layer_id, indices, weights)``
+        gets the routing (slots in ascending biased-score order);
+      * ``union_budget > 0`` with several rows caps the expert union
+        (``cap_union``), accumulating the kept share in ``route_stats``;
+      * ``expert_fn(e) -> (w1, w3, w2)`` operand tuples; per distinct expert,
+        ascending: g = min(x W1^T, limit), u = clip(x W3^T, +-limit),
+        h = silu(g) * u * gate (first slot of the row), out[rows] += h W2^T;
+      * ``shared_fn(x)`` (None = no shared expert) is added in f32 after the
+        routed sum; the result is cast to x.dtype.  x enters the experts as
+        f32 (bf16 x exactly; f32 x is not rounded).
+    With ``expert_fn`` a ``ResidentExperts`` (or ``MoEWeights``) and no
+    ``pinned_gather_fn``, the routed loop and a ``SharedExpert`` run in the
+    fused decode kernels (ds_moe_decode) instead of one qmm per expert.
+    ``prefetch_fn(layer_id, experts)`` is called before the experts run.
+    ``pipeline=True`` with ``async_submit_fn(layer, e) -> future of (operands
+    dict, nbytes, was_hit, read_s, pack_s)`` and ``async_finalize_fn(layer,
+    experts, saved)`` takes every expert's operands from its future and calls
+    the finalize hook before the sorted scatter-add, as the reference's read
+    pipeline does; the result equals the plain path.
     """
-    bad = {k for k, v in unsupported.items() if v not in (None, False, 0)}
-    if bad:
-        raise NotImplementedError(f"moe_layer: SSD-paging options {sorted(bad)} have no counterpart "
-                                  "(experts are resident in HBM)")
-    if limit != weights.swiglu_limit:
-        weights = MoEWeights(weights.w1, weights.w3, weights.w2, weights.shared_w1, weights.shared_w3,
-                             weights.shared_w2, limit, weights.route_before_down)
-    x2 = x.reshape(-1, x.shape[-1])
-    logits = (x2.float() @ gate_w.float().T).contiguous()
-    w, idx = route_sqrtsoftplus(logits, gate_b, top_k, route_scale)
+    import numpy as np
+
+    H = x.shape[-1]
+    x2 = require_cuda(x.reshape(-1, H), "x", (torch.bfloat16, torch.float32))
+    T = x2.shape[0]
+    gate_w = require_cuda(gate_w, "gate_w")
+    scores = sqrtsoftplus_scores(x2, gate_w).contiguous()
+    bias = gate_b if gate_b is not None else torch.zeros(gate_w.shape[0], device=x2.device)
+    w_d, idx_d = route_topk(scores, bias, top_k, route_scale)
+    w_d, idx_d = w_d.flip(-1).contiguous(), idx_d.flip(-1).contiguous()   # ascending, as the reference
+    idx_np = idx_d.cpu().numpy().astype(np.int64)
+    w_np = w_d.cpu().numpy().astype(np.float32)
+    if union_budget > 0 and T > 1:
+        idx_np, w_np, coverage = cap_union(idx_np, w_np, scores.shape[1], union_budget,
+                                           scores=scores.cpu().numpy(), strict=union_strict)
+        if route_stats is not None:
+            route_stats["coverage"] += coverage * T
+            route_stats["calls"] += T
+        idx_d = torch.as_tensor(idx_np, dtype=torch.int32, device=x2.device)
+        w_d = torch.as_tensor(w_np, device=x2.device)
+    unique = np.unique(idx_np)
+    unique = unique[unique >= 0]
+    if prefetch_fn is not None:
+        prefetch_fn(layer_id, [int(e) for e in unique])
+
+    resident = expert_fn.weights if isinstance(expert_fn, ResidentExperts) else (
+        expert_fn if isinstance(expert_fn, MoEWeights) else None)
+    piped = pipeline and async_submit_fn is not None and async_finalize_fn is not None
+    if resident is not None and pinned_gather_fn is None and not piped:
+        fuse_shared = isinstance(shared_fn, SharedExpert) and shared_fn.limit == limit
+        layer = _routed_only(resident, shared_fn if fuse_shared else None, limit)
+        ids32 = idx_d.to(torch.int32).contiguous()
+        # a shared expert computed apart is added to the unrounded routed sum
+        f32_sum = shared_fn is not None and not fuse_shared and x2.dtype != torch.float32
+        if f32_sum and resident.w1.fmt == _abi.DS_FMT_FP4:
+            resident.prepare_tc()          # the f32-output decode kernels read the scale atoms
+        out = torch.empty(x2.shape, dtype=torch.float32 if f32_sum else x2.dtype, device=x2.device)
+        try:
+            for r0 in range(0, T, MAX_DECODE_TOKENS):
+                r1 = min(T, r0 + MAX_DECODE_TOKENS)
+                moe_decode(x2[r0:r1], layer, ids32[r0:r1], w_d[r0:r1].contiguous(), out=out[r0:r1],
+                           out_f32=f32_sum)
+        except NotImplementedError:
+            out = None                     # no unrounded-output kernel for this geometry: per-expert path
+        if out is not None:
+            if trace_hook is not None:
+                trace_hook(layer_id, idx_np.tolist(), w_np.tolist())
+            if shared_fn is not None and not fuse_shared:
+                out = (out.float() + shared_fn(x2).float()).to(x2.dtype)
+            return out.reshape(x.shape)
+
+    if resident is not None:
+        expert_fn = ResidentExperts(resident)
+    shared_out = shared_fn(x2).float() if shared_fn is not None else None
+    out = torch.zeros((T, H), dtype=torch.float32, device=x2.device)
+
+    def contrib(e: int, ops):
+        """rows routed to e (first slot each), and their weighted expert outputs."""
+        mask = idx_np == e
+        rows = np.nonzero(mask.any(axis=1))[0]
+        cols = mask[rows].argmax(axis=1)
+        rows_d = torch.as_tensor(rows, dtype=torch.int64, device=x2.device)
+        g, u, w2 = gate_up_qmm(x2[rows_d].float(), ops, stack_single_row=stack_gateup)
+        g = torch.clamp(g, max=limit)
+        u = torch.clamp(u, -limit, limit)
+        h = g / (1.0 + torch.exp(-g)) * u
+        rw = torch.as_tensor(w_np[rows, cols], device=x2.device).reshape(-1, 1)
+        return rows_d, qmm(h * rw, w2)
+
+    if piped and pinned_gather_fn is None:
+        # the reference's read pipeline: every expert's operands come from a
+        # future, the caller's finalize hook runs before the sorted scatter-add
+        futs = {int(e): async_submit_fn(layer_id, int(e)) for e in unique}
+        saved = {}
+        try:
+            for e, fut in futs.items():
+                ops, nbytes, was_hit, read_s, pack_s = fut.result()
+                rows_d, c = contrib(e, ops)
+                saved[e] = (rows_d.cpu().numpy(), c, ops, nbytes, was_hit, read_s, pack_s)
+        except Exception:
+            for fut in futs.values():
+                if not fut.done():
+                    fut.cancel()
+            raise
+        async_finalize_fn(layer_id, [int(e) for e in unique], saved)
+        for e in unique:
+            rows, c = saved[int(e)][:2]
+            out.index_add_(0, torch.as_tensor(rows, dtype=torch.int64, device=x2.device), c)
+    else:
+        pinned = pinned_gather_fn(layer_id, x2, idx_np, w_np) if pinned_gather_fn is not None else {}
+        for expert in unique:
+            e = int(expert)
+            if e in pinned:
+                rows, c = pinned[e]
+                out.index_add_(0, torch.as_tensor(rows, dtype=torch.int64, device=x2.device), c.float())
+                continue
+            rows_d, c = contrib(e, expert_fn(e))
+            out.index_add_(0, rows_d, c)
     if trace_hook is not None:
-        trace_hook(layer_id, idx.cpu().tolist(), w.cpu().tolist())
-    xb = x2.to(torch.bfloat16).contiguous()
-    out = torch.empty_like(xb)
-    for r0 in range(0, xb.shape[0], MAX_DECODE_TOKENS):
-        r1 = min(xb.shape[0], r0 + MAX_DECODE_TOKENS)
-        moe_decode(xb[r0:r1], weights, idx[r0:r1].contiguous(), w[r0:r1].contiguous(), out=out[r0:r1])
-    return out.reshape(x.shape).to(x.dtype)
+        trace_hook(layer_id, idx_np.tolist(), w_np.tolist())
+    if shared_out is not None:
+        out = out + shared_out
+    return out.to(x2.dtype).reshape(x.shape)
 
 
 def _static_input(t: torch.Tensor | None, shape, dtype, device, name: str) -> torch.Tensor:

@@ -16,8 +16,12 @@
  * Layout conventions (all row-major, K = input features contiguous):
  *   FP4  : packed [N, K/2] u8, two e2m1 codes per byte, LOW nibble = even
  *          element; scales [N, K/32] u8 (ue8m0: 2^(b-127), 0xFF = NaN).
- *   Q3   : words [N, K*3/32] u32 (builder-defined 3-bit layout, see DESIGN),
- *          scales / biases [N, K/64] f16; w = f32(scale)*q + f32(bias).
+ *   Q3   : words [N, K*3/32] u32, scales / biases [N, K/64] f16;
+ *          w = f32(scale)*q + f32(bias).  One 64-element group = six
+ *          little-endian u32 words: word w (0..3) holds the low two bits of
+ *          elements 16w+i at bits [2i, 2i+2) (i = 0..15); word 4+h holds
+ *          bit 2 of the codes: element 16(2h+v)+j at bit 8v+j and element
+ *          16(2h+v)+8+j at bit 16+8v+j (v in {0,1}, j = 0..7).
  *   BF16 : [N, K] bf16.
  *   Expert banks stack E experts: [E, N, ...] with the per-expert layout above.
  */
@@ -187,6 +191,16 @@ int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tok
                   const int32_t* topk_ids, const float* topk_w, void* out,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* One compressed matrix times a batch of activations: out[r, n] =
+ * sum_k x[r, k] * W[n, k], W dequantised in registers (exactly: FP4 codes times
+ * their ue8m0 scale; Q3 as f32(scale)*q + f32(bias)), f32 accumulate.
+ * Replaces qmm (src/deepseeker/mlx_forward.py:84-103: mx.quantized_matmul with
+ * mode="mxfp4", or bits=3 / group 64 with biases).
+ *   w   : one matrix (n_experts = 1), DS_FMT_FP4 or DS_FMT_Q3, [N = rows, K = cols]
+ *   x   : [rows, K] f32 (DS_F32) or bf16 (DS_BF16), 16-byte aligned
+ *   out : [rows, N] f32.  K <= 6144 (eight x rows staged in shared memory). */
+int ds_qmm(const DsExpertBank* w, const void* x, int x_dtype, int64_t rows, float* out, void* stream);
+
 /* ---- sort-and-pad of routed pairs by expert ---------------------------- */
 
 /* Output capacities ds_moe_align needs for topk_ids [m, k] over n_experts:
@@ -262,15 +276,25 @@ int ds_dense_swiglu(const float* x, int64_t tokens, int hidden, int inter, int n
 
 /* ds_moe_decode without a workspace.  No counterpart in the reference (its
  * MLX runtime owns all scratch); added for callers that may not allocate
- * device memory at all while decoding.  Scratch comes from a static device
- * array of ds_moe_decode_noalloc_max_scratch() bytes (8 MiB) per device;
- * a layer whose ds_moe_decode_workspace_size() exceeds it is rejected with
- * DS_ERANGE.  Same arguments, kernels and results as ds_moe_decode.
+ * device memory at all while decoding, e.g. a serving loop whose device memory
+ * is carved up once by its own pool.  Scratch comes from a static device array
+ * of ds_moe_decode_noalloc_max_scratch() bytes (8 MiB) per device.
+ *   - Kernels: exactly those ds_moe_decode runs when given a workspace of
+ *     that size (the fastest path whose scratch fits: tcgen05 for FP4 banks
+ *     with scale atoms, the q3 kernels for Q3 banks, else the generic ones),
+ *     so results equal ds_moe_decode's bit for bit whenever
+ *     ds_moe_decode_workspace_size() <= the limit, and stay within the
+ *     decode tolerance (rel-L2 <= 1e-3 of the f32 oracle) otherwise.
+ *   - Limit: a layer whose generic-path scratch (256 + (min(tokens*k, E) + 1)
+ *     * tokens * max(inter, shared_inter) * 4 bytes, rounded up to 256) exceeds
+ *     the array is rejected with DS_ERANGE.
  *   - The first call on each device resolves the array's address (setup,
  *     cudaGetSymbolAddress with that device current); make that first call
  *     before any stream capture and before any latency-sensitive phase.
  *   - Each call clears the array's error word on `stream` (cudaMemsetAsync);
- *     nothing else has to start at zero.
+ *     nothing else has to start at zero.  ds_moe_decode_noalloc_status reads
+ *     the word back: bit 0 = an expert id >= n_experts was skipped, bit 1 = a
+ *     bounded device wait gave up (outputs of that call are then undefined).
  *   - All calls on one device share the array: two calls that may overlap
  *     (different streams, or host threads without ordering) race on it and
  *     corrupt each other's results.  Serialise them on one stream. */
@@ -278,6 +302,10 @@ size_t ds_moe_decode_noalloc_max_scratch(void);
 int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens,
                           const int32_t* topk_ids, const float* topk_w, void* out,
                           void* stream);
+/* Copy the no-allocation scratch's error word of the current device into *err
+ * (host or device memory; one cudaMemcpyAsync on `stream`, read it after the
+ * stream has finished).  No counterpart in the reference. */
+int ds_moe_decode_noalloc_status(int32_t* err, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Expert-parallel decode over NVLink peer memory.

@@ -181,6 +181,9 @@ def test_layout_errors(tmp_path):
         ld.read_banks_host(LAYER, [0, 1])
     with pytest.raises(KeyError):
         ld.read_banks_host(LAYER, [7])
+    # one prefix per call: the result is keyed by layer index alone
+    with pytest.raises(ValueError, match="one prefix per call"):
+        ld.load_expert_banks([(LAYER, 0, "layers"), (LAYER, 1, "mtp")])
     ld.close()
 
 
