@@ -788,6 +788,7 @@ int dispatch_tokens(const DecodeArgs& a, cudaStream_t st) {
 // caller provides (workspace_bytes); ds_moe_decode and ds_moe_decode_noalloc
 // both come through here, so a given (layer, tokens, scratch size) always runs
 // the same kernels:
+//   one token, FP4 banks, bf16 x         -> register-dequant kernel (moe_decode_rd.cu)
 //   FP4 banks with scale atoms, bf16 x  -> tcgen05 kernels (moe_decode_t5.cu)
 //   Q3 banks, bf16 x                    -> dp2a CUDA-core kernels (moe_decode_q3.cu)
 //   single-token FP4 without atoms      -> mma.sync kernels (moe_decode_tc.cu)
@@ -795,6 +796,8 @@ int dispatch_tokens(const DecodeArgs& a, cudaStream_t st) {
 // A path whose scratch does not fit in workspace_bytes is skipped.
 // `uncached`: encode tensor maps on the stack for this call only.
 int dispatch(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t s, bool uncached) {
+  if (ds::decode::rd_supported(a) && workspace_bytes >= ds::decode::rd_workspace_bytes(a.d))
+    return ds::decode::launch_rd(a, workspace, workspace_bytes, s);
   if (ds::decode::t5_supported(a) && workspace_bytes >= ds::decode::t5_workspace_bytes(a.d, a.tokens))
     return ds::decode::launch_t5(a, workspace, workspace_bytes, s);
   if (ds::decode::q3_supported(a) && workspace_bytes >= ds::decode::q3_workspace_bytes(a.d, a.tokens))
@@ -817,6 +820,7 @@ extern "C" int ds_moe_decode_workspace_size(const DsMoeDesc* desc, int64_t token
       tokens <= ds::decode::kMaxTokens)
     total = std::max(total, ds::decode::t5_workspace_bytes(*desc, (int)tokens));
   if (desc->w1.format == DS_FMT_Q3) total = std::max(total, ds::decode::q3_workspace_bytes(*desc, (int)tokens));
+  if (desc->w1.format == DS_FMT_FP4 && tokens == 1) total = std::max(total, ds::decode::rd_workspace_bytes(*desc));
   *bytes = total;
   return DS_OK;
 }
@@ -969,10 +973,12 @@ extern "C" int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x
   void* scratch = nullptr;
   if ((st = noalloc_scratch(&scratch)) != DS_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The error word is the only scratch that must start at zero (every other
-  // byte the kernels read is written earlier in the same call); clear it on
-  // the stream so that it reports this call alone.
-  DS_CHECK_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int), s));
+  // The error word and the single-token kernel's control words are the only
+  // scratch that must start at zero (every other byte the kernels read is
+  // written earlier in the same call); clear them on the stream so that the
+  // word reports this call alone and an earlier call that gave up leaves no
+  // trace.
+  DS_CHECK_CUDA(cudaMemsetAsync(scratch, 0, ds::decode::rd_control_bytes(*desc), s));
   DecodeArgs a;
   a.d = *desc;
   a.x = x;

@@ -107,6 +107,15 @@ int launch_tc(const DecodeArgs& a, cudaStream_t st);
 // so no host heap either).
 int launch_tc_uncached(const DecodeArgs& a, cudaStream_t st);
 
+// Single-token register-dequant pipeline (moe_decode_rd.cu): FP4 banks (no
+// scale atoms needed), bf16 x, one cooperative kernel per layer.  Its
+// workspace holds control words that must be zero before the first call and
+// that every completed call leaves zero.
+bool rd_supported(const DecodeArgs& a);
+size_t rd_workspace_bytes(const DsMoeDesc& d);
+size_t rd_control_bytes(const DsMoeDesc& d);  // leading workspace bytes: error word + control words
+int launch_rd(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t st);
+
 // tcgen05 pipeline for 1..8 tokens (moe_decode_t5.cu): FP4 banks that carry
 // prepared scale atoms, bf16 x.  Needs its own workspace size.
 bool t5_supported(const DecodeArgs& a);

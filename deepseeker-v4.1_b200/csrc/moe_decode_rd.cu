@@ -1,0 +1,747 @@
+// Single-token routed-expert MoE layer, register-dequant path: FP4 routed
+// experts (checkpoint layout, no prepared scale atoms needed) + optional bf16
+// shared expert, bf16 x, one token.  One cooperative persistent kernel per
+// layer, one CTA per SM, every warp independent:
+//
+// Streaming.  A warp's unit of work is 16 weight rows x 4 K-groups of 128
+// elements (4 KB of FP4 or bf16 weights).  Each lane loads 16 bytes of two
+// rows per K-group straight from HBM into registers (coalesced 128-bit
+// loads, L2 evict-first), two units in flight per warp (double buffer).  No
+// shared-memory staging ring and no producer/consumer hand-off: the
+// bytes-in-flight come from every warp issuing its next unit's loads before
+// it computes the current one.
+//
+// Dot products.  FP4 codes are decoded in registers (cvt.rn.f16x2.e2m1x2:
+// exact) into mma.sync m16n8k16 A fragments (f16, f32 accumulate).  The B
+// operand is the activation laid out so that column n of the 16x8 B tile
+// only carries the K elements of the lane group t = n, i.e. of ONE 32-element
+// weight block: C[row][n] is then the dot product of that row with that
+// block, and each block's ue8m0 scale (times the activation block's
+// power-of-two scale) multiplies its own f32 partial.  Dequant is exact, the
+// products are exact, the accumulation is f32.  Activations enter as f16
+// scaled per 32-block by a power of two (bf16 x: exactly; the SwiGLU
+// intermediate h: as an f16 hi + lo pair, ~22 significant bits, in columns
+// 0-3 and 4-7).  The shared expert's bf16 weights feed bf16 MMAs directly
+// (x exact; its h as three bf16 pieces).
+//
+// Phase A (gate/up): tasks of 8 rows of W1 and the same 8 rows of W3 over the
+//   full K (a routed expert), or over a K quarter (the shared expert, whose
+//   rows are 4x wider); each CTA takes a contiguous range of tasks, so h of a
+//   routed task is finished inside the CTA (SwiGLU clamps, route weight); the
+//   four quarters of a shared task are summed by the CTA that finishes last
+//   (arrival counter).
+// Grid barrier (bounded spin).  Before it, every CTA prefetches its phase-B
+//   weights into L2 and issues its first phase-B unit's loads.
+// Phase B (down + combine): each CTA owns a contiguous range of ~H/G output
+//   rows: all routed slots' W2 rows and the shared W2 rows of that range, so
+//   the combine (routed slots in ascending expert id, then the shared output
+//   rounded to bf16, reference mlx_forward.py:388-419 / mlx_runner.py:776-781)
+//   happens in the CTA with no further pass.
+//
+// Control words (grid barrier, shared-task counters) live in the workspace,
+// must be zero before the first call and are left zero by every call that
+// completes.  Every wait is bounded by %globaltimer (2 s); on expiry the
+// kernel sets kErrWaitTimeout in the error word and stops waiting.
+#include <algorithm>
+
+#include "moe_decode.cuh"
+#include "ptx.cuh"
+
+namespace ds {
+namespace decode {
+namespace {
+
+using namespace ds::ptx;
+
+constexpr int kWarps = 8;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kMaxSlotsRd = 32;
+constexpr int kMaxTasksPerCta = 256;
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr int kZeroBytes = 128;
+
+struct RdParams {
+  const uint8_t* w1;  // FP4 [E][I][H/2]
+  const uint8_t* w3;
+  const uint8_t* w2;  // FP4 [E][H][I/2]
+  const uint8_t* s1;  // ue8m0 [E][I][H/32]
+  const uint8_t* s3;
+  const uint8_t* s2;  // ue8m0 [E][H][I/32]
+  const uint8_t* sw1; // bf16 [Is][H] (null: no shared expert)
+  const uint8_t* sw3;
+  const uint8_t* sw2; // bf16 [H][Is]
+  const __nv_bfloat16* x;
+  const int32_t* ids;
+  const float* gates;
+  void* out;
+  float* h_r;         // [kMaxSlotsRd][I]
+  float* h_s;         // [Is]
+  float2* part_sh;    // [4][Is]
+  unsigned* ctl;      // [0] arrive, [1] depart, [2 + pg] shared-task arrivals
+  int* err;
+  int H, I, E, Is, k;
+  int out_f32;
+  float limit;
+  uint32_t smem_a_part, smem_b_hq, smem_b_hsc, smem_b_hsp, smem_b_part;  // byte offsets
+};
+
+// ---------------------------------------------------------------- small helpers
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ldg_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// 2^e as f32 for e in [-126, 127]
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+// Power-of-two exponent that maps a block whose largest magnitude has f32
+// bits `m` into [2^14, 2^15) (f16's top binade but one), clamped to normal
+// f32 scale factors.
+__device__ __forceinline__ int block_shift(uint32_t m) {
+  if (m == 0u || m >= 0x7F800000u) return 0;
+  const int e = m < 0x00800000u ? -127 : (int)(m >> 23) - 127;
+  return max(-126, min(126, 14 - e));
+}
+
+__device__ __forceinline__ float silu_clamped(float g, float u, float limit) {
+  if (limit > 0.0f) {
+    g = fminf(g, limit);
+    u = fminf(fmaxf(u, -limit), limit);
+  }
+  return (g / (1.0f + expf(-g))) * u;
+}
+
+__device__ __forceinline__ float byte_scale(uint32_t word, int b) { return ds::u8m0_value((word >> (8 * b)) & 0xFFu); }
+
+// ---------------------------------------------------------------- units
+
+enum UnitKind : int { kAShared = 0, kARouted = 1, kBRouted = 2, kBShared = 3, kNone = 4 };
+
+struct Unit {
+  int kind;
+  const uint8_t* ra;   // lane's first 16-byte chunk of row g (null: zeros)
+  const uint8_t* rb;   // same for row g + 8
+  const uint8_t* sra;  // scale bytes of row g at the unit's first K-group (FP4)
+  const uint8_t* srb;
+  int nkg;             // K-groups (FP4) or 32-element chunks (bf16): 1..4
+  int kabs;            // FP4: absolute K-group index of the first group; bf16: first element
+  int slot;
+  int idx;             // unit index inside the CTA (partial-sum slot)
+};
+
+struct Buf {
+  uint4 a[4], b[4];
+  uint32_t sa[4], sb[4];
+};
+
+__device__ __forceinline__ void load_unit(Buf& f, const Unit& u, uint64_t pol) {
+  const int fp4 = (u.kind == kARouted || u.kind == kBRouted);
+  // FP4: K-group stride 64 bytes; bf16: 32-element chunk stride 64 bytes
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const bool on = j < u.nkg && u.kind != kNone;
+    f.a[j] = (on && u.ra) ? ldg_stream(u.ra + 64 * j, pol) : make_uint4(0u, 0u, 0u, 0u);
+    f.b[j] = (on && u.rb) ? ldg_stream(u.rb + 64 * j, pol) : make_uint4(0u, 0u, 0u, 0u);
+    f.sa[j] = (on && fp4 && u.ra) ? ldg_u32(u.sra + 4 * j) : 0x7F7F7F7Fu;
+    f.sb[j] = (on && fp4 && u.rb) ? ldg_u32(u.srb + 4 * j) : 0x7F7F7F7Fu;
+  }
+}
+
+// FP4 unit: per-lane partials of rows g and g+8, already multiplied by the
+// weight-block and activation-block scales.  bsrc(kg) = this lane's B source
+// for K-group kg (16 f16x2 words); bsc(kg, blk) = activation scale of block
+// blk (0..3) of that group.
+template <typename BSrc, typename BScale>
+__device__ __forceinline__ void fp4_unit(const Buf& f, int nkg, int blk_lane0, BSrc bsrc, BScale bsc,
+                                         float& acc0, float& acc1) {
+#pragma unroll
+  for (int kg = 0; kg < 4; ++kg) {
+    if (kg < nkg) {
+      const uint8_t* bp = bsrc(kg);
+      const uint4 x0 = lds128(bp), x1 = lds128(bp + 16), x2 = lds128(bp + 32), x3 = lds128(bp + 48);
+      const uint32_t xr[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
+                               x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+      const uint32_t wa[4] = {f.a[kg].x, f.a[kg].y, f.a[kg].z, f.a[kg].w};
+      const uint32_t wb[4] = {f.b[kg].x, f.b[kg].y, f.b[kg].z, f.b[kg].w};
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint32_t ha[4], hb[4];
+        e2m1x8_to_f16x2(wa[w], ha);
+        e2m1x8_to_f16x2(wb[w], hb);
+        const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
+        const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
+        mma_f16(c, a0, xr[4 * w], xr[4 * w + 1], c);
+        mma_f16(c, a1, xr[4 * w + 2], xr[4 * w + 3], c);
+      }
+      // columns 2t', 2t'+1 of this lane <-> blocks blk_lane0, blk_lane0 + 1 of the group
+      const float f0 = bsc(kg, blk_lane0), f1 = bsc(kg, blk_lane0 + 1);
+      acc0 = fmaf(c[0], byte_scale(f.sa[kg], blk_lane0) * f0, acc0);
+      acc0 = fmaf(c[1], byte_scale(f.sa[kg], blk_lane0 + 1) * f1, acc0);
+      acc1 = fmaf(c[2], byte_scale(f.sb[kg], blk_lane0) * f0, acc1);
+      acc1 = fmaf(c[3], byte_scale(f.sb[kg], blk_lane0 + 1) * f1, acc1);
+    }
+  }
+}
+
+// bf16 unit: C accumulated over the unit's chunks; bsrc(j) = this lane's B
+// source (8 bf16) for chunk j.
+template <typename BSrc>
+__device__ __forceinline__ void bf16_unit(const Buf& f, int nch, BSrc bsrc, float (&c)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j < nch) {
+      const uint4 xv = lds128(bsrc(j));
+      const uint32_t a0[4] = {f.a[j].x, f.b[j].x, f.a[j].y, f.b[j].y};
+      const uint32_t a1[4] = {f.a[j].z, f.b[j].z, f.a[j].w, f.b[j].w};
+      mma_bf16(c, a0, xv.x, xv.y, c);
+      mma_bf16(c, a1, xv.z, xv.w, c);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- the kernel
+
+struct Slots1 {
+  int count;
+  int expert[kMaxSlotsRd];
+  float gate[kMaxSlotsRd];
+};
+
+__global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ Slots1 slots;
+  __shared__ int s_last[kMaxTasksPerCta];
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int H = p.H, I = p.I, Is = p.Is;
+  const bool has_sh = p.sw1 != nullptr;
+  const uint64_t pol = policy_evict_first();
+
+  unsigned char* zero = smem;                                     // kZeroBytes of zeros
+  unsigned char* xb = smem + kZeroBytes;                          // x bf16 [H]
+  unsigned char* xq = xb + 2 * H;                                 // x f16 [H/32][32]
+  float* xsc = reinterpret_cast<float*>(xq + 2 * H);              // [H/32]
+  float2* part_a = reinterpret_cast<float2*>(smem + p.smem_a_part);
+  unsigned char* hq = smem + p.smem_b_hq;                         // [S][I/32][2][32] f16
+  float* hsc = reinterpret_cast<float*>(smem + p.smem_b_hsc);     // [S][I/32]
+  unsigned char* hsp = smem + p.smem_b_hsp;                       // [3][Is] bf16
+  float* part_b = reinterpret_cast<float*>(smem + p.smem_b_part); // [units][16]
+
+  // ---- prologue: slots (warp 0), x staging (all warps)
+  if (tid < kZeroBytes / 4) reinterpret_cast<uint32_t*>(zero)[tid] = 0u;
+  if (tid == 0) s_abort = 0;
+  if (warp == 0) {
+    int id = -1;
+    float gt = 0.f;
+    if (lane < p.k) {
+      id = p.ids[lane];
+      gt = p.gates[lane];
+      if (id >= p.E) {
+        atomicOr(p.err, kErrExpertRange);
+        id = -1;
+      }
+      if (id < 0) id = -1;
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, id);
+    const bool first = id >= 0 && (__ffs(same) - 1) == lane;
+    const unsigned firsts = __ballot_sync(0xffffffffu, first);
+    int rank = 0;
+    for (int j = 0; j < 32; ++j) {
+      const int idj = __shfl_sync(0xffffffffu, id, j);
+      rank += ((firsts >> j) & 1u) && idj < id;
+    }
+    if (first) {
+      slots.expert[rank] = id;
+      slots.gate[rank] = gt;
+    }
+    if (lane == 0) slots.count = __popc(firsts);
+  }
+  for (int b = warp; b < H / 32; b += kWarps) {
+    const __nv_bfloat16 v = p.x[32 * b + lane];
+    reinterpret_cast<__nv_bfloat16*>(xb)[32 * b + lane] = v;
+    const float f = __bfloat162float(v);
+    const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(f) & 0x7FFFFFFFu);
+    const int se = block_shift(m);
+    reinterpret_cast<__half*>(xq)[32 * b + lane] = __float2half_rn(f * exp2i(se));
+    if (lane == 0) xsc[b] = exp2i(-se);
+  }
+  __syncthreads();
+  const int S = slots.count;
+
+  // ---- phase A: task list [shared quarters][routed pair groups]
+  const int upt = H / 512;                       // units per task
+  const int n_sh = has_sh ? 4 * (Is / 8) : 0;
+  const int n_rt = S * (I / 8);
+  const int n_tasks = n_sh + n_rt;
+  const int ta0 = (int)((int64_t)c * n_tasks / G), ta1 = (int)((int64_t)(c + 1) * n_tasks / G);
+  const int nua = (ta1 - ta0) * upt;
+  const uint8_t* my_zero = zero;
+
+  auto unit_a = [&](int u) -> Unit {
+    Unit d;
+    d.idx = u;
+    d.slot = 0;
+    d.sra = d.srb = nullptr;
+    if (u >= nua) {
+      d.kind = kNone;
+      d.ra = d.rb = nullptr;
+      d.nkg = 0;
+      d.kabs = 0;
+      return d;
+    }
+    const int task = ta0 + u / upt, part = u - (u / upt) * upt;
+    d.nkg = 4;
+    if (task < n_sh) {
+      const int pg = task >> 2, q = task & 3;
+      const int row = 8 * pg + g;
+      const int k0 = q * (H / 4) + part * 128;
+      d.kind = kAShared;
+      d.kabs = k0;
+      d.ra = p.sw1 + ((size_t)row * H + k0 + 8 * t) * 2;
+      d.rb = p.sw3 + ((size_t)row * H + k0 + 8 * t) * 2;
+    } else {
+      const int rt = task - n_sh;
+      const int s = rt / (I / 8), pg = rt - s * (I / 8);
+      const size_t row = (size_t)slots.expert[s] * I + 8 * pg + g;
+      const int kg0 = part * 4;
+      d.kind = kARouted;
+      d.slot = s;
+      d.kabs = kg0;
+      d.ra = p.w1 + row * (H / 2) + 64 * kg0 + 16 * t;
+      d.rb = p.w3 + row * (H / 2) + 64 * kg0 + 16 * t;
+      d.sra = p.s1 + row * (H / 32) + 4 * kg0;
+      d.srb = p.s3 + row * (H / 32) + 4 * kg0;
+    }
+    return d;
+  };
+
+  auto compute_a = [&](const Buf& f, const Unit& d) {
+    if (d.kind == kAShared) {
+      float cc[4] = {0.f, 0.f, 0.f, 0.f};
+      const unsigned char* xsrc = (g == 0) ? xb + 2 * (d.kabs + 8 * t) : my_zero;
+      const int step = (g == 0) ? 64 : 0;
+      bf16_unit(f, 4, [&](int j) { return xsrc + step * j; }, cc);
+      if (t == 0) part_a[d.idx * 8 + g] = make_float2(cc[0], cc[2]);
+    } else if (d.kind == kARouted) {
+      float acc0 = 0.f, acc1 = 0.f;
+      const bool bvalid = g == t;                      // column n = t carries block t
+      const int blk0 = 2 * (t & 1);
+      fp4_unit(
+          f, 4, blk0,
+          [&](int kg) -> const uint8_t* {
+            return bvalid ? xq + (size_t)(4 * (d.kabs + kg) + t) * 64 : my_zero;
+          },
+          [&](int kg, int blk) { return xsc[4 * (d.kabs + kg) + blk]; }, acc0, acc1);
+      if (t >= 2) acc0 = acc1 = 0.f;                   // columns 4-7 are empty for one token
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      if (t == 0) part_a[d.idx * 8 + g] = make_float2(acc0, acc1);
+    }
+  };
+
+  {
+    Buf b0, b1;
+    int u = warp;
+    Unit d0 = unit_a(u);
+    load_unit(b0, d0, pol);
+    while (u < nua) {
+      Unit d1 = unit_a(u + kWarps);
+      load_unit(b1, d1, pol);
+      compute_a(b0, d0);
+      u += kWarps;
+      if (u >= nua) break;
+      d0 = unit_a(u + kWarps);
+      load_unit(b0, d0, pol);
+      compute_a(b1, d1);
+      u += kWarps;
+    }
+  }
+  __syncthreads();
+
+  // ---- phase A epilogue: h of every task of this CTA
+  for (int i = tid; i < (ta1 - ta0) * 8; i += kThreads) {
+    const int tl = i >> 3, r = i & 7, task = ta0 + tl;
+    float G1 = 0.f, U1 = 0.f;
+    for (int q = 0; q < upt; ++q) {
+      const float2 v = part_a[(tl * upt + q) * 8 + r];
+      G1 += v.x;
+      U1 += v.y;
+    }
+    if (task < n_sh) {
+      const int pg = task >> 2, qq = task & 3;
+      p.part_sh[(size_t)qq * Is + 8 * pg + r] = make_float2(G1, U1);
+    } else {
+      const int rt = task - n_sh;
+      const int s = rt / (I / 8), pg = rt - s * (I / 8);
+      p.h_r[(size_t)s * I + 8 * pg + r] = silu_clamped(G1, U1, p.limit) * slots.gate[s];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  // shared tasks: the CTA that delivers the fourth quarter of a pair group sums them
+  const int sh_first = ta0, sh_end = min(ta1, n_sh);
+  for (int tl = tid; tl < sh_end - sh_first; tl += kThreads) {
+    const int pg = (sh_first + tl) >> 2;
+    s_last[tl] = atomicAdd(&p.ctl[2 + pg], 1u) == 3u;
+  }
+  __syncthreads();
+  __threadfence();
+  for (int i = tid; i < (sh_end - sh_first) * 8; i += kThreads) {
+    const int tl = i >> 3, r = i & 7;
+    if (!s_last[tl]) continue;
+    const int pg = (sh_first + tl) >> 2;
+    float G1 = 0.f, U1 = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 v = __ldcg(&p.part_sh[(size_t)q * Is + 8 * pg + r]);
+      G1 += v.x;
+      U1 += v.y;
+    }
+    p.h_s[8 * pg + r] = silu_clamped(G1, U1, 10.0f);   // the shared expert always clamps at 10
+    if (r == 0) p.ctl[2 + pg] = 0u;
+  }
+  __threadfence();
+
+  // ---- phase B geometry: output rows [n0, n1) of this CTA
+  const int n0 = (int)((int64_t)c * H / G), n1 = (int)((int64_t)(c + 1) * H / G);
+  const int nkgb = I / 128;
+  const int ups = (nkgb + 3) / 4;                // routed units per (tile, slot)
+  const int ush = has_sh ? Is / 128 : 0;         // shared units per tile (128-wide K slices)
+  const int upt_b = S * ups + ush;               // units per tile
+  const int ntiles = (n1 - n0 + 15) / 16;
+  const int nub = ntiles * upt_b;
+
+  auto unit_b = [&](int u) -> Unit {
+    Unit d;
+    d.idx = u;
+    d.slot = 0;
+    d.sra = d.srb = nullptr;
+    d.ra = d.rb = nullptr;
+    if (u >= nub) {
+      d.kind = kNone;
+      d.nkg = 0;
+      d.kabs = 0;
+      return d;
+    }
+    const int tile = u / upt_b, r = u - tile * upt_b;
+    const int row0 = n0 + 16 * tile + g, row1 = row0 + 8;
+    if (r < S * ups) {
+      const int s = r / ups, kq = r - s * ups;
+      const int kg0 = 4 * kq;
+      d.kind = kBRouted;
+      d.slot = s;
+      d.kabs = kg0;
+      d.nkg = min(4, nkgb - kg0);
+      const size_t e = slots.expert[s];
+      if (row0 < n1) {
+        d.ra = p.w2 + (e * H + row0) * (I / 2) + 64 * kg0 + 16 * t;
+        d.sra = p.s2 + (e * H + row0) * (I / 32) + 4 * kg0;
+      }
+      if (row1 < n1) {
+        d.rb = p.w2 + (e * H + row1) * (I / 2) + 64 * kg0 + 16 * t;
+        d.srb = p.s2 + (e * H + row1) * (I / 32) + 4 * kg0;
+      }
+    } else {
+      const int k0 = (r - S * ups) * 128;
+      d.kind = kBShared;
+      d.kabs = k0;
+      d.nkg = 4;
+      if (row0 < n1) d.ra = p.sw2 + ((size_t)row0 * Is + k0 + 8 * t) * 2;
+      if (row1 < n1) d.rb = p.sw2 + ((size_t)row1 * Is + k0 + 8 * t) * 2;
+    }
+    return d;
+  };
+
+  // L2 prefetch of this CTA's phase-B weights, then its first units' loads
+  if (tid < S) {
+    const size_t e = slots.expert[tid];
+    prefetch_l2(p.w2 + (e * H + n0) * (I / 2), (uint32_t)((n1 - n0) * (I / 2)));
+    const size_t soff = (e * H + n0) * (I / 32), sbytes = (size_t)(n1 - n0) * (I / 32);
+    if (soff % 16 == 0 && sbytes % 16 == 0) prefetch_l2(p.s2 + soff, (uint32_t)sbytes);
+  } else if (tid == kMaxSlotsRd && has_sh) {
+    prefetch_l2(p.sw2 + (size_t)n0 * Is * 2, (uint32_t)((size_t)(n1 - n0) * Is * 2));
+  }
+  Buf b0, b1;
+  Unit d0 = unit_b(warp);
+  load_unit(b0, d0, pol);
+
+  // ---- grid barrier (h of every CTA visible afterwards)
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    atomicAdd(&p.ctl[0], 1u);
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire(&p.ctl[0]) < (unsigned)G) {
+      __nanosleep(64);
+      if (globaltimer_ns() - t0 > kWaitNs) {
+        atomicOr(p.err, kErrWaitTimeout);
+        s_abort = 1;
+        break;
+      }
+    }
+    if (!s_abort && atomicAdd(&p.ctl[1], 1u) == (unsigned)G - 1u) {
+      atomicExch(&p.ctl[0], 0u);
+      atomicExch(&p.ctl[1], 0u);
+    }
+  }
+  __syncthreads();
+  if (s_abort) return;
+
+  // ---- phase B prologue: h as MMA-ready pieces
+  for (int i = warp; i < S * (I / 32); i += kWarps) {
+    const float v = __ldcg(&p.h_r[(size_t)(i / (I / 32)) * I + 32 * (i % (I / 32)) + lane]);
+    const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7FFFFFFFu);
+    const int se = block_shift(m);
+    const float vs = v * exp2i(se);
+    const __half hi = __float2half_rn(vs);
+    const __half lo = __float2half_rn(vs - __half2float(hi));
+    __half* dst = reinterpret_cast<__half*>(hq + (size_t)i * 128);
+    dst[lane] = hi;
+    dst[32 + lane] = lo;
+    if (lane == 0) hsc[i] = exp2i(-se);
+  }
+  if (has_sh) {
+    __nv_bfloat16* d3 = reinterpret_cast<__nv_bfloat16*>(hsp);
+    for (int i = tid; i < Is; i += kThreads) {
+      const float v = __ldcg(&p.h_s[i]);
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      const float r1 = v - __bfloat162float(hi);
+      const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+      d3[i] = hi;
+      d3[Is + i] = mid;
+      d3[2 * Is + i] = lo;
+    }
+  }
+  __syncthreads();
+
+  auto compute_b = [&](const Buf& f, const Unit& d) {
+    if (d.kind == kBRouted) {
+      float acc0 = 0.f, acc1 = 0.f;
+      const bool bvalid = (g & 3) == t;                // hi pieces in columns 0-3, lo in 4-7
+      const int piece = g >> 2;
+      const int blk0 = 2 * (t & 1);
+      const unsigned char* hbase = hq + (size_t)d.slot * (I / 32) * 128;
+      const float* sbase = hsc + (size_t)d.slot * (I / 32);
+      fp4_unit(
+          f, d.nkg, blk0,
+          [&](int kg) -> const uint8_t* {
+            return bvalid ? hbase + (size_t)(4 * (d.kabs + kg) + t) * 128 + 64 * piece : my_zero;
+          },
+          [&](int kg, int blk) { return sbase[4 * (d.kabs + kg) + blk]; }, acc0, acc1);
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+      if (t == 0) {
+        part_b[d.idx * 16 + g] = acc0;
+        part_b[d.idx * 16 + g + 8] = acc1;
+      }
+    } else if (d.kind == kBShared) {
+      float cc[4] = {0.f, 0.f, 0.f, 0.f};
+      const bool bvalid = g < 3;                       // hi, mid, lo pieces in columns 0, 1, 2
+      const unsigned char* src = bvalid ? hsp + ((size_t)g * Is + d.kabs + 8 * t) * 2 : my_zero;
+      const int step = bvalid ? 64 : 0;
+      bf16_unit(f, 4, [&](int j) { return src + step * j; }, cc);
+      float v0 = cc[0] + cc[1], v1 = cc[2] + cc[3];
+      v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+      v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+      if (t == 0) {
+        part_b[d.idx * 16 + g] = v0;
+        part_b[d.idx * 16 + g + 8] = v1;
+      }
+    }
+  };
+
+  {
+    int u = warp;
+    while (u < nub) {
+      Unit d1 = unit_b(u + kWarps);
+      load_unit(b1, d1, pol);
+      compute_b(b0, d0);
+      u += kWarps;
+      if (u >= nub) break;
+      d0 = unit_b(u + kWarps);
+      load_unit(b0, d0, pol);
+      compute_b(b1, d1);
+      u += kWarps;
+    }
+  }
+  __syncthreads();
+
+  // ---- combine: routed slots in ascending expert id, then the shared expert
+  for (int n = n0 + tid; n < n1; n += kThreads) {
+    const int tile = (n - n0) >> 4, rr = (n - n0) & 15;
+    const float* pb = part_b + (size_t)tile * upt_b * 16 + rr;
+    float routed = 0.f;
+    for (int s = 0; s < S; ++s) {
+      float v = 0.f;
+      for (int q = 0; q < ups; ++q) v += pb[(s * ups + q) * 16];
+      routed += v;
+    }
+    float sh = 0.f;
+    for (int q = 0; q < ush; ++q) sh += pb[(S * ups + q) * 16];
+    if (has_sh) routed += __bfloat162float(__float2bfloat16_rn(sh));
+    if (p.out_f32)
+      static_cast<float*>(p.out)[n] = routed;
+    else
+      static_cast<__nv_bfloat16*>(p.out)[n] = __float2bfloat16_rn(routed);
+  }
+}
+
+struct RdLayout {
+  size_t h_r, h_s, part_sh, ctl, total;
+  uint32_t a_part, b_hq, b_hsc, b_hsp, b_part, smem;
+};
+
+size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+RdLayout rd_layout(const DsMoeDesc& d) {
+  RdLayout L;
+  const size_t H = d.hidden, I = d.inter, Is = d.shared_w1 ? d.shared_inter : 0;
+  const int S = std::min(d.top_k, d.n_experts);
+  size_t o = 256;  // [0, 256): error word (offset 0), as every decode path keeps it
+  L.ctl = o;     o += up256((2 + Is / 8) * 4);
+  L.h_r = o;     o += up256((size_t)kMaxSlotsRd * I * 4);
+  L.h_s = o;     o += up256(Is * 4 + 4);
+  L.part_sh = o; o += up256(4 * Is * 8 + 8);
+  L.total = o;
+  // shared memory (one union for phase A and phase B after the zero block)
+  const int G = ds::sm_count();
+  const int upt = (int)(H / 512);
+  const int n_tasks = (Is ? 4 * (int)(Is / 8) : 0) + S * (int)(I / 8);
+  const int tasks_cta = (n_tasks + G - 1) / G + 1;
+  uint32_t a = kZeroBytes + 4 * (uint32_t)H + 4 * (uint32_t)(H / 32);
+  a = (a + 15) / 16 * 16;
+  L.a_part = a;
+  a += (uint32_t)tasks_cta * upt * 8 * 8;
+  uint32_t b = kZeroBytes;
+  L.b_hq = b;
+  b += (uint32_t)(S * (I / 32) * 128);
+  L.b_hsc = b;
+  b += (uint32_t)(S * (I / 32) * 4);
+  b = (b + 15) / 16 * 16;
+  L.b_hsp = b;
+  b += (uint32_t)(3 * Is * 2);
+  b = (b + 15) / 16 * 16;
+  L.b_part = b;
+  const int rows_cta = (int)((H + G - 1) / G) + 1;
+  const int ntiles = (rows_cta + 15) / 16;
+  const int ups = (int)((I / 128 + 3) / 4);
+  b += (uint32_t)(ntiles * (S * ups + (Is ? (int)(Is / 128) : 0)) * 16 * 4);
+  L.smem = std::max(a, b);
+  return L;
+}
+
+}  // namespace
+
+bool rd_supported(const DecodeArgs& a) {
+  const DsMoeDesc& d = a.d;
+  if (a.x_f32 || a.tokens != 1 || d.w1.format != DS_FMT_FP4) return false;
+  if (!d.route_before_down) return false;
+  if (a.out_sh != nullptr || a.sh_w2_ld != 0 || a.sh_row0 != 0 || a.sh_row1 != (1 << 30)) return false;
+  if (d.hidden % 512 != 0 || d.inter % 128 != 0 || d.top_k > kMaxSlotsRd) return false;
+  const bool sh = d.shared_w1 != nullptr;
+  if (sh && d.shared_inter % 128 != 0) return false;
+  if (!ds::aligned(a.x, 16) || !ds::aligned(d.w1.data, 16) || !ds::aligned(d.w3.data, 16) ||
+      !ds::aligned(d.w2.data, 16) || !ds::aligned(d.w1.scales, 4) || !ds::aligned(d.w3.scales, 4) ||
+      !ds::aligned(d.w2.scales, 4))
+    return false;
+  if (sh && (!ds::aligned(d.shared_w1, 16) || !ds::aligned(d.shared_w3, 16) || !ds::aligned(d.shared_w2, 16)))
+    return false;
+  const RdLayout L = rd_layout(d);
+  const int G = ds::sm_count();
+  const int n_tasks = (sh ? 4 * (d.shared_inter / 8) : 0) + std::min(d.top_k, d.n_experts) * (d.inter / 8);
+  if ((n_tasks + G - 1) / G + 1 > kMaxTasksPerCta) return false;
+  return L.smem <= 200 * 1024;
+}
+
+size_t rd_workspace_bytes(const DsMoeDesc& d) { return rd_layout(d).total; }
+
+size_t rd_control_bytes(const DsMoeDesc& d) {
+  const RdLayout L = rd_layout(d);
+  return L.h_r;  // error word + control words precede h
+}
+
+int launch_rd(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const DsMoeDesc& d = a.d;
+  const RdLayout L = rd_layout(d);
+  DS_REQUIRE(workspace_bytes >= L.total, DS_EINVAL, "moe_decode: workspace %zu bytes < %zu (register-dequant path)",
+             workspace_bytes, L.total);
+  char* ws = static_cast<char*>(workspace);
+  RdParams p;
+  p.w1 = static_cast<const uint8_t*>(d.w1.data);
+  p.w3 = static_cast<const uint8_t*>(d.w3.data);
+  p.w2 = static_cast<const uint8_t*>(d.w2.data);
+  p.s1 = static_cast<const uint8_t*>(d.w1.scales);
+  p.s3 = static_cast<const uint8_t*>(d.w3.scales);
+  p.s2 = static_cast<const uint8_t*>(d.w2.scales);
+  const bool sh = d.shared_w1 != nullptr;
+  p.sw1 = sh ? static_cast<const uint8_t*>(d.shared_w1) : nullptr;
+  p.sw3 = sh ? static_cast<const uint8_t*>(d.shared_w3) : nullptr;
+  p.sw2 = sh ? static_cast<const uint8_t*>(d.shared_w2) : nullptr;
+  p.x = static_cast<const __nv_bfloat16*>(a.x);
+  p.ids = a.ids;
+  p.gates = a.gates;
+  p.out = a.out;
+  p.h_r = reinterpret_cast<float*>(ws + L.h_r);
+  p.h_s = reinterpret_cast<float*>(ws + L.h_s);
+  p.part_sh = reinterpret_cast<float2*>(ws + L.part_sh);
+  p.ctl = reinterpret_cast<unsigned*>(ws + L.ctl);
+  p.err = a.err;
+  p.H = d.hidden;
+  p.I = d.inter;
+  p.E = d.n_experts;
+  p.Is = sh ? d.shared_inter : 0;
+  p.k = d.top_k;
+  p.out_f32 = d.out_f32 ? 1 : 0;
+  p.limit = d.swiglu_limit;
+  p.smem_a_part = L.a_part;
+  p.smem_b_hq = L.b_hq;
+  p.smem_b_hsc = L.b_hsc;
+  p.smem_b_hsp = L.b_hsp;
+  p.smem_b_part = L.b_part;
+  static const cudaError_t attr_rc =
+      cudaFuncSetAttribute(rd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  DS_CHECK_CUDA(attr_rc);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ds::sm_count());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L.smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, rd_kernel, p));
+  return DS_OK;
+}
+
+}  // namespace decode
+}  // namespace ds

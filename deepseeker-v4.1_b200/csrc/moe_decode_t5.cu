@@ -261,7 +261,8 @@ __device__ void tail_h_shared(const T5Params& p, int r0, int lane) {
   sum_two<kT>(p.part_sh + (size_t)i * kT, p.part_sh + ((size_t)KP * Is + i) * kT, (size_t)Is * kT, KP, g, u);
 #pragma unroll
   for (int t = 0; t < kT; ++t) {
-    const float h = silu_glu(g[t], u[t], p.limit);
+    // the shared expert always clamps at 10 (src/deepseeker/mlx_runner.py:776-781)
+    const float h = silu_glu(g[t], u[t], 10.0f);
     const __nv_bfloat16 hi = __float2bfloat16_rn(h);
     p.hb[(size_t)(2 * t) * Is + i] = hi;
     p.hb[(size_t)(2 * t + 1) * Is + i] = __float2bfloat16_rn(h - __bfloat162float(hi));

@@ -247,7 +247,7 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     key = (device.index if device.index is not None else torch.cuda.current_device(), 0)
     ws = _WS.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WS[key] = ws
     return ws
 
@@ -674,7 +674,7 @@ class DecodeGraph:
         self.w = torch.empty(tokens, top_k, dtype=torch.float32, device=device)
         self.ids = torch.empty(tokens, top_k, dtype=torch.int32, device=device)
         self.out = torch.empty(tokens, H, dtype=torch.bfloat16, device=device)
-        self.workspace = torch.empty(weights.decode_workspace_bytes(tokens, top_k), dtype=torch.uint8, device=device)
+        self.workspace = torch.zeros(weights.decode_workspace_bytes(tokens, top_k), dtype=torch.uint8, device=device)
         self._step()                      # first call outside the capture: module load, attributes, caches
         torch.cuda.synchronize(device)
         self.graph = torch.cuda.CUDAGraph()
