@@ -734,7 +734,7 @@ WsLayout ws_layout(const DsMoeDesc* d, int64_t tokens) {
   const bool sh = d->shared_w1 != nullptr;
   w.h_stride = (int)align_up(std::max(d->inter, sh ? d->shared_inter : 0), 4);
   w.err_off = 0;
-  w.h_off = 256;
+  w.h_off = ds::decode::kWsReserved;
   w.total = w.h_off + (size_t)(w.max_slots + 1) * tokens * w.h_stride * sizeof(float);
   w.total = align_up(w.total, 256);
   return w;
@@ -920,7 +920,7 @@ namespace {
 
 // Scratch limit: 8 MiB.  The call runs the kernels ds_moe_decode would run
 // with a workspace of this size (dispatch() above): the fastest path whose
-// scratch fits.  The generic kernels need 256 + (slots + 1) * tokens * stride
+// scratch fits.  The generic kernels need 4096 + (slots + 1) * tokens * stride
 // * 4 bytes (slots = min(tokens * k, experts), stride = max(inter,
 // shared_inter)); config 2's layer (hidden 4096, inter 2048, top-8) fits every
 // path at one token.

@@ -8,6 +8,14 @@ namespace ds {
 namespace decode {
 
 constexpr int kMaxTokens = 8;
+
+// Bytes [0, kWsReserved) of every decode workspace: the error word at offset
+// 0 (written by every path) and, from byte 256, the single-token kernel's
+// control words (grid barrier, shared-expert arrival counters), which must be
+// zero before a call and are left zero by every call that completes.  No
+// path lays any other data out below kWsReserved, so calls of different
+// layers and paths can share one workspace.
+constexpr size_t kWsReserved = 4096;
 constexpr int kMaxEntries = 128;  // tokens * top_k
 
 // Error bits written to the workspace error word.

@@ -549,7 +549,7 @@ Q3Layout q3_layout(const DsMoeDesc& d, int T) {
   const int Is = d.shared_w1 ? d.shared_inter : 0;
   L.max_chunks = (S + kChunk - 1) / kChunk;
   const size_t blocks = (size_t)L.max_chunks * kChunk * T * (d.inter / 64);
-  size_t o = 256;                                 // error word
+  size_t o = kWsReserved;                         // error word (offset 0), reserved control block
   L.hpk = o;  o += up256(blocks * kPk * 4);
   L.hsx = o;  o += up256(blocks * sizeof(float2));
   L.hsh = o;  o += up256((size_t)kShGU * T * 2 * Is * 4);

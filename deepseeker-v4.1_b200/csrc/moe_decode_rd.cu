@@ -38,7 +38,8 @@
 //   rounded to bf16, reference mlx_forward.py:388-419 / mlx_runner.py:776-781)
 //   happens in the CTA with no further pass.
 //
-// Control words (grid barrier, shared-task counters) live in the workspace,
+// Control words (grid barrier, shared-task counters) live in the workspace's
+// reserved block [256, kWsReserved), where no path writes anything else; they
 // must be zero before the first call and are left zero by every call that
 // completes.  Every wait is bounded by %globaltimer (2 s); on expiry the
 // kernel sets kErrWaitTimeout in the error word and stops waiting.
@@ -625,8 +626,8 @@ RdLayout rd_layout(const DsMoeDesc& d) {
   RdLayout L;
   const size_t H = d.hidden, I = d.inter, Is = d.shared_w1 ? d.shared_inter : 0;
   const int S = std::min(d.top_k, d.n_experts);
-  size_t o = 256;  // [0, 256): error word (offset 0), as every decode path keeps it
-  L.ctl = o;     o += up256((2 + Is / 8) * 4);
+  L.ctl = 256;   // control words in the reserved block after the error word
+  size_t o = kWsReserved;
   L.h_r = o;     o += up256((size_t)kMaxSlotsRd * I * 4);
   L.h_s = o;     o += up256(Is * 4 + 4);
   L.part_sh = o; o += up256(4 * Is * 8 + 8);
@@ -668,6 +669,7 @@ bool rd_supported(const DecodeArgs& a) {
   if (d.hidden % 512 != 0 || d.inter % 128 != 0 || d.top_k > kMaxSlotsRd) return false;
   const bool sh = d.shared_w1 != nullptr;
   if (sh && d.shared_inter % 128 != 0) return false;
+  if (sh && (size_t)(256 + 4 * (2 + d.shared_inter / 8)) > kWsReserved) return false;  // control words fit
   if (!ds::aligned(a.x, 16) || !ds::aligned(d.w1.data, 16) || !ds::aligned(d.w3.data, 16) ||
       !ds::aligned(d.w2.data, 16) || !ds::aligned(d.w1.scales, 4) || !ds::aligned(d.w3.scales, 4) ||
       !ds::aligned(d.w2.scales, 4))
@@ -683,10 +685,7 @@ bool rd_supported(const DecodeArgs& a) {
 
 size_t rd_workspace_bytes(const DsMoeDesc& d) { return rd_layout(d).total; }
 
-size_t rd_control_bytes(const DsMoeDesc& d) {
-  const RdLayout L = rd_layout(d);
-  return L.h_r;  // error word + control words precede h
-}
+size_t rd_control_bytes(const DsMoeDesc&) { return kWsReserved; }
 
 int launch_rd(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t st) {
   const DsMoeDesc& d = a.d;

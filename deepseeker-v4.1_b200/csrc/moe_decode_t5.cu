@@ -786,7 +786,7 @@ T5Layout t5_layout(const DsMoeDesc& d, int T) {
   L.KPb = (int)(I / (512 * kStagesPerItem));
   L.KPbs = Is ? (int)(Is / (128 * kStagesPerItem)) : 0;
   size_t o = 0;
-  L.ints = o;        o += 256;
+  L.ints = o;        o = kWsReserved;            // [0] error word, [1] slot count; reserved block
   L.slot_expert = o; o += up256(kMaxSlots5 * 4);
   L.gate = o;        o += up256(kMaxSlots5 * kMaxT * 4);
   L.xq = o;          o += up256(kPieceRows * H / 2);

@@ -172,7 +172,12 @@ typedef struct DsMoeDesc {
                             with scale atoms); DS_ENOTSUP otherwise.         */
 } DsMoeDesc;
 
-/* Workspace bytes ds_moe_decode needs for `tokens` rows. */
+/* Workspace bytes ds_moe_decode needs for `tokens` rows.  The first 4096
+ * bytes of a workspace are reserved (error word, control words of the
+ * single-token kernel): zero them once before the first call with that
+ * workspace (e.g. allocate it zero-filled); every call that completes leaves
+ * the control words zero, so layers and token counts may share it.  After a
+ * call that reported a bounded-wait timeout, zero it again. */
 int ds_moe_decode_workspace_size(const DsMoeDesc* desc, int64_t tokens,
                                  size_t* bytes);
 
@@ -285,7 +290,7 @@ int ds_dense_swiglu(const float* x, int64_t tokens, int hidden, int inter, int n
  *     so results equal ds_moe_decode's bit for bit whenever
  *     ds_moe_decode_workspace_size() <= the limit, and stay within the
  *     decode tolerance (rel-L2 <= 1e-3 of the f32 oracle) otherwise.
- *   - Limit: a layer whose generic-path scratch (256 + (min(tokens*k, E) + 1)
+ *   - Limit: a layer whose generic-path scratch (4096 + (min(tokens*k, E) + 1)
  *     * tokens * max(inter, shared_inter) * 4 bytes, rounded up to 256) exceeds
  *     the array is rejected with DS_ERANGE.
  *   - The first call on each device resolves the array's address (setup,
