@@ -11,25 +11,27 @@
 // bytes-in-flight come from every warp issuing its next unit's loads before
 // it computes the current one.
 //
-// Dot products.  FP4 codes are decoded in registers (cvt.rn.f16x2.e2m1x2:
-// exact) into mma.sync m16n8k16 A fragments (f16, f32 accumulate).  The B
-// operand is the activation laid out so that column n of the 16x8 B tile
-// only carries the K elements of the lane group t = n, i.e. of ONE 32-element
-// weight block: C[row][n] is then the dot product of that row with that
-// block, and each block's ue8m0 scale (times the activation block's
-// power-of-two scale) multiplies its own f32 partial.  Dequant is exact, the
-// products are exact, the accumulation is f32.  Activations enter as f16
-// scaled per 32-block by a power of two (bf16 x: exactly; the SwiGLU
-// intermediate h: as an f16 hi + lo pair, ~22 significant bits, in columns
-// 0-3 and 4-7).  The shared expert's bf16 weights feed bf16 MMAs directly
-// (x exact; its h as three bf16 pieces).
+// Dot products.  FP4 codes become e4m3 bytes in registers with integer ops
+// alone (code c -> ((c&7)<<2) | ((c&8)<<4), the value times 2^-6, exact for
+// every code including the subnormal 0.5), the A fragments of mma.sync
+// m16n8k32 e4m3 (f32 accumulate).  The B operand is the activation laid out
+// so that column n of the 32x8 B tile only carries the K elements of lane
+// group t = n, i.e. of ONE 32-element weight block: C[row][n] is then the dot
+// product of that row with that block, and each block's ue8m0 scale (times
+// the activation block's power-of-two scale) multiplies its own f32 partial.
+// Dequant is exact, products are exact, accumulation is f32.  Activations
+// enter as e4m3 pieces of a per-32-block power-of-two scaling: bf16 x as two
+// pieces (exactly), the SwiGLU intermediate h as four (~16 significant bits,
+// two MMA chains), in columns 0-3 / 4-7.  The shared expert's bf16 weights
+// feed bf16 MMAs directly (x exact; its h as three bf16 pieces).
 //
 // Phase A (gate/up): tasks of 8 rows of W1 and the same 8 rows of W3 over the
 //   full K (a routed expert), or over a K quarter (the shared expert, whose
 //   rows are 4x wider); each CTA takes a contiguous range of tasks, so h of a
 //   routed task is finished inside the CTA (SwiGLU clamps, route weight); the
-//   four quarters of a shared task are summed by the CTA that finishes last
-//   (arrival counter).
+//   four quarters of a shared task are summed by the CTA that finishes last,
+//   and each 32-row block of a routed h is cut into its e4m3 pieces by the
+//   CTA that delivers its last 8 rows (arrival counters), once for all CTAs.
 // Grid barrier (bounded spin).  Before it, every CTA prefetches its phase-B
 //   weights into L2 and issues its first phase-B unit's loads.
 // Phase B (down + combine): each CTA owns a contiguous range of ~H/G output
@@ -43,6 +45,8 @@
 // must be zero before the first call and are left zero by every call that
 // completes.  Every wait is bounded by %globaltimer (2 s); on expiry the
 // kernel sets kErrWaitTimeout in the error word and stops waiting.
+#include <cuda_fp8.h>
+
 #include <algorithm>
 
 #include "moe_decode.cuh"
@@ -75,10 +79,14 @@ struct RdParams {
   const int32_t* ids;
   const float* gates;
   void* out;
-  float* h_r;         // [kMaxSlotsRd][I]
-  float* h_s;         // [Is]
+  float* h_r;         // [kMaxSlotsRd][I] f32
+  uint8_t* hq8;       // [kMaxSlotsRd][I/32][4 pieces][32] e4m3 (piece byte order)
+  float* hsc;         // [kMaxSlotsRd][I/32] scale of each block's pieces (incl. 2^6)
+  float* h_s;         // [Is] f32
+  __nv_bfloat16* hsp; // [3][Is] bf16 pieces of h_s
   float2* part_sh;    // [4][Is]
-  unsigned* ctl;      // [0] arrive, [1] depart, [2 + pg] shared-task arrivals
+  unsigned* ctl;      // [0] arrive, [1] depart, [2 + pg] shared-task arrivals,
+                      // [2 + Is/8 + slot*(I/32) + blk] routed h-block arrivals
   int* err;
   int H, I, E, Is, k;
   int out_f32;
@@ -114,18 +122,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 
 __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
-// 2^e as f32 for e in [-126, 127]
-__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
-
-// Power-of-two exponent that maps a block whose largest magnitude has f32
-// bits `m` into [2^14, 2^15) (f16's top binade but one), clamped to normal
-// f32 scale factors.
-__device__ __forceinline__ int block_shift(uint32_t m) {
-  if (m == 0u || m >= 0x7F800000u) return 0;
-  const int e = m < 0x00800000u ? -127 : (int)(m >> 23) - 127;
-  return max(-126, min(126, 14 - e));
-}
-
 __device__ __forceinline__ float silu_clamped(float g, float u, float limit) {
   if (limit > 0.0f) {
     g = fminf(g, limit);
@@ -134,7 +130,64 @@ __device__ __forceinline__ float silu_clamped(float g, float u, float limit) {
   return (g / (1.0f + expf(-g))) * u;
 }
 
-__device__ __forceinline__ float byte_scale(uint32_t word, int b) { return ds::u8m0_value((word >> (8 * b)) & 0xFFu); }
+
+// e4m3 bytes (value = e2m1 * 2^-6) of the low / high nibbles of the four
+// bytes of w: code c -> sign (c & 8) << 4 | magnitude (c & 7) << 2.
+__device__ __forceinline__ uint32_t fp4lo_e4m3(uint32_t w) {
+  return ((w << 2) & 0x1C1C1C1Cu) | ((w << 4) & 0x80808080u);
+}
+__device__ __forceinline__ uint32_t fp4hi_e4m3(uint32_t w) {
+  return ((w >> 2) & 0x1C1C1C1Cu) | (w & 0x80808080u);
+}
+
+// D += A(16x32, e4m3, row) * B(32x8, e4m3, col), f32 accumulate.
+__device__ __forceinline__ void mma_e4m3(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Exponent bits of ue8m0 byte i (0..3) of w as an f32 (2^(b-127) for b in
+// 1..254; byte 0 gives 0, byte 255 gives inf: a NaN-coded block makes the
+// sums it enters non-finite).
+__device__ __forceinline__ float ue8m0_lo(uint32_t w) { return __uint_as_float((w << 23) & 0x7F800000u); }
+__device__ __forceinline__ float ue8m0_hi(uint32_t w) { return __uint_as_float((w << 15) & 0x7F800000u); }
+
+// Byte position of element j (0..31) inside a 32-byte e4m3 piece: per group
+// of eight elements, the four even ones then the four odd ones -- the order
+// in which lane group t's B registers meet the low / high nibbles of a word.
+__device__ __forceinline__ int piece_pos(int j) { return (j >> 3) * 8 + (j & 1) * 4 + ((j & 7) >> 1); }
+
+__device__ __forceinline__ uint8_t to_e4m3(float v) {
+  return (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ float from_e4m3(uint8_t b) {
+  return __half2float(__half(__nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3)));
+}
+
+// Element j of a 32-block (one per lane): scale the block so that its largest
+// magnitude lands in [2^7, 2^8) and write `np` e4m3 pieces (each the
+// rounding of what the earlier ones left) to dst[p * 32 + piece_pos(j)];
+// returns the factor that undoes the scaling times 2^6 (the e2m1 -> e4m3
+// offset of the weights).
+__device__ __forceinline__ float split_e4m3(float v, int np, uint8_t* dst, int lane) {
+  const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7FFFFFFFu);
+  int se = 0;
+  if (m != 0u && m < 0x7F800000u) {
+    const int e = m < 0x00800000u ? -127 : (int)(m >> 23) - 127;
+    se = max(-120, min(120, 7 - e));
+  }
+  float r = v * __uint_as_float((uint32_t)(se + 127) << 23);
+  const int pos = piece_pos(lane);
+  for (int p = 0; p < np; ++p) {
+    const uint8_t q = to_e4m3(r);
+    dst[p * 32 + pos] = q;
+    r -= from_e4m3(q);
+  }
+  return __uint_as_float((uint32_t)(6 - se + 127) << 23);
+}
 
 // ---------------------------------------------------------------- units
 
@@ -171,38 +224,43 @@ __device__ __forceinline__ void load_unit(Buf& f, const Unit& u, uint64_t pol) {
 }
 
 // FP4 unit: per-lane partials of rows g and g+8, already multiplied by the
-// weight-block and activation-block scales.  bsrc(kg) = this lane's B source
-// for K-group kg (16 f16x2 words); bsc(kg, blk) = activation scale of block
-// blk (0..3) of that group.
-template <typename BSrc, typename BScale>
-__device__ __forceinline__ void fp4_unit(const Buf& f, int nkg, int blk_lane0, BSrc bsrc, BScale bsc,
+// weight-block and activation-block scales.  For K-group kg and MMA chain ch
+// (NCH chains of two pieces each), bsrc(kg, ch) = this lane's 32-byte B
+// source; bsc(kg, blk) = the activation scale of block blk (0..3) of the
+// group.  Lane (g, t) holds columns 2(t&1), 2(t&1)+1 of its pieces: blocks
+// blk0 = 2(t&1) and blk0 + 1.
+template <int NCH, typename BSrc, typename BScale>
+__device__ __forceinline__ void fp4_unit(const Buf& f, int nkg, int blk0, BSrc bsrc, BScale bsc,
                                          float& acc0, float& acc1) {
 #pragma unroll
   for (int kg = 0; kg < 4; ++kg) {
     if (kg < nkg) {
-      const uint8_t* bp = bsrc(kg);
-      const uint4 x0 = lds128(bp), x1 = lds128(bp + 16), x2 = lds128(bp + 32), x3 = lds128(bp + 48);
-      const uint32_t xr[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
-                               x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
       const uint32_t wa[4] = {f.a[kg].x, f.a[kg].y, f.a[kg].z, f.a[kg].w};
       const uint32_t wb[4] = {f.b[kg].x, f.b[kg].y, f.b[kg].z, f.b[kg].w};
+      uint32_t A[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        A[j][0] = fp4lo_e4m3(wa[j]);
+        A[j][1] = fp4lo_e4m3(wb[j]);
+        A[j][2] = fp4hi_e4m3(wa[j]);
+        A[j][3] = fp4hi_e4m3(wb[j]);
+      }
       float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        uint32_t ha[4], hb[4];
-        e2m1x8_to_f16x2(wa[w], ha);
-        e2m1x8_to_f16x2(wb[w], hb);
-        const uint32_t a0[4] = {ha[0], hb[0], ha[1], hb[1]};
-        const uint32_t a1[4] = {ha[2], hb[2], ha[3], hb[3]};
-        mma_f16(c, a0, xr[4 * w], xr[4 * w + 1], c);
-        mma_f16(c, a1, xr[4 * w + 2], xr[4 * w + 3], c);
+      for (int ch = 0; ch < NCH; ++ch) {
+        const uint8_t* bp = bsrc(kg, ch);
+        const uint4 q0 = lds128(bp), q1 = lds128(bp + 16);
+        mma_e4m3(c, A[0], q0.x, q0.y);
+        mma_e4m3(c, A[1], q0.z, q0.w);
+        mma_e4m3(c, A[2], q1.x, q1.y);
+        mma_e4m3(c, A[3], q1.z, q1.w);
       }
-      // columns 2t', 2t'+1 of this lane <-> blocks blk_lane0, blk_lane0 + 1 of the group
-      const float f0 = bsc(kg, blk_lane0), f1 = bsc(kg, blk_lane0 + 1);
-      acc0 = fmaf(c[0], byte_scale(f.sa[kg], blk_lane0) * f0, acc0);
-      acc0 = fmaf(c[1], byte_scale(f.sa[kg], blk_lane0 + 1) * f1, acc0);
-      acc1 = fmaf(c[2], byte_scale(f.sb[kg], blk_lane0) * f0, acc1);
-      acc1 = fmaf(c[3], byte_scale(f.sb[kg], blk_lane0 + 1) * f1, acc1);
+      const float f0 = bsc(kg, blk0), f1 = bsc(kg, blk0 + 1);
+      const uint32_t sa = f.sa[kg] >> (8 * blk0), sb = f.sb[kg] >> (8 * blk0);
+      acc0 = fmaf(c[0], ue8m0_lo(sa) * f0, acc0);
+      acc0 = fmaf(c[1], ue8m0_hi(sa) * f1, acc0);
+      acc1 = fmaf(c[2], ue8m0_lo(sb) * f0, acc1);
+      acc1 = fmaf(c[3], ue8m0_hi(sb) * f1, acc1);
     }
   }
 }
@@ -245,10 +303,10 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
 
   unsigned char* zero = smem;                                     // kZeroBytes of zeros
   unsigned char* xb = smem + kZeroBytes;                          // x bf16 [H]
-  unsigned char* xq = xb + 2 * H;                                 // x f16 [H/32][32]
+  unsigned char* xq = xb + 2 * H;                                 // x e4m3 [H/32][2 pieces][32]
   float* xsc = reinterpret_cast<float*>(xq + 2 * H);              // [H/32]
   float2* part_a = reinterpret_cast<float2*>(smem + p.smem_a_part);
-  unsigned char* hq = smem + p.smem_b_hq;                         // [S][I/32][2][32] f16
+  unsigned char* hq = smem + p.smem_b_hq;                         // [S][I/32][4][32] e4m3
   float* hsc = reinterpret_cast<float*>(smem + p.smem_b_hsc);     // [S][I/32]
   unsigned char* hsp = smem + p.smem_b_hsp;                       // [3][Is] bf16
   float* part_b = reinterpret_cast<float*>(smem + p.smem_b_part); // [units][16]
@@ -285,11 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   for (int b = warp; b < H / 32; b += kWarps) {
     const __nv_bfloat16 v = p.x[32 * b + lane];
     reinterpret_cast<__nv_bfloat16*>(xb)[32 * b + lane] = v;
-    const float f = __bfloat162float(v);
-    const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(f) & 0x7FFFFFFFu);
-    const int se = block_shift(m);
-    reinterpret_cast<__half*>(xq)[32 * b + lane] = __float2half_rn(f * exp2i(se));
-    if (lane == 0) xsc[b] = exp2i(-se);
+    const float sc = split_e4m3(__bfloat162float(v), 2, xq + 64 * b, lane);   // bf16: two pieces are exact
+    if (lane == 0) xsc[b] = sc;
   }
   __syncthreads();
   const int S = slots.count;
@@ -350,17 +405,19 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
       if (t == 0) part_a[d.idx * 8 + g] = make_float2(cc[0], cc[2]);
     } else if (d.kind == kARouted) {
       float acc0 = 0.f, acc1 = 0.f;
-      const bool bvalid = g == t;                      // column n = t carries block t
-      const int blk0 = 2 * (t & 1);
-      fp4_unit(
-          f, 4, blk0,
-          [&](int kg) -> const uint8_t* {
-            return bvalid ? xq + (size_t)(4 * (d.kabs + kg) + t) * 64 : my_zero;
+      // column n = g' carries block t' = n & 3 of the group, piece n >> 2
+      const bool bvalid = (g & 3) == t;
+      const int piece = g >> 2;
+      fp4_unit<1>(
+          f, 4, 2 * (t & 1),
+          [&](int kg, int) -> const uint8_t* {
+            return bvalid ? xq + (size_t)((4 * (d.kabs + kg) + t) * 2 + piece) * 32 : my_zero;
           },
           [&](int kg, int blk) { return xsc[4 * (d.kabs + kg) + blk]; }, acc0, acc1);
-      if (t >= 2) acc0 = acc1 = 0.f;                   // columns 4-7 are empty for one token
       acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
       acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
       if (t == 0) part_a[d.idx * 8 + g] = make_float2(acc0, acc1);
     }
   };
@@ -404,27 +461,59 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   }
   __threadfence();
   __syncthreads();
-  // shared tasks: the CTA that delivers the fourth quarter of a pair group sums them
-  const int sh_first = ta0, sh_end = min(ta1, n_sh);
-  for (int tl = tid; tl < sh_end - sh_first; tl += kThreads) {
-    const int pg = (sh_first + tl) >> 2;
-    s_last[tl] = atomicAdd(&p.ctl[2 + pg], 1u) == 3u;
+  // Arrivals: a shared pair group is complete with its fourth quarter, a
+  // routed h block (32 rows) with its fourth pair group; the CTA that
+  // completes one finishes it for everybody.
+  unsigned* ctl_sh = p.ctl + 2;
+  unsigned* ctl_blk = p.ctl + 2 + Is / 8;
+  for (int tl = tid; tl < ta1 - ta0; tl += kThreads) {
+    const int task = ta0 + tl;
+    if (task < n_sh) {
+      s_last[tl] = atomicAdd(&ctl_sh[task >> 2], 1u) == 3u;
+    } else {
+      const int rt = task - n_sh;
+      const int sl = rt / (I / 8), pg = rt - sl * (I / 8);
+      s_last[tl] = atomicAdd(&ctl_blk[sl * (I / 32) + (pg >> 2)], 1u) == 3u;
+    }
   }
   __syncthreads();
   __threadfence();
-  for (int i = tid; i < (sh_end - sh_first) * 8; i += kThreads) {
-    const int tl = i >> 3, r = i & 7;
+  for (int tl = warp; tl < ta1 - ta0; tl += kWarps) {
     if (!s_last[tl]) continue;
-    const int pg = (sh_first + tl) >> 2;
-    float G1 = 0.f, U1 = 0.f;
+    const int task = ta0 + tl;
+    if (task < n_sh) {
+      // shared pair group: h of its 8 rows from the four quarters, and its bf16 pieces
+      const int pg = task >> 2;
+      if (lane < 8) {
+        float G1 = 0.f, U1 = 0.f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 v = __ldcg(&p.part_sh[(size_t)q * Is + 8 * pg + r]);
-      G1 += v.x;
-      U1 += v.y;
+        for (int q = 0; q < 4; ++q) {
+          const float2 v = __ldcg(&p.part_sh[(size_t)q * Is + 8 * pg + lane]);
+          G1 += v.x;
+          U1 += v.y;
+        }
+        const int row = 8 * pg + lane;
+        const float h = silu_clamped(G1, U1, 10.0f);   // the shared expert always clamps at 10
+        const __nv_bfloat16 hi = __float2bfloat16_rn(h);
+        const float r1 = h - __bfloat162float(hi);
+        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+        p.hsp[row] = hi;
+        p.hsp[Is + row] = mid;
+        p.hsp[2 * Is + row] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+        if (lane == 0) ctl_sh[pg] = 0u;
+      }
+    } else {
+      // routed h block: four e4m3 pieces of its 32 values and their scale
+      const int rt = task - n_sh;
+      const int sl = rt / (I / 8), blk = (rt - sl * (I / 8)) >> 2;
+      const size_t bi = (size_t)sl * (I / 32) + blk;
+      const float v = __ldcg(&p.h_r[(size_t)sl * I + 32 * blk + lane]);
+      const float sc = split_e4m3(v, 4, p.hq8 + bi * 128, lane);
+      if (lane == 0) {
+        p.hsc[bi] = sc;
+        ctl_blk[bi] = 0u;
+      }
     }
-    p.h_s[8 * pg + r] = silu_clamped(G1, U1, 10.0f);   // the shared expert always clamps at 10
-    if (r == 0) p.ctl[2 + pg] = 0u;
   }
   __threadfence();
 
@@ -513,30 +602,15 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   __syncthreads();
   if (s_abort) return;
 
-  // ---- phase B prologue: h as MMA-ready pieces
-  for (int i = warp; i < S * (I / 32); i += kWarps) {
-    const float v = __ldcg(&p.h_r[(size_t)(i / (I / 32)) * I + 32 * (i % (I / 32)) + lane]);
-    const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7FFFFFFFu);
-    const int se = block_shift(m);
-    const float vs = v * exp2i(se);
-    const __half hi = __float2half_rn(vs);
-    const __half lo = __float2half_rn(vs - __half2float(hi));
-    __half* dst = reinterpret_cast<__half*>(hq + (size_t)i * 128);
-    dst[lane] = hi;
-    dst[32 + lane] = lo;
-    if (lane == 0) hsc[i] = exp2i(-se);
-  }
-  if (has_sh) {
-    __nv_bfloat16* d3 = reinterpret_cast<__nv_bfloat16*>(hsp);
-    for (int i = tid; i < Is; i += kThreads) {
-      const float v = __ldcg(&p.h_s[i]);
-      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-      const float r1 = v - __bfloat162float(hi);
-      const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
-      const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
-      d3[i] = hi;
-      d3[Is + i] = mid;
-      d3[2 * Is + i] = lo;
+  // ---- phase B prologue: the prepared activation pieces into shared memory
+  {
+    const int nq = S * (I / 32) * 128 / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(p.hq8);
+    for (int i = tid; i < nq; i += kThreads) reinterpret_cast<uint4*>(hq)[i] = __ldcg(src + i);
+    for (int i = tid; i < S * (I / 32); i += kThreads) hsc[i] = __ldcg(&p.hsc[i]);
+    if (has_sh) {
+      const uint4* s3 = reinterpret_cast<const uint4*>(p.hsp);
+      for (int i = tid; i < 3 * Is * 2 / 16; i += kThreads) reinterpret_cast<uint4*>(hsp)[i] = __ldcg(s3 + i);
     }
   }
   __syncthreads();
@@ -544,15 +618,15 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   auto compute_b = [&](const Buf& f, const Unit& d) {
     if (d.kind == kBRouted) {
       float acc0 = 0.f, acc1 = 0.f;
-      const bool bvalid = (g & 3) == t;                // hi pieces in columns 0-3, lo in 4-7
+      // chain ch: pieces 2ch (columns 0-3) and 2ch + 1 (columns 4-7)
+      const bool bvalid = (g & 3) == t;
       const int piece = g >> 2;
-      const int blk0 = 2 * (t & 1);
       const unsigned char* hbase = hq + (size_t)d.slot * (I / 32) * 128;
       const float* sbase = hsc + (size_t)d.slot * (I / 32);
-      fp4_unit(
-          f, d.nkg, blk0,
-          [&](int kg) -> const uint8_t* {
-            return bvalid ? hbase + (size_t)(4 * (d.kabs + kg) + t) * 128 + 64 * piece : my_zero;
+      fp4_unit<2>(
+          f, d.nkg, 2 * (t & 1),
+          [&](int kg, int ch) -> const uint8_t* {
+            return bvalid ? hbase + (size_t)((4 * (d.kabs + kg) + t) * 4 + 2 * ch + piece) * 32 : my_zero;
           },
           [&](int kg, int blk) { return sbase[4 * (d.kabs + kg) + blk]; }, acc0, acc1);
       acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
@@ -616,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
 }
 
 struct RdLayout {
-  size_t h_r, h_s, part_sh, ctl, total;
+  size_t h_r, hq8, hsc, h_s, hsp, part_sh, ctl, total;
   uint32_t a_part, b_hq, b_hsc, b_hsp, b_part, smem;
 };
 
@@ -629,7 +703,10 @@ RdLayout rd_layout(const DsMoeDesc& d) {
   L.ctl = 256;   // control words in the reserved block after the error word
   size_t o = kWsReserved;
   L.h_r = o;     o += up256((size_t)kMaxSlotsRd * I * 4);
+  L.hq8 = o;     o += up256((size_t)kMaxSlotsRd * (I / 32) * 128);
+  L.hsc = o;     o += up256((size_t)kMaxSlotsRd * (I / 32) * 4);
   L.h_s = o;     o += up256(Is * 4 + 4);
+  L.hsp = o;     o += up256(3 * Is * 2 + 16);
   L.part_sh = o; o += up256(4 * Is * 8 + 8);
   L.total = o;
   // shared memory (one union for phase A and phase B after the zero block)
@@ -669,7 +746,9 @@ bool rd_supported(const DecodeArgs& a) {
   if (d.hidden % 512 != 0 || d.inter % 128 != 0 || d.top_k > kMaxSlotsRd) return false;
   const bool sh = d.shared_w1 != nullptr;
   if (sh && d.shared_inter % 128 != 0) return false;
-  if (sh && (size_t)(256 + 4 * (2 + d.shared_inter / 8)) > kWsReserved) return false;  // control words fit
+  const size_t words = 2 + (sh ? d.shared_inter / 8 : 0) +
+                       (size_t)std::min(d.top_k, d.n_experts) * (d.inter / 32);
+  if (256 + 4 * words > kWsReserved) return false;  // the control words fit the reserved block
   if (!ds::aligned(a.x, 16) || !ds::aligned(d.w1.data, 16) || !ds::aligned(d.w3.data, 16) ||
       !ds::aligned(d.w2.data, 16) || !ds::aligned(d.w1.scales, 4) || !ds::aligned(d.w3.scales, 4) ||
       !ds::aligned(d.w2.scales, 4))
@@ -709,7 +788,10 @@ int launch_rd(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   p.gates = a.gates;
   p.out = a.out;
   p.h_r = reinterpret_cast<float*>(ws + L.h_r);
+  p.hq8 = reinterpret_cast<uint8_t*>(ws + L.hq8);
+  p.hsc = reinterpret_cast<float*>(ws + L.hsc);
   p.h_s = reinterpret_cast<float*>(ws + L.h_s);
+  p.hsp = reinterpret_cast<__nv_bfloat16*>(ws + L.hsp);
   p.part_sh = reinterpret_cast<float2*>(ws + L.part_sh);
   p.ctl = reinterpret_cast<unsigned*>(ws + L.ctl);
   p.err = a.err;

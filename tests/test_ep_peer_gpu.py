@@ -45,7 +45,9 @@ def test_peer_single_rank_equals_decode(cuda):
     # fewer rows than the communicator holds
     out1 = pl.__class__(comm, layer, E, K, rows=1)(x4[:1].contiguous(), i4[:1].contiguous(), w4[:1].contiguous())
     ref1 = moe.moe_decode(x4[:1].contiguous(), layer, i4[:1].contiguous(), w4[:1].contiguous())
-    assert torch.equal(out1, ref1), rel_l2(out1, ref1)
+    # one row: ds_moe_decode takes the single-token kernel, the exchange path
+    # the tcgen05 kernels, so the two agree within the decode tolerance
+    assert rel_l2(out1, ref1) < 1e-3
     comm.close()
 
 
