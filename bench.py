@@ -720,10 +720,12 @@ def run_stack(args) -> dict:
             "e2e": {"value": round(world * b * max(e2e_steps, 1) / (e2e_ms * 1e-3), 2) if e2e_steps else None,
                     "unit": "tokens/s", "h2d_bytes_per_step": b * (H * 2 + NL * E * 4),
                     "d2h_bytes_per_step": b * H * 2},
-            # ours per layer: router + prep/gemm/h/gemm/combine (FP4, tcgen05) or
-            # gate_up/down/combine (q3) per 8-token chunk, + 2 exchange kernels (peer)
+            # ours per layer: router + the single-token kernel (FP4, b = 1, one GPU)
+            # or prep/gemm/h/gemm/combine (FP4, tcgen05) or gate_up/down/combine
+            # (q3) per 8-token chunk, + 2 exchange kernels (peer)
             "gpu_launches": args.steps * sum(
-                1 + (5 if f == "fp4" else 3) * (((b + 7) // 8) if world == 1 else 1) + (2 if peer else 0)
+                1 + ((1 if (b == 1 and world == 1) else 5) if f == "fp4" else 3)
+                * (((b + 7) // 8) if world == 1 else 1) + (2 if peer else 0)
                 for f in fmts) if (world == 1 or peer) else None,
             "clocks": clocks,
         }
@@ -1110,15 +1112,16 @@ def run_decode(args) -> dict:
                          "launch_achieved": round(launch_achieved, 1),
                          "launch_frac": round(launch_achieved / pk["hbm_gbs"], 4),
                          "traffic": traffic,
-                         "kernel": "ds_moe_decode: " + (
-                             ("t5_prep + t5_gemm(gate/up) + t5_h + t5_gemm(down) + t5_combine"
-                              if use_t5 else "moe_tc_gate_up + moe_tc_down")
-                             if fmt == "fp4" else "moe_gate_up_kernel + moe_down_kernel (q3)"),
+                         "kernel": "route_topk + ds_moe_decode: " + (
+                             ("rd_kernel (one cooperative launch: gate/up, grid barrier, down + combine)"
+                              if tokens == 1 else
+                              "t5_prep + t5_gemm(gate/up) + t5_h + t5_gemm(down) + t5_combine")
+                             if fmt == "fp4" else "q3_gate_up + q3_down + q3_combine"),
                          "bytes_per_launch": step_bytes, "peak_kind": kind},
             "e2e": {"value": round(world * tokens * args.steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * (H * 2 + E * 4), "d2h_bytes_per_step": tokens * H * 2},
-            "gpu_launches": (6 if use_t5 else 3)
-                            * args.steps,
+            # router + the layer's decode kernels, per step
+            "gpu_launches": (1 + (1 if tokens == 1 else 5) if fmt == "fp4" else 1 + 3) * args.steps,
             "clocks": clocks,
         }
     if dist is not None:

@@ -58,7 +58,7 @@ namespace {
 
 using namespace ds::ptx;
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kMaxSlotsRd = 32;
 constexpr int kMaxTasksPerCta = 256;
@@ -191,95 +191,93 @@ __device__ __forceinline__ float split_e4m3(float v, int np, uint8_t* dst, int l
 
 // ---------------------------------------------------------------- units
 
-enum UnitKind : int { kAShared = 0, kARouted = 1, kBRouted = 2, kBShared = 3, kNone = 4 };
+enum UnitKind : int { kShared = 0, kRouted = 1, kNone = 2 };
 
+// One unit of a warp: 16 weight rows (lane (g, t) streams rows g and g + 8)
+// x up to 4 K-groups of 128 elements (FP4) or 4 chunks of 32 elements (bf16).
 struct Unit {
   int kind;
-  const uint8_t* ra;   // lane's first 16-byte chunk of row g (null: zeros)
-  const uint8_t* rb;   // same for row g + 8
-  const uint8_t* sra;  // scale bytes of row g at the unit's first K-group (FP4)
+  const uint8_t* ra;   // this lane's 16 bytes of row g at the unit's first group (null: zeros)
+  const uint8_t* rb;   // the same for row g + 8
+  const uint8_t* sra;  // ue8m0 bytes of row g at the unit's first group (FP4)
   const uint8_t* srb;
-  int nkg;             // K-groups (FP4) or 32-element chunks (bf16): 1..4
-  int kabs;            // FP4: absolute K-group index of the first group; bf16: first element
+  int nkg;             // groups in this unit: 1..4 (0: no unit)
+  int kabs;            // FP4: absolute index of its first K-group; bf16: first element
   int slot;
   int idx;             // unit index inside the CTA (partial-sum slot)
 };
 
+// Weight registers: slot j holds group (FP4) or chunk (bf16) j of rows g and
+// g + 8 and, for FP4, their four ue8m0 bytes of that group.
 struct Buf {
   uint4 a[4], b[4];
   uint32_t sa[4], sb[4];
 };
 
-__device__ __forceinline__ void load_unit(Buf& f, const Unit& u, uint64_t pol) {
-  const int fp4 = (u.kind == kARouted || u.kind == kBRouted);
-  // FP4: K-group stride 64 bytes; bf16: 32-element chunk stride 64 bytes
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const bool on = j < u.nkg && u.kind != kNone;
-    f.a[j] = (on && u.ra) ? ldg_stream(u.ra + 64 * j, pol) : make_uint4(0u, 0u, 0u, 0u);
-    f.b[j] = (on && u.rb) ? ldg_stream(u.rb + 64 * j, pol) : make_uint4(0u, 0u, 0u, 0u);
-    f.sa[j] = (on && fp4 && u.ra) ? ldg_u32(u.sra + 4 * j) : 0x7F7F7F7Fu;
-    f.sb[j] = (on && fp4 && u.rb) ? ldg_u32(u.srb + 4 * j) : 0x7F7F7F7Fu;
-  }
+// Issue the loads of group j of unit u into slot j (zeros past the unit).
+__device__ __forceinline__ void load_slot(Buf& f, const Unit& u, int j, uint64_t pol) {
+  const bool on = j < u.nkg;
+  f.a[j] = (on && u.ra) ? ldg_stream(u.ra + 64 * j, pol) : make_uint4(0u, 0u, 0u, 0u);
+  f.b[j] = (on && u.rb) ? ldg_stream(u.rb + 64 * j, pol) : make_uint4(0u, 0u, 0u, 0u);
+  const bool sc = on && u.kind == kRouted;
+  f.sa[j] = (sc && u.ra) ? ldg_u32(u.sra + 4 * j) : 0x7F7F7F7Fu;
+  f.sb[j] = (sc && u.rb) ? ldg_u32(u.srb + 4 * j) : 0x7F7F7F7Fu;
 }
 
-// FP4 unit: per-lane partials of rows g and g+8, already multiplied by the
-// weight-block and activation-block scales.  For K-group kg and MMA chain ch
-// (NCH chains of two pieces each), bsrc(kg, ch) = this lane's 32-byte B
-// source; bsc(kg, blk) = the activation scale of block blk (0..3) of the
-// group.  Lane (g, t) holds columns 2(t&1), 2(t&1)+1 of its pieces: blocks
-// blk0 = 2(t&1) and blk0 + 1.
-template <int NCH, typename BSrc, typename BScale>
-__device__ __forceinline__ void fp4_unit(const Buf& f, int nkg, int blk0, BSrc bsrc, BScale bsc,
-                                         float& acc0, float& acc1) {
-#pragma unroll
-  for (int kg = 0; kg < 4; ++kg) {
-    if (kg < nkg) {
-      const uint32_t wa[4] = {f.a[kg].x, f.a[kg].y, f.a[kg].z, f.a[kg].w};
-      const uint32_t wb[4] = {f.b[kg].x, f.b[kg].y, f.b[kg].z, f.b[kg].w};
-      uint32_t A[4][4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        A[j][0] = fp4lo_e4m3(wa[j]);
-        A[j][1] = fp4lo_e4m3(wb[j]);
-        A[j][2] = fp4hi_e4m3(wa[j]);
-        A[j][3] = fp4hi_e4m3(wb[j]);
-      }
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
-        const uint8_t* bp = bsrc(kg, ch);
-        const uint4 q0 = lds128(bp), q1 = lds128(bp + 16);
-        mma_e4m3(c, A[0], q0.x, q0.y);
-        mma_e4m3(c, A[1], q0.z, q0.w);
-        mma_e4m3(c, A[2], q1.x, q1.y);
-        mma_e4m3(c, A[3], q1.z, q1.w);
-      }
-      const float f0 = bsc(kg, blk0), f1 = bsc(kg, blk0 + 1);
-      const uint32_t sa = f.sa[kg] >> (8 * blk0), sb = f.sb[kg] >> (8 * blk0);
-      acc0 = fmaf(c[0], ue8m0_lo(sa) * f0, acc0);
-      acc0 = fmaf(c[1], ue8m0_hi(sa) * f1, acc0);
-      acc1 = fmaf(c[2], ue8m0_lo(sb) * f0, acc1);
-      acc1 = fmaf(c[3], ue8m0_hi(sb) * f1, acc1);
-    }
-  }
-}
-
-// bf16 unit: C accumulated over the unit's chunks; bsrc(j) = this lane's B
-// source (8 bf16) for chunk j.
-template <typename BSrc>
-__device__ __forceinline__ void bf16_unit(const Buf& f, int nch, BSrc bsrc, float (&c)[4]) {
+// FP4 group: decode the two rows' 32 + 32 codes into e4m3 A fragments, NCH
+// chains of four MMAs against the lane's B sources bp[ch] (two accumulators
+// for overlap), then this lane's two blocks' scales: acc0 / acc1 gather the
+// partials of rows g / g + 8.  f0 / f1: activation scales of blocks blk0 and
+// blk0 + 1 of the group.
+template <int NCH>
+__device__ __forceinline__ void fp4_group(const uint4 qa, const uint4 qb, uint32_t sa, uint32_t sb,
+                                          const uint8_t* const (&bp)[NCH], float f0, float f1, int blk0,
+                                          float& acc0, float& acc1) {
+  const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w};
+  const uint32_t wb[4] = {qb.x, qb.y, qb.z, qb.w};
+  uint32_t A[4][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    if (j < nch) {
-      const uint4 xv = lds128(bsrc(j));
-      const uint32_t a0[4] = {f.a[j].x, f.b[j].x, f.a[j].y, f.b[j].y};
-      const uint32_t a1[4] = {f.a[j].z, f.b[j].z, f.a[j].w, f.b[j].w};
-      mma_bf16(c, a0, xv.x, xv.y, c);
-      mma_bf16(c, a1, xv.z, xv.w, c);
-    }
+    A[j][0] = fp4lo_e4m3(wa[j]);
+    A[j][1] = fp4lo_e4m3(wb[j]);
+    A[j][2] = fp4hi_e4m3(wa[j]);
+    A[j][3] = fp4hi_e4m3(wb[j]);
   }
+  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) {
+    const uint4 q0 = lds128(bp[ch]), q1 = lds128(bp[ch] + 16);
+    mma_e4m3(c0, A[0], q0.x, q0.y);
+    mma_e4m3(c1, A[1], q0.z, q0.w);
+    mma_e4m3(c0, A[2], q1.x, q1.y);
+    mma_e4m3(c1, A[3], q1.z, q1.w);
+  }
+  sa >>= 8 * blk0;
+  sb >>= 8 * blk0;
+  acc0 = fmaf(c0[0] + c1[0], ue8m0_lo(sa) * f0, acc0);
+  acc0 = fmaf(c0[1] + c1[1], ue8m0_hi(sa) * f1, acc0);
+  acc1 = fmaf(c0[2] + c1[2], ue8m0_lo(sb) * f0, acc1);
+  acc1 = fmaf(c0[3] + c1[3], ue8m0_hi(sb) * f1, acc1);
 }
+
+// bf16 chunk (32 elements of rows g and g + 8): two MMAs into c, B = xv.
+__device__ __forceinline__ void bf16_chunk(const uint4 qa, const uint4 qb, const uint4 xv, float (&c)[4]) {
+  const uint32_t a0[4] = {qa.x, qb.x, qa.y, qb.y};
+  const uint32_t a1[4] = {qa.z, qb.z, qa.w, qb.w};
+  mma_bf16(c, a0, xv.x, xv.y, c);
+  mma_bf16(c, a1, xv.z, xv.w, c);
+}
+
+// x / d for small x by a multiply-high (m = ceil(2^32 / d)); exact for
+// x < 2^32 / d, which holds for every index divided here.
+struct FastDiv {
+  uint32_t m;
+  int d;
+  __device__ __forceinline__ explicit FastDiv(int dd) : d(dd) {
+    m = dd > 1 ? (uint32_t)(0xFFFFFFFFull / (uint64_t)dd + 1ull) : 0u;
+  }
+  __device__ __forceinline__ int div(int x) const { return d > 1 ? (int)__umulhi((uint32_t)x, m) : x; }
+};
 
 // ---------------------------------------------------------------- the kernel
 
@@ -354,39 +352,46 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   const int n_sh = has_sh ? 4 * (Is / 8) : 0;
   const int n_rt = S * (I / 8);
   const int n_tasks = n_sh + n_rt;
-  const int ta0 = (int)((int64_t)c * n_tasks / G), ta1 = (int)((int64_t)(c + 1) * n_tasks / G);
-  const int nua = (ta1 - ta0) * upt;
+  (void)n_tasks;
+  // every CTA takes the same share of shared-expert tasks and of routed tasks
+  // (the two kinds cost different compute per byte): local task tl < nsc is
+  // shared task s0 + tl, the others routed task r0 + tl - nsc
+  const int s0 = (int)((int64_t)c * n_sh / G), nsc = (int)((int64_t)(c + 1) * n_sh / G) - s0;
+  const int r0 = (int)((int64_t)c * n_rt / G), nrc = (int)((int64_t)(c + 1) * n_rt / G) - r0;
+  const int ntl = nsc + nrc;
+  auto task_of = [&](int tl) { return tl < nsc ? s0 + tl : n_sh + r0 + (tl - nsc); };
+  const int nua = ntl * upt;
   const uint8_t* my_zero = zero;
+
+  const FastDiv div_upt(upt), div_i8(I / 8);
 
   auto unit_a = [&](int u) -> Unit {
     Unit d;
     d.idx = u;
     d.slot = 0;
-    d.sra = d.srb = nullptr;
-    if (u >= nua) {
-      d.kind = kNone;
-      d.ra = d.rb = nullptr;
-      d.nkg = 0;
-      d.kabs = 0;
-      return d;
-    }
-    const int task = ta0 + u / upt, part = u - (u / upt) * upt;
+    d.ra = d.rb = d.sra = d.srb = nullptr;
+    d.kind = kNone;
+    d.nkg = 0;
+    d.kabs = 0;
+    if (u >= nua) return d;
+    const int tq = div_upt.div(u);
+    const int task = task_of(tq), part = u - tq * upt;
     d.nkg = 4;
     if (task < n_sh) {
       const int pg = task >> 2, q = task & 3;
       const int row = 8 * pg + g;
       const int k0 = q * (H / 4) + part * 128;
-      d.kind = kAShared;
+      d.kind = kShared;
       d.kabs = k0;
       d.ra = p.sw1 + ((size_t)row * H + k0 + 8 * t) * 2;
       d.rb = p.sw3 + ((size_t)row * H + k0 + 8 * t) * 2;
     } else {
       const int rt = task - n_sh;
-      const int s = rt / (I / 8), pg = rt - s * (I / 8);
-      const size_t row = (size_t)slots.expert[s] * I + 8 * pg + g;
+      const int sl = div_i8.div(rt), pg = rt - sl * (I / 8);
+      const size_t row = (size_t)slots.expert[sl] * I + 8 * pg + g;
       const int kg0 = part * 4;
-      d.kind = kARouted;
-      d.slot = s;
+      d.kind = kRouted;
+      d.slot = sl;
       d.kabs = kg0;
       d.ra = p.w1 + row * (H / 2) + 64 * kg0 + 16 * t;
       d.rb = p.w3 + row * (H / 2) + 64 * kg0 + 16 * t;
@@ -396,54 +401,54 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
     return d;
   };
 
-  auto compute_a = [&](const Buf& f, const Unit& d) {
-    if (d.kind == kAShared) {
-      float cc[4] = {0.f, 0.f, 0.f, 0.f};
-      const unsigned char* xsrc = (g == 0) ? xb + 2 * (d.kabs + 8 * t) : my_zero;
-      const int step = (g == 0) ? 64 : 0;
-      bf16_unit(f, 4, [&](int j) { return xsrc + step * j; }, cc);
-      if (t == 0) part_a[d.idx * 8 + g] = make_float2(cc[0], cc[2]);
-    } else if (d.kind == kARouted) {
-      float acc0 = 0.f, acc1 = 0.f;
-      // column n = g' carries block t' = n & 3 of the group, piece n >> 2
-      const bool bvalid = (g & 3) == t;
-      const int piece = g >> 2;
-      fp4_unit<1>(
-          f, 4, 2 * (t & 1),
-          [&](int kg, int) -> const uint8_t* {
-            return bvalid ? xq + (size_t)((4 * (d.kabs + kg) + t) * 2 + piece) * 32 : my_zero;
-          },
-          [&](int kg, int blk) { return xsc[4 * (d.kabs + kg) + blk]; }, acc0, acc1);
-      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-      if (t == 0) part_a[d.idx * 8 + g] = make_float2(acc0, acc1);
-    }
-  };
-
+  // Walk this warp's units; group kg of the next unit is loaded into slot kg
+  // as soon as the current unit has consumed it.
   {
-    Buf b0, b1;
-    int u = warp;
-    Unit d0 = unit_a(u);
-    load_unit(b0, d0, pol);
-    while (u < nua) {
-      Unit d1 = unit_a(u + kWarps);
-      load_unit(b1, d1, pol);
-      compute_a(b0, d0);
-      u += kWarps;
-      if (u >= nua) break;
-      d0 = unit_a(u + kWarps);
-      load_unit(b0, d0, pol);
-      compute_a(b1, d1);
-      u += kWarps;
+    // B sources: routed columns n = g' carry block t' = n & 3 of a group,
+    // piece n >> 2 of x; the shared expert's column 0 carries x itself
+    const bool rvalid = (g & 3) == t;
+    const int rpiece = g >> 2;
+    Buf f;
+    Unit cur = unit_a(warp);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) load_slot(f, cur, j, pol);
+    for (int u = warp; u < nua; u += kWarps) {
+      const Unit nxt = unit_a(u + kWarps);
+      if (cur.kind == kRouted) {
+        float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+        for (int kg = 0; kg < 4; ++kg) {
+          const int kga = cur.kabs + kg;
+          const uint8_t* bp[1] = {rvalid ? xq + (size_t)((4 * kga + t) * 2 + rpiece) * 32 : my_zero};
+          const int blk0 = 2 * (t & 1);
+          fp4_group<1>(f.a[kg], f.b[kg], f.sa[kg], f.sb[kg], bp, xsc[4 * kga + blk0], xsc[4 * kga + blk0 + 1],
+                       blk0, acc0, acc1);
+          load_slot(f, nxt, kg, pol);
+        }
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        if (t == 0) part_a[cur.idx * 8 + g] = make_float2(acc0, acc1);
+      } else {
+        float cc[4] = {0.f, 0.f, 0.f, 0.f};
+        const unsigned char* xsrc = (g == 0) ? xb + 2 * (cur.kabs + 8 * t) : my_zero;
+        const int step = (g == 0) ? 64 : 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          bf16_chunk(f.a[j], f.b[j], lds128(xsrc + step * j), cc);
+          load_slot(f, nxt, j, pol);
+        }
+        if (t == 0) part_a[cur.idx * 8 + g] = make_float2(cc[0], cc[2]);
+      }
+      cur = nxt;
     }
   }
   __syncthreads();
 
   // ---- phase A epilogue: h of every task of this CTA
-  for (int i = tid; i < (ta1 - ta0) * 8; i += kThreads) {
-    const int tl = i >> 3, r = i & 7, task = ta0 + tl;
+  for (int i = tid; i < ntl * 8; i += kThreads) {
+    const int tl = i >> 3, r = i & 7, task = task_of(tl);
     float G1 = 0.f, U1 = 0.f;
     for (int q = 0; q < upt; ++q) {
       const float2 v = part_a[(tl * upt + q) * 8 + r];
@@ -459,15 +464,15 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
       p.h_r[(size_t)s * I + 8 * pg + r] = silu_clamped(G1, U1, p.limit) * slots.gate[s];
     }
   }
-  __threadfence();
   __syncthreads();
   // Arrivals: a shared pair group is complete with its fourth quarter, a
   // routed h block (32 rows) with its fourth pair group; the CTA that
   // completes one finishes it for everybody.
   unsigned* ctl_sh = p.ctl + 2;
   unsigned* ctl_blk = p.ctl + 2 + Is / 8;
-  for (int tl = tid; tl < ta1 - ta0; tl += kThreads) {
-    const int task = ta0 + tl;
+  for (int tl = tid; tl < ntl; tl += kThreads) {
+    const int task = task_of(tl);
+    __threadfence();   // release this CTA's rows of the task (written before the barrier above)
     if (task < n_sh) {
       s_last[tl] = atomicAdd(&ctl_sh[task >> 2], 1u) == 3u;
     } else {
@@ -477,10 +482,10 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
     }
   }
   __syncthreads();
-  __threadfence();
-  for (int tl = warp; tl < ta1 - ta0; tl += kWarps) {
+  for (int tl = warp; tl < ntl; tl += kWarps) {
     if (!s_last[tl]) continue;
-    const int task = ta0 + tl;
+    __threadfence();   // acquire: the other CTAs' rows of this task
+    const int task = task_of(tl);
     if (task < n_sh) {
       // shared pair group: h of its 8 rows from the four quarters, and its bf16 pieces
       const int pg = task >> 2;
@@ -515,7 +520,6 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
       }
     }
   }
-  __threadfence();
 
   // ---- phase B geometry: output rows [n0, n1) of this CTA
   const int n0 = (int)((int64_t)c * H / G), n1 = (int)((int64_t)(c + 1) * H / G);
@@ -526,28 +530,28 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   const int ntiles = (n1 - n0 + 15) / 16;
   const int nub = ntiles * upt_b;
 
+  const FastDiv div_uptb(upt_b), div_ups(ups);
+
   auto unit_b = [&](int u) -> Unit {
     Unit d;
     d.idx = u;
     d.slot = 0;
     d.sra = d.srb = nullptr;
     d.ra = d.rb = nullptr;
-    if (u >= nub) {
-      d.kind = kNone;
-      d.nkg = 0;
-      d.kabs = 0;
-      return d;
-    }
-    const int tile = u / upt_b, r = u - tile * upt_b;
+    d.kind = kNone;
+    d.nkg = 0;
+    d.kabs = 0;
+    if (u >= nub) return d;
+    const int tile = div_uptb.div(u), r = u - tile * upt_b;
     const int row0 = n0 + 16 * tile + g, row1 = row0 + 8;
     if (r < S * ups) {
-      const int s = r / ups, kq = r - s * ups;
+      const int sl = div_ups.div(r), kq = r - sl * ups;
       const int kg0 = 4 * kq;
-      d.kind = kBRouted;
-      d.slot = s;
+      d.kind = kRouted;
+      d.slot = sl;
       d.kabs = kg0;
       d.nkg = min(4, nkgb - kg0);
-      const size_t e = slots.expert[s];
+      const size_t e = slots.expert[sl];
       if (row0 < n1) {
         d.ra = p.w2 + (e * H + row0) * (I / 2) + 64 * kg0 + 16 * t;
         d.sra = p.s2 + (e * H + row0) * (I / 32) + 4 * kg0;
@@ -558,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
       }
     } else {
       const int k0 = (r - S * ups) * 128;
-      d.kind = kBShared;
+      d.kind = kShared;
       d.kabs = k0;
       d.nkg = 4;
       if (row0 < n1) d.ra = p.sw2 + ((size_t)row0 * Is + k0 + 8 * t) * 2;
@@ -576,9 +580,10 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   } else if (tid == kMaxSlotsRd && has_sh) {
     prefetch_l2(p.sw2 + (size_t)n0 * Is * 2, (uint32_t)((size_t)(n1 - n0) * Is * 2));
   }
-  Buf b0, b1;
-  Unit d0 = unit_b(warp);
-  load_unit(b0, d0, pol);
+  Buf fb;
+  Unit curb = unit_b(warp);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) load_slot(fb, curb, j, pol);
 
   // ---- grid barrier (h of every CTA visible afterwards)
   __syncthreads();
@@ -615,56 +620,57 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   }
   __syncthreads();
 
-  auto compute_b = [&](const Buf& f, const Unit& d) {
-    if (d.kind == kBRouted) {
-      float acc0 = 0.f, acc1 = 0.f;
-      // chain ch: pieces 2ch (columns 0-3) and 2ch + 1 (columns 4-7)
-      const bool bvalid = (g & 3) == t;
-      const int piece = g >> 2;
-      const unsigned char* hbase = hq + (size_t)d.slot * (I / 32) * 128;
-      const float* sbase = hsc + (size_t)d.slot * (I / 32);
-      fp4_unit<2>(
-          f, d.nkg, 2 * (t & 1),
-          [&](int kg, int ch) -> const uint8_t* {
-            return bvalid ? hbase + (size_t)((4 * (d.kabs + kg) + t) * 4 + 2 * ch + piece) * 32 : my_zero;
-          },
-          [&](int kg, int blk) { return sbase[4 * (d.kabs + kg) + blk]; }, acc0, acc1);
-      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-      if (t == 0) {
-        part_b[d.idx * 16 + g] = acc0;
-        part_b[d.idx * 16 + g + 8] = acc1;
-      }
-    } else if (d.kind == kBShared) {
-      float cc[4] = {0.f, 0.f, 0.f, 0.f};
-      const bool bvalid = g < 3;                       // hi, mid, lo pieces in columns 0, 1, 2
-      const unsigned char* src = bvalid ? hsp + ((size_t)g * Is + d.kabs + 8 * t) * 2 : my_zero;
-      const int step = bvalid ? 64 : 0;
-      bf16_unit(f, 4, [&](int j) { return src + step * j; }, cc);
-      float v0 = cc[0] + cc[1], v1 = cc[2] + cc[3];
-      v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
-      v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
-      if (t == 0) {
-        part_b[d.idx * 16 + g] = v0;
-        part_b[d.idx * 16 + g + 8] = v1;
-      }
-    }
-  };
-
   {
-    int u = warp;
-    while (u < nub) {
-      Unit d1 = unit_b(u + kWarps);
-      load_unit(b1, d1, pol);
-      compute_b(b0, d0);
-      u += kWarps;
-      if (u >= nub) break;
-      d0 = unit_b(u + kWarps);
-      load_unit(b0, d0, pol);
-      compute_b(b1, d1);
-      u += kWarps;
+    // B sources: routed chain ch carries pieces 2ch (columns 0-3) and
+    // 2ch + 1 (columns 4-7) of h; the shared expert's columns 0-2 its three
+    // bf16 pieces
+    const bool rvalid = (g & 3) == t;
+    const int rpiece = g >> 2;
+    for (int u = warp; u < nub; u += kWarps) {
+      const Unit nxt = unit_b(u + kWarps);
+      if (curb.kind == kRouted) {
+        float acc0 = 0.f, acc1 = 0.f;
+        const unsigned char* hbase = hq + (size_t)curb.slot * (I / 32) * 128;
+        const float* sbase = hsc + (size_t)curb.slot * (I / 32);
+#pragma unroll
+        for (int kg = 0; kg < 4; ++kg) {
+          if (kg < curb.nkg) {
+            const int kga = curb.kabs + kg;
+            const uint8_t* bp[2] = {rvalid ? hbase + (size_t)((4 * kga + t) * 4 + rpiece) * 32 : my_zero,
+                                    rvalid ? hbase + (size_t)((4 * kga + t) * 4 + 2 + rpiece) * 32 : my_zero};
+            const int blk0 = 2 * (t & 1);
+            fp4_group<2>(fb.a[kg], fb.b[kg], fb.sa[kg], fb.sb[kg], bp, sbase[4 * kga + blk0],
+                         sbase[4 * kga + blk0 + 1], blk0, acc0, acc1);
+          }
+          load_slot(fb, nxt, kg, pol);
+        }
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        if (t == 0) {
+          part_b[curb.idx * 16 + g] = acc0;
+          part_b[curb.idx * 16 + g + 8] = acc1;
+        }
+      } else {
+        float cc[4] = {0.f, 0.f, 0.f, 0.f};
+        const bool bvalid = g < 3;
+        const unsigned char* src = bvalid ? hsp + ((size_t)g * Is + curb.kabs + 8 * t) * 2 : my_zero;
+        const int step = bvalid ? 64 : 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          bf16_chunk(fb.a[j], fb.b[j], lds128(src + step * j), cc);
+          load_slot(fb, nxt, j, pol);
+        }
+        float v0 = cc[0] + cc[1], v1 = cc[2] + cc[3];
+        v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+        if (t == 0) {
+          part_b[curb.idx * 16 + g] = v0;
+          part_b[curb.idx * 16 + g + 8] = v1;
+        }
+      }
+      curb = nxt;
     }
   }
   __syncthreads();
