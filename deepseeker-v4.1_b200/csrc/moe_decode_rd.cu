@@ -1,52 +1,53 @@
 // Single-token routed-expert MoE layer, register-dequant path: FP4 routed
 // experts (checkpoint layout, no prepared scale atoms needed) + optional bf16
-// shared expert, bf16 x, one token.  One cooperative persistent kernel per
-// layer, one CTA per SM, every warp independent:
+// shared expert, bf16 x, one token, SwiGLU clamp on.  One cooperative
+// persistent kernel per layer, one CTA per SM, every warp independent:
 //
 // Streaming.  A warp's unit of work is 16 weight rows x 4 K-groups of 128
-// elements (4 KB of FP4 or bf16 weights).  Each lane loads 16 bytes of two
-// rows per K-group straight from HBM into registers (coalesced 128-bit
-// loads, L2 evict-first), two units in flight per warp (double buffer).  No
-// shared-memory staging ring and no producer/consumer hand-off: the
-// bytes-in-flight come from every warp issuing its next unit's loads before
-// it computes the current one.
+// elements (4 KB of FP4) or 16 rows x 128 bf16 elements (4 KB).  Each lane
+// loads 16 bytes of two rows per group straight from HBM into registers
+// (coalesced 128-bit loads, L2 evict-first), and reloads each group's
+// registers with the next unit's bytes as soon as it has consumed them, so
+// every warp keeps about one unit in flight without a shared-memory ring.
 //
-// Dot products.  FP4 codes become e4m3 bytes in registers with integer ops
-// alone (code c -> ((c&7)<<2) | ((c&8)<<4), the value times 2^-6, exact for
-// every code including the subnormal 0.5), the A fragments of mma.sync
-// m16n8k32 e4m3 (f32 accumulate).  The B operand is the activation laid out
-// so that column n of the 32x8 B tile only carries the K elements of lane
-// group t = n, i.e. of ONE 32-element weight block: C[row][n] is then the dot
-// product of that row with that block, and each block's ue8m0 scale (times
-// the activation block's power-of-two scale) multiplies its own f32 partial.
-// Dequant is exact, products are exact, accumulation is f32.  Activations
-// enter as e4m3 pieces of a per-32-block power-of-two scaling: bf16 x as two
-// pieces (exactly), the SwiGLU intermediate h as four (~16 significant bits,
-// two MMA chains), in columns 0-3 / 4-7.  The shared expert's bf16 weights
-// feed bf16 MMAs directly (x exact; its h as three bf16 pieces).
+// Dot products: mma.sync m16n8k16 f16 with f32 accumulate, A = the weights
+// decoded in registers, B = the activation laid out so that column n of the
+// 16x8 B tile only carries the K elements of lane group t = n, i.e. of ONE
+// 32-element weight block: C[row][n] is the dot product of that row with
+// that block, and each block's ue8m0 scale (times the activation block's
+// power-of-two scale) multiplies its own f32 partial.  The FP4 decode is split
+// between two units of the SM: one word of every four goes through the
+// hardware e2m1 -> f16x2 conversion (exact values), the other three through
+// integer ops (code c -> f16 bits sign << 15 | magnitude << 9, i.e. the value
+// times 2^-14, exact for every code including the subnormal 0.5) into a
+// second accumulator that is rescaled by 2^14.  Dequant and products are
+// exact, accumulation is f32.  bf16 x enters as f16 scaled per 32-block by a
+// power of two (exact); the SwiGLU intermediate h as an f16 hi + lo pair
+// (~22 significant bits) scaled per slot from its bound |h| <= L max(L, 0.28) |gate|
+// (columns 0-3 hi, 4-7 lo).  The shared expert's bf16 weights feed bf16 MMAs
+// directly (x exact; its h as three bf16 pieces).
 //
 // Phase A (gate/up): tasks of 8 rows of W1 and the same 8 rows of W3 over the
 //   full K (a routed expert), or over a K quarter (the shared expert, whose
-//   rows are 4x wider); each CTA takes a contiguous range of tasks, so h of a
-//   routed task is finished inside the CTA (SwiGLU clamps, route weight); the
-//   four quarters of a shared task are summed by the CTA that finishes last,
-//   and each 32-row block of a routed h is cut into its e4m3 pieces by the
-//   CTA that delivers its last 8 rows (arrival counters), once for all CTAs.
-// Grid barrier (bounded spin).  Before it, every CTA prefetches its phase-B
-//   weights into L2 and issues its first phase-B unit's loads.
-// Phase B (down + combine): each CTA owns a contiguous range of ~H/G output
-//   rows: all routed slots' W2 rows and the shared W2 rows of that range, so
-//   the combine (routed slots in ascending expert id, then the shared output
-//   rounded to bf16, reference mlx_forward.py:388-419 / mlx_runner.py:776-781)
-//   happens in the CTA with no further pass.
+//   rows are 4x wider); every CTA takes the same share of both kinds.  A
+//   routed task finishes h for its 8 rows (clamps, route weight) and writes
+//   them as MMA-ready pieces; a shared quarter writes its partial sums.  The
+//   down projection's weights of this CTA are prefetched into L2 at the
+//   start (the gate/up phase leaves HBM bandwidth to spare).
+// Grid barrier (bounded spin).  Before it, every CTA issues its first
+//   phase-B unit's loads.
+// Phase B (down + combine): each CTA sums the shared quarters into h_s (its
+//   bf16 pieces), then owns a contiguous range of ~H/G output rows: all
+//   routed slots' W2 rows and the shared W2 rows of that range, so the
+//   combine (routed slots in ascending expert id, then the shared output
+//   rounded to bf16, reference mlx_forward.py:388-419 /
+//   mlx_runner.py:776-781) happens in the CTA with no further pass.
 //
-// Control words (grid barrier, shared-task counters) live in the workspace's
-// reserved block [256, kWsReserved), where no path writes anything else; they
-// must be zero before the first call and are left zero by every call that
-// completes.  Every wait is bounded by %globaltimer (2 s); on expiry the
-// kernel sets kErrWaitTimeout in the error word and stops waiting.
-#include <cuda_fp8.h>
-
+// Control words (the grid barrier) live in the workspace's reserved block
+// [256, kWsReserved), where no path writes anything else; they must be zero
+// before the first call and are left zero by every call that completes.
+// The barrier wait is bounded by %globaltimer (2 s); on expiry the kernel
+// sets kErrWaitTimeout in the error word and stops waiting.
 #include <algorithm>
 
 #include "moe_decode.cuh"
@@ -64,6 +65,7 @@ constexpr int kMaxSlotsRd = 32;
 constexpr int kMaxTasksPerCta = 256;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr int kZeroBytes = 128;
+constexpr int kCvtWords = 1;  // words (of four per 16-byte group) decoded by the conversion unit
 
 struct RdParams {
   const uint8_t* w1;  // FP4 [E][I][H/2]
@@ -79,19 +81,14 @@ struct RdParams {
   const int32_t* ids;
   const float* gates;
   void* out;
-  float* h_r;         // [kMaxSlotsRd][I] f32
-  uint8_t* hq8;       // [kMaxSlotsRd][I/32][4 pieces][32] e4m3 (piece byte order)
-  float* hsc;         // [kMaxSlotsRd][I/32] scale of each block's pieces (incl. 2^6)
-  float* h_s;         // [Is] f32
-  __nv_bfloat16* hsp; // [3][Is] bf16 pieces of h_s
-  float2* part_sh;    // [4][Is]
-  unsigned* ctl;      // [0] arrive, [1] depart, [2 + pg] shared-task arrivals,
-                      // [2 + Is/8 + slot*(I/32) + blk] routed h-block arrivals
+  __half* hq;         // [kMaxSlotsRd][I/32][2 pieces][32] f16, element order of piece_pos16
+  float2* part_sh;    // [4][Is] (gate, up) partial sums of the shared expert's K quarters
+  unsigned* ctl;      // [0] arrive, [1] depart
   int* err;
   int H, I, E, Is, k;
   int out_f32;
   float limit;
-  uint32_t smem_a_part, smem_b_hq, smem_b_hsc, smem_b_hsp, smem_b_part;  // byte offsets
+  uint32_t smem_a_part, smem_b_hq, smem_b_hsp, smem_b_part;  // byte offsets
 };
 
 // ---------------------------------------------------------------- small helpers
@@ -130,64 +127,53 @@ __device__ __forceinline__ float silu_clamped(float g, float u, float limit) {
   return (g / (1.0f + expf(-g))) * u;
 }
 
+// 2^e as an f32 for e in [-126, 127]
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 
-// e4m3 bytes (value = e2m1 * 2^-6) of the low / high nibbles of the four
-// bytes of w: code c -> sign (c & 8) << 4 | magnitude (c & 7) << 2.
-__device__ __forceinline__ uint32_t fp4lo_e4m3(uint32_t w) {
-  return ((w << 2) & 0x1C1C1C1Cu) | ((w << 4) & 0x80808080u);
-}
-__device__ __forceinline__ uint32_t fp4hi_e4m3(uint32_t w) {
-  return ((w >> 2) & 0x1C1C1C1Cu) | (w & 0x80808080u);
-}
-
-// D += A(16x32, e4m3, row) * B(32x8, e4m3, col), f32 accumulate.
-__device__ __forceinline__ void mma_e4m3(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+// Exponent that maps a block whose largest magnitude has f32 bits m into
+// [2^14, 2^15), f16's last full binade but one (0 for an all-zero or
+// non-finite block).
+__device__ __forceinline__ int f16_block_shift(uint32_t m) {
+  if (m == 0u || m >= 0x7F800000u) return 0;
+  const int e = m < 0x00800000u ? -127 : (int)(m >> 23) - 127;
+  return max(-126, min(126, 14 - e));
 }
 
-// Exponent bits of ue8m0 byte i (0..3) of w as an f32 (2^(b-127) for b in
+// Exponent bits of ue8m0 byte 0 / byte 1 of w as an f32 (2^(b-127) for b in
 // 1..254; byte 0 gives 0, byte 255 gives inf: a NaN-coded block makes the
 // sums it enters non-finite).
 __device__ __forceinline__ float ue8m0_lo(uint32_t w) { return __uint_as_float((w << 23) & 0x7F800000u); }
 __device__ __forceinline__ float ue8m0_hi(uint32_t w) { return __uint_as_float((w << 15) & 0x7F800000u); }
 
-// Byte position of element j (0..31) inside a 32-byte e4m3 piece: per group
-// of eight elements, the four even ones then the four odd ones -- the order
-// in which lane group t's B registers meet the low / high nibbles of a word.
-__device__ __forceinline__ int piece_pos(int j) { return (j >> 3) * 8 + (j & 1) * 4 + ((j & 7) >> 1); }
-
-__device__ __forceinline__ uint8_t to_e4m3(float v) {
-  return (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
-}
-__device__ __forceinline__ float from_e4m3(uint8_t b) {
-  return __half2float(__half(__nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3)));
+// Integer decode of the eight e2m1 codes of w (nibble k = element k) into
+// four f16x2 registers: P_k = (element k, element k + 4), each the code's
+// value times 2^-14 (f16 bits sign << 15 | (e1 e0 m) << 9).
+__device__ __forceinline__ void e2m1x8_to_f16x2_int(uint32_t w, uint32_t (&p)[4]) {
+  p[0] = ((w << 9) & 0x0E000E00u) | ((w << 12) & 0x80008000u);
+  p[1] = ((w << 5) & 0x0E000E00u) | ((w << 8) & 0x80008000u);
+  p[2] = ((w << 1) & 0x0E000E00u) | ((w << 4) & 0x80008000u);
+  p[3] = ((w >> 3) & 0x0E000E00u) | (w & 0x80008000u);
 }
 
-// Element j of a 32-block (one per lane): scale the block so that its largest
-// magnitude lands in [2^7, 2^8) and write `np` e4m3 pieces (each the
-// rounding of what the earlier ones left) to dst[p * 32 + piece_pos(j)];
-// returns the factor that undoes the scaling times 2^6 (the e2m1 -> e4m3
-// offset of the weights).
-__device__ __forceinline__ float split_e4m3(float v, int np, uint8_t* dst, int lane) {
-  const uint32_t m = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7FFFFFFFu);
-  int se = 0;
-  if (m != 0u && m < 0x7F800000u) {
-    const int e = m < 0x00800000u ? -127 : (int)(m >> 23) - 127;
-    se = max(-120, min(120, 7 - e));
-  }
-  float r = v * __uint_as_float((uint32_t)(se + 127) << 23);
-  const int pos = piece_pos(lane);
-  for (int p = 0; p < np; ++p) {
-    const uint8_t q = to_e4m3(r);
-    dst[p * 32 + pos] = q;
-    r -= from_e4m3(q);
-  }
-  return __uint_as_float((uint32_t)(6 - se + 127) << 23);
+// Slot (in f16 units) of element e (0..31) of a block in an activation piece:
+// per group of eight, the pair order in which that word's weight registers
+// meet the K dimension -- natural order for words decoded by the conversion
+// unit, (0, 4, 1, 5, 2, 6, 3, 7) for words decoded by integer ops.
+__device__ __forceinline__ int piece_pos16(int e) {
+  const int j = e >> 3, r = e & 7;
+  return 8 * j + (j < kCvtWords ? r : 2 * (r & 3) + (r >> 2));
 }
+
+// x / d for small x by a multiply-high (m = ceil(2^32 / d)); exact for
+// x < 2^32 / d, which holds for every index divided here.
+struct FastDiv {
+  uint32_t m;
+  int d;
+  __device__ __forceinline__ explicit FastDiv(int dd) : d(dd) {
+    m = dd > 1 ? (uint32_t)(0xFFFFFFFFull / (uint64_t)dd + 1ull) : 0u;
+  }
+  __device__ __forceinline__ int div(int x) const { return d > 1 ? (int)__umulhi((uint32_t)x, m) : x; }
+};
 
 // ---------------------------------------------------------------- units
 
@@ -224,40 +210,48 @@ __device__ __forceinline__ void load_slot(Buf& f, const Unit& u, int j, uint64_t
   f.sb[j] = (sc && u.rb) ? ldg_u32(u.srb + 4 * j) : 0x7F7F7F7Fu;
 }
 
-// FP4 group: decode the two rows' 32 + 32 codes into e4m3 A fragments, NCH
-// chains of four MMAs against the lane's B sources bp[ch] (two accumulators
-// for overlap), then this lane's two blocks' scales: acc0 / acc1 gather the
-// partials of rows g / g + 8.  f0 / f1: activation scales of blocks blk0 and
-// blk0 + 1 of the group.
-template <int NCH>
+// FP4 group (this lane's 32-element block of rows g and g + 8): decode, eight
+// MMAs against the lane's 64-byte B source bp (word j's activations at
+// bp + 16 j), then this lane's two blocks' scales into acc0 / acc1 (rows g /
+// g + 8).  f0 / f1: activation scales of blocks blk0 and blk0 + 1 of the
+// group.  `scale` false: the lane's columns are empty (skip the scales, whose
+// NaN code would otherwise turn 0 into NaN).
 __device__ __forceinline__ void fp4_group(const uint4 qa, const uint4 qb, uint32_t sa, uint32_t sb,
-                                          const uint8_t* const (&bp)[NCH], float f0, float f1, int blk0,
+                                          const uint8_t* bp, float f0, float f1, int blk0, bool scale,
                                           float& acc0, float& acc1) {
   const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w};
   const uint32_t wb[4] = {qb.x, qb.y, qb.z, qb.w};
-  uint32_t A[4][4];
+  float cx[4] = {0.f, 0.f, 0.f, 0.f};  // words decoded by the conversion unit: true values
+  float cy[4] = {0.f, 0.f, 0.f, 0.f};  // words decoded by integer ops: values times 2^-14
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    A[j][0] = fp4lo_e4m3(wa[j]);
-    A[j][1] = fp4lo_e4m3(wb[j]);
-    A[j][2] = fp4hi_e4m3(wa[j]);
-    A[j][3] = fp4hi_e4m3(wb[j]);
+    uint32_t pa[4], pb[4];
+    if (j < kCvtWords) {
+      e2m1x8_to_f16x2(wa[j], pa);
+      e2m1x8_to_f16x2(wb[j], pb);
+    } else {
+      e2m1x8_to_f16x2_int(wa[j], pa);
+      e2m1x8_to_f16x2_int(wb[j], pb);
+    }
+    const uint4 xv = lds128(bp + 16 * j);
+    const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]};
+    const uint32_t a1[4] = {pa[2], pb[2], pa[3], pb[3]};
+    if (j < kCvtWords) {
+      mma_f16(cx, a0, xv.x, xv.y, cx);
+      mma_f16(cx, a1, xv.z, xv.w, cx);
+    } else {
+      mma_f16(cy, a0, xv.x, xv.y, cy);
+      mma_f16(cy, a1, xv.z, xv.w, cy);
+    }
   }
-  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int ch = 0; ch < NCH; ++ch) {
-    const uint4 q0 = lds128(bp[ch]), q1 = lds128(bp[ch] + 16);
-    mma_e4m3(c0, A[0], q0.x, q0.y);
-    mma_e4m3(c1, A[1], q0.z, q0.w);
-    mma_e4m3(c0, A[2], q1.x, q1.y);
-    mma_e4m3(c1, A[3], q1.z, q1.w);
+  if (scale) {
+    sa >>= 8 * blk0;
+    sb >>= 8 * blk0;
+    acc0 = fmaf(fmaf(cy[0], 16384.0f, cx[0]), ue8m0_lo(sa) * f0, acc0);
+    acc0 = fmaf(fmaf(cy[1], 16384.0f, cx[1]), ue8m0_hi(sa) * f1, acc0);
+    acc1 = fmaf(fmaf(cy[2], 16384.0f, cx[2]), ue8m0_lo(sb) * f0, acc1);
+    acc1 = fmaf(fmaf(cy[3], 16384.0f, cx[3]), ue8m0_hi(sb) * f1, acc1);
   }
-  sa >>= 8 * blk0;
-  sb >>= 8 * blk0;
-  acc0 = fmaf(c0[0] + c1[0], ue8m0_lo(sa) * f0, acc0);
-  acc0 = fmaf(c0[1] + c1[1], ue8m0_hi(sa) * f1, acc0);
-  acc1 = fmaf(c0[2] + c1[2], ue8m0_lo(sb) * f0, acc1);
-  acc1 = fmaf(c0[3] + c1[3], ue8m0_hi(sb) * f1, acc1);
 }
 
 // bf16 chunk (32 elements of rows g and g + 8): two MMAs into c, B = xv.
@@ -268,29 +262,19 @@ __device__ __forceinline__ void bf16_chunk(const uint4 qa, const uint4 qb, const
   mma_bf16(c, a1, xv.z, xv.w, c);
 }
 
-// x / d for small x by a multiply-high (m = ceil(2^32 / d)); exact for
-// x < 2^32 / d, which holds for every index divided here.
-struct FastDiv {
-  uint32_t m;
-  int d;
-  __device__ __forceinline__ explicit FastDiv(int dd) : d(dd) {
-    m = dd > 1 ? (uint32_t)(0xFFFFFFFFull / (uint64_t)dd + 1ull) : 0u;
-  }
-  __device__ __forceinline__ int div(int x) const { return d > 1 ? (int)__umulhi((uint32_t)x, m) : x; }
-};
-
 // ---------------------------------------------------------------- the kernel
 
 struct Slots1 {
   int count;
   int expert[kMaxSlotsRd];
   float gate[kMaxSlotsRd];
+  float hmul[kMaxSlotsRd];  // power of two that puts the slot's |h| bound under 2^15
+  float hdiv[kMaxSlotsRd];  // its inverse
 };
 
 __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ Slots1 slots;
-  __shared__ int s_last[kMaxTasksPerCta];
   __shared__ int s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -301,13 +285,13 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
 
   unsigned char* zero = smem;                                     // kZeroBytes of zeros
   unsigned char* xb = smem + kZeroBytes;                          // x bf16 [H]
-  unsigned char* xq = xb + 2 * H;                                 // x e4m3 [H/32][2 pieces][32]
+  unsigned char* xq = xb + 2 * H;                                 // x f16 [H/32][32] (piece_pos16 order)
   float* xsc = reinterpret_cast<float*>(xq + 2 * H);              // [H/32]
   float2* part_a = reinterpret_cast<float2*>(smem + p.smem_a_part);
-  unsigned char* hq = smem + p.smem_b_hq;                         // [S][I/32][4][32] e4m3
-  float* hsc = reinterpret_cast<float*>(smem + p.smem_b_hsc);     // [S][I/32]
+  unsigned char* hq = smem + p.smem_b_hq;                         // [S][I/32][2][32] f16
   unsigned char* hsp = smem + p.smem_b_hsp;                       // [3][Is] bf16
   float* part_b = reinterpret_cast<float*>(smem + p.smem_b_part); // [units][16]
+  const uint8_t* my_zero = zero;
 
   // ---- prologue: slots (warp 0), x staging (all warps)
   if (tid < kZeroBytes / 4) reinterpret_cast<uint32_t*>(zero)[tid] = 0u;
@@ -335,34 +319,55 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
     if (first) {
       slots.expert[rank] = id;
       slots.gate[rank] = gt;
+      // |h| <= L max(L, 0.28) |gate|: |silu(min(g, L))| <= max(L, 0.28), |clip(u)| <= L
+      const float bound = p.limit * fmaxf(p.limit, 0.2785f) * gt;
+      const int sh = f16_block_shift(__float_as_uint(bound) & 0x7FFFFFFFu);
+      slots.hmul[rank] = exp2i(sh);
+      slots.hdiv[rank] = exp2i(-sh);
     }
     if (lane == 0) slots.count = __popc(firsts);
   }
   for (int b = warp; b < H / 32; b += kWarps) {
     const __nv_bfloat16 v = p.x[32 * b + lane];
     reinterpret_cast<__nv_bfloat16*>(xb)[32 * b + lane] = v;
-    const float sc = split_e4m3(__bfloat162float(v), 2, xq + 64 * b, lane);   // bf16: two pieces are exact
-    if (lane == 0) xsc[b] = sc;
+    const float f = __bfloat162float(v);
+    const int se = f16_block_shift(__reduce_max_sync(0xffffffffu, __float_as_uint(f) & 0x7FFFFFFFu));
+    reinterpret_cast<__half*>(xq)[32 * b + piece_pos16(lane)] = __float2half_rn(f * exp2i(se));
+    if (lane == 0) xsc[b] = exp2i(-se);
   }
   __syncthreads();
   const int S = slots.count;
 
-  // ---- phase A: task list [shared quarters][routed pair groups]
+  // ---- phase B geometry (known now): output rows [n0, n1) of this CTA
+  const int n0 = (int)((int64_t)c * H / G), n1 = (int)((int64_t)(c + 1) * H / G);
+  const int nkgb = I / 128;
+  const int ups = (nkgb + 3) / 4;                // routed units per (tile, slot)
+  const int ush = has_sh ? Is / 128 : 0;         // shared units per tile (128-wide K slices)
+  const int upt_b = S * ups + ush;               // units per tile
+  const int ntiles = (n1 - n0 + 15) / 16;
+  const int nub = ntiles * upt_b;
+
+  // the down projection's weights of this CTA's rows into L2 while the
+  // gate/up phase (compute-bound) leaves HBM bandwidth to spare
+  if (tid < S) {
+    const size_t e = slots.expert[tid];
+    prefetch_l2(p.w2 + (e * H + n0) * (I / 2), (uint32_t)((n1 - n0) * (I / 2)));
+    const size_t soff = (e * H + n0) * (I / 32), sbytes = (size_t)(n1 - n0) * (I / 32);
+    if (soff % 16 == 0 && sbytes % 16 == 0) prefetch_l2(p.s2 + soff, (uint32_t)sbytes);
+  } else if (tid == kMaxSlotsRd && has_sh) {
+    prefetch_l2(p.sw2 + (size_t)n0 * Is * 2, (uint32_t)((size_t)(n1 - n0) * Is * 2));
+  }
+
+  // ---- phase A: every CTA takes the same share of shared-expert tasks and
+  // of routed tasks (the two kinds cost different compute per byte): local
+  // task tl < nsc is shared task s0 + tl, the others routed task r0 + tl - nsc
   const int upt = H / 512;                       // units per task
   const int n_sh = has_sh ? 4 * (Is / 8) : 0;
   const int n_rt = S * (I / 8);
-  const int n_tasks = n_sh + n_rt;
-  (void)n_tasks;
-  // every CTA takes the same share of shared-expert tasks and of routed tasks
-  // (the two kinds cost different compute per byte): local task tl < nsc is
-  // shared task s0 + tl, the others routed task r0 + tl - nsc
   const int s0 = (int)((int64_t)c * n_sh / G), nsc = (int)((int64_t)(c + 1) * n_sh / G) - s0;
   const int r0 = (int)((int64_t)c * n_rt / G), nrc = (int)((int64_t)(c + 1) * n_rt / G) - r0;
   const int ntl = nsc + nrc;
-  auto task_of = [&](int tl) { return tl < nsc ? s0 + tl : n_sh + r0 + (tl - nsc); };
   const int nua = ntl * upt;
-  const uint8_t* my_zero = zero;
-
   const FastDiv div_upt(upt), div_i8(I / 8);
 
   auto unit_a = [&](int u) -> Unit {
@@ -374,10 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
     d.nkg = 0;
     d.kabs = 0;
     if (u >= nua) return d;
-    const int tq = div_upt.div(u);
-    const int task = task_of(tq), part = u - tq * upt;
+    const int tl = div_upt.div(u), part = u - tl * upt;
     d.nkg = 4;
-    if (task < n_sh) {
+    if (tl < nsc) {
+      const int task = s0 + tl;
       const int pg = task >> 2, q = task & 3;
       const int row = 8 * pg + g;
       const int k0 = q * (H / 4) + part * 128;
@@ -386,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
       d.ra = p.sw1 + ((size_t)row * H + k0 + 8 * t) * 2;
       d.rb = p.sw3 + ((size_t)row * H + k0 + 8 * t) * 2;
     } else {
-      const int rt = task - n_sh;
+      const int rt = r0 + tl - nsc;
       const int sl = div_i8.div(rt), pg = rt - sl * (I / 8);
       const size_t row = (size_t)slots.expert[sl] * I + 8 * pg + g;
       const int kg0 = part * 4;
@@ -404,10 +409,9 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   // Walk this warp's units; group kg of the next unit is loaded into slot kg
   // as soon as the current unit has consumed it.
   {
-    // B sources: routed columns n = g' carry block t' = n & 3 of a group,
-    // piece n >> 2 of x; the shared expert's column 0 carries x itself
-    const bool rvalid = (g & 3) == t;
-    const int rpiece = g >> 2;
+    // B sources: routed column n = g' < 4 carries block n of a group (x has
+    // one piece, columns 4-7 stay empty); the shared expert's column 0 x itself
+    const bool rvalid = g == t;
     Buf f;
     Unit cur = unit_a(warp);
 #pragma unroll
@@ -419,16 +423,13 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
 #pragma unroll
         for (int kg = 0; kg < 4; ++kg) {
           const int kga = cur.kabs + kg;
-          const uint8_t* bp[1] = {rvalid ? xq + (size_t)((4 * kga + t) * 2 + rpiece) * 32 : my_zero};
           const int blk0 = 2 * (t & 1);
-          fp4_group<1>(f.a[kg], f.b[kg], f.sa[kg], f.sb[kg], bp, xsc[4 * kga + blk0], xsc[4 * kga + blk0 + 1],
-                       blk0, acc0, acc1);
+          fp4_group(f.a[kg], f.b[kg], f.sa[kg], f.sb[kg], rvalid ? xq + (size_t)(4 * kga + t) * 64 : my_zero,
+                    xsc[4 * kga + blk0], xsc[4 * kga + blk0 + 1], blk0, t < 2, acc0, acc1);
           load_slot(f, nxt, kg, pol);
         }
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
         acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
         if (t == 0) part_a[cur.idx * 8 + g] = make_float2(acc0, acc1);
       } else {
         float cc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -446,92 +447,34 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   }
   __syncthreads();
 
-  // ---- phase A epilogue: h of every task of this CTA
+  // ---- phase A epilogue: routed h of every routed task (MMA-ready pieces),
+  // partial sums of every shared quarter
   for (int i = tid; i < ntl * 8; i += kThreads) {
-    const int tl = i >> 3, r = i & 7, task = task_of(tl);
+    const int tl = i >> 3, r = i & 7;
     float G1 = 0.f, U1 = 0.f;
     for (int q = 0; q < upt; ++q) {
       const float2 v = part_a[(tl * upt + q) * 8 + r];
       G1 += v.x;
       U1 += v.y;
     }
-    if (task < n_sh) {
-      const int pg = task >> 2, qq = task & 3;
-      p.part_sh[(size_t)qq * Is + 8 * pg + r] = make_float2(G1, U1);
+    if (tl < nsc) {
+      const int task = s0 + tl;
+      p.part_sh[(size_t)(task & 3) * Is + 8 * (task >> 2) + r] = make_float2(G1, U1);
     } else {
-      const int rt = task - n_sh;
-      const int s = rt / (I / 8), pg = rt - s * (I / 8);
-      p.h_r[(size_t)s * I + 8 * pg + r] = silu_clamped(G1, U1, p.limit) * slots.gate[s];
-    }
-  }
-  __syncthreads();
-  // Arrivals: a shared pair group is complete with its fourth quarter, a
-  // routed h block (32 rows) with its fourth pair group; the CTA that
-  // completes one finishes it for everybody.
-  unsigned* ctl_sh = p.ctl + 2;
-  unsigned* ctl_blk = p.ctl + 2 + Is / 8;
-  for (int tl = tid; tl < ntl; tl += kThreads) {
-    const int task = task_of(tl);
-    __threadfence();   // release this CTA's rows of the task (written before the barrier above)
-    if (task < n_sh) {
-      s_last[tl] = atomicAdd(&ctl_sh[task >> 2], 1u) == 3u;
-    } else {
-      const int rt = task - n_sh;
+      const int rt = r0 + tl - nsc;
       const int sl = rt / (I / 8), pg = rt - sl * (I / 8);
-      s_last[tl] = atomicAdd(&ctl_blk[sl * (I / 32) + (pg >> 2)], 1u) == 3u;
-    }
-  }
-  __syncthreads();
-  for (int tl = warp; tl < ntl; tl += kWarps) {
-    if (!s_last[tl]) continue;
-    __threadfence();   // acquire: the other CTAs' rows of this task
-    const int task = task_of(tl);
-    if (task < n_sh) {
-      // shared pair group: h of its 8 rows from the four quarters, and its bf16 pieces
-      const int pg = task >> 2;
-      if (lane < 8) {
-        float G1 = 0.f, U1 = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 v = __ldcg(&p.part_sh[(size_t)q * Is + 8 * pg + lane]);
-          G1 += v.x;
-          U1 += v.y;
-        }
-        const int row = 8 * pg + lane;
-        const float h = silu_clamped(G1, U1, 10.0f);   // the shared expert always clamps at 10
-        const __nv_bfloat16 hi = __float2bfloat16_rn(h);
-        const float r1 = h - __bfloat162float(hi);
-        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
-        p.hsp[row] = hi;
-        p.hsp[Is + row] = mid;
-        p.hsp[2 * Is + row] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
-        if (lane == 0) ctl_sh[pg] = 0u;
-      }
-    } else {
-      // routed h block: four e4m3 pieces of its 32 values and their scale
-      const int rt = task - n_sh;
-      const int sl = rt / (I / 8), blk = (rt - sl * (I / 8)) >> 2;
-      const size_t bi = (size_t)sl * (I / 32) + blk;
-      const float v = __ldcg(&p.h_r[(size_t)sl * I + 32 * blk + lane]);
-      const float sc = split_e4m3(v, 4, p.hq8 + bi * 128, lane);
-      if (lane == 0) {
-        p.hsc[bi] = sc;
-        ctl_blk[bi] = 0u;
-      }
+      const float h = silu_clamped(G1, U1, p.limit) * slots.gate[sl] * slots.hmul[sl];
+      const __half hi = __float2half_rn(h);
+      const __half lo = __float2half_rn(h - __half2float(hi));
+      __half* dst = p.hq + ((size_t)sl * (I / 32) + (pg >> 2)) * 64;
+      const int pos = piece_pos16(8 * (pg & 3) + r);
+      dst[pos] = hi;
+      dst[32 + pos] = lo;
     }
   }
 
-  // ---- phase B geometry: output rows [n0, n1) of this CTA
-  const int n0 = (int)((int64_t)c * H / G), n1 = (int)((int64_t)(c + 1) * H / G);
-  const int nkgb = I / 128;
-  const int ups = (nkgb + 3) / 4;                // routed units per (tile, slot)
-  const int ush = has_sh ? Is / 128 : 0;         // shared units per tile (128-wide K slices)
-  const int upt_b = S * ups + ush;               // units per tile
-  const int ntiles = (n1 - n0 + 15) / 16;
-  const int nub = ntiles * upt_b;
-
+  // ---- phase B: first units' loads, then the grid barrier
   const FastDiv div_uptb(upt_b), div_ups(ups);
-
   auto unit_b = [&](int u) -> Unit {
     Unit d;
     d.idx = u;
@@ -570,25 +513,14 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
     }
     return d;
   };
-
-  // L2 prefetch of this CTA's phase-B weights, then its first units' loads
-  if (tid < S) {
-    const size_t e = slots.expert[tid];
-    prefetch_l2(p.w2 + (e * H + n0) * (I / 2), (uint32_t)((n1 - n0) * (I / 2)));
-    const size_t soff = (e * H + n0) * (I / 32), sbytes = (size_t)(n1 - n0) * (I / 32);
-    if (soff % 16 == 0 && sbytes % 16 == 0) prefetch_l2(p.s2 + soff, (uint32_t)sbytes);
-  } else if (tid == kMaxSlotsRd && has_sh) {
-    prefetch_l2(p.sw2 + (size_t)n0 * Is * 2, (uint32_t)((size_t)(n1 - n0) * Is * 2));
-  }
   Buf fb;
   Unit curb = unit_b(warp);
 #pragma unroll
   for (int j = 0; j < 4; ++j) load_slot(fb, curb, j, pol);
 
-  // ---- grid barrier (h of every CTA visible afterwards)
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
+    __threadfence();   // release this CTA's h pieces and shared partials
     atomicAdd(&p.ctl[0], 1u);
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire(&p.ctl[0]) < (unsigned)G) {
@@ -607,22 +539,37 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
   __syncthreads();
   if (s_abort) return;
 
-  // ---- phase B prologue: the prepared activation pieces into shared memory
+  // ---- phase B prologue: routed h pieces into shared memory; the shared
+  // expert's h from its four quarters, as three bf16 pieces
   {
     const int nq = S * (I / 32) * 128 / 16;
-    const uint4* src = reinterpret_cast<const uint4*>(p.hq8);
+    const uint4* src = reinterpret_cast<const uint4*>(p.hq);
     for (int i = tid; i < nq; i += kThreads) reinterpret_cast<uint4*>(hq)[i] = __ldcg(src + i);
-    for (int i = tid; i < S * (I / 32); i += kThreads) hsc[i] = __ldcg(&p.hsc[i]);
     if (has_sh) {
-      const uint4* s3 = reinterpret_cast<const uint4*>(p.hsp);
-      for (int i = tid; i < 3 * Is * 2 / 16; i += kThreads) reinterpret_cast<uint4*>(hsp)[i] = __ldcg(s3 + i);
+      __nv_bfloat16* d3 = reinterpret_cast<__nv_bfloat16*>(hsp);
+      for (int i = tid; i < Is; i += kThreads) {
+        float G1 = 0.f, U1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 v = __ldcg(&p.part_sh[(size_t)q * Is + i]);
+          G1 += v.x;
+          U1 += v.y;
+        }
+        const float h = silu_clamped(G1, U1, 10.0f);   // the shared expert always clamps at 10
+        const __nv_bfloat16 hi = __float2bfloat16_rn(h);
+        const float r1 = h - __bfloat162float(hi);
+        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+        d3[i] = hi;
+        d3[Is + i] = mid;
+        d3[2 * Is + i] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+      }
     }
   }
   __syncthreads();
 
   {
-    // B sources: routed chain ch carries pieces 2ch (columns 0-3) and
-    // 2ch + 1 (columns 4-7) of h; the shared expert's columns 0-2 its three
+    // B sources: routed column n = g' carries block n & 3 of a group, piece
+    // n >> 2 (0: hi, 1: lo) of h; the shared expert's columns 0-2 its three
     // bf16 pieces
     const bool rvalid = (g & 3) == t;
     const int rpiece = g >> 2;
@@ -631,16 +578,14 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
       if (curb.kind == kRouted) {
         float acc0 = 0.f, acc1 = 0.f;
         const unsigned char* hbase = hq + (size_t)curb.slot * (I / 32) * 128;
-        const float* sbase = hsc + (size_t)curb.slot * (I / 32);
+        const float hs = slots.hdiv[curb.slot];
 #pragma unroll
         for (int kg = 0; kg < 4; ++kg) {
           if (kg < curb.nkg) {
             const int kga = curb.kabs + kg;
-            const uint8_t* bp[2] = {rvalid ? hbase + (size_t)((4 * kga + t) * 4 + rpiece) * 32 : my_zero,
-                                    rvalid ? hbase + (size_t)((4 * kga + t) * 4 + 2 + rpiece) * 32 : my_zero};
-            const int blk0 = 2 * (t & 1);
-            fp4_group<2>(fb.a[kg], fb.b[kg], fb.sa[kg], fb.sb[kg], bp, sbase[4 * kga + blk0],
-                         sbase[4 * kga + blk0 + 1], blk0, acc0, acc1);
+            fp4_group(fb.a[kg], fb.b[kg], fb.sa[kg], fb.sb[kg],
+                      rvalid ? hbase + (size_t)((4 * kga + t) * 2 + rpiece) * 64 : my_zero, hs, hs, 2 * (t & 1),
+                      true, acc0, acc1);
           }
           load_slot(fb, nxt, kg, pol);
         }
@@ -696,8 +641,8 @@ __global__ void __launch_bounds__(kThreads, 1) rd_kernel(const RdParams p) {
 }
 
 struct RdLayout {
-  size_t h_r, hq8, hsc, h_s, hsp, part_sh, ctl, total;
-  uint32_t a_part, b_hq, b_hsc, b_hsp, b_part, smem;
+  size_t hq, part_sh, ctl, total;
+  uint32_t a_part, b_hq, b_hsp, b_part, smem;
 };
 
 size_t up256(size_t v) { return (v + 255) / 256 * 256; }
@@ -706,20 +651,16 @@ RdLayout rd_layout(const DsMoeDesc& d) {
   RdLayout L;
   const size_t H = d.hidden, I = d.inter, Is = d.shared_w1 ? d.shared_inter : 0;
   const int S = std::min(d.top_k, d.n_experts);
-  L.ctl = 256;   // control words in the reserved block after the error word
+  L.ctl = 256;   // grid-barrier words in the reserved block after the error word
   size_t o = kWsReserved;
-  L.h_r = o;     o += up256((size_t)kMaxSlotsRd * I * 4);
-  L.hq8 = o;     o += up256((size_t)kMaxSlotsRd * (I / 32) * 128);
-  L.hsc = o;     o += up256((size_t)kMaxSlotsRd * (I / 32) * 4);
-  L.h_s = o;     o += up256(Is * 4 + 4);
-  L.hsp = o;     o += up256(3 * Is * 2 + 16);
+  L.hq = o;      o += up256((size_t)kMaxSlotsRd * (I / 32) * 128);
   L.part_sh = o; o += up256(4 * Is * 8 + 8);
   L.total = o;
   // shared memory (one union for phase A and phase B after the zero block)
   const int G = ds::sm_count();
   const int upt = (int)(H / 512);
-  const int n_tasks = (Is ? 4 * (int)(Is / 8) : 0) + S * (int)(I / 8);
-  const int tasks_cta = (n_tasks + G - 1) / G + 1;
+  const int n_sh = Is ? 4 * (int)(Is / 8) : 0, n_rt = S * (int)(I / 8);
+  const int tasks_cta = (n_sh + G - 1) / G + (n_rt + G - 1) / G;
   uint32_t a = kZeroBytes + 4 * (uint32_t)H + 4 * (uint32_t)(H / 32);
   a = (a + 15) / 16 * 16;
   L.a_part = a;
@@ -727,9 +668,6 @@ RdLayout rd_layout(const DsMoeDesc& d) {
   uint32_t b = kZeroBytes;
   L.b_hq = b;
   b += (uint32_t)(S * (I / 32) * 128);
-  L.b_hsc = b;
-  b += (uint32_t)(S * (I / 32) * 4);
-  b = (b + 15) / 16 * 16;
   L.b_hsp = b;
   b += (uint32_t)(3 * Is * 2);
   b = (b + 15) / 16 * 16;
@@ -747,14 +685,11 @@ RdLayout rd_layout(const DsMoeDesc& d) {
 bool rd_supported(const DecodeArgs& a) {
   const DsMoeDesc& d = a.d;
   if (a.x_f32 || a.tokens != 1 || d.w1.format != DS_FMT_FP4) return false;
-  if (!d.route_before_down) return false;
+  if (!d.route_before_down || !(d.swiglu_limit > 0.0f)) return false;   // h scale from the clamp bound
   if (a.out_sh != nullptr || a.sh_w2_ld != 0 || a.sh_row0 != 0 || a.sh_row1 != (1 << 30)) return false;
   if (d.hidden % 512 != 0 || d.inter % 128 != 0 || d.top_k > kMaxSlotsRd) return false;
   const bool sh = d.shared_w1 != nullptr;
   if (sh && d.shared_inter % 128 != 0) return false;
-  const size_t words = 2 + (sh ? d.shared_inter / 8 : 0) +
-                       (size_t)std::min(d.top_k, d.n_experts) * (d.inter / 32);
-  if (256 + 4 * words > kWsReserved) return false;  // the control words fit the reserved block
   if (!ds::aligned(a.x, 16) || !ds::aligned(d.w1.data, 16) || !ds::aligned(d.w3.data, 16) ||
       !ds::aligned(d.w2.data, 16) || !ds::aligned(d.w1.scales, 4) || !ds::aligned(d.w3.scales, 4) ||
       !ds::aligned(d.w2.scales, 4))
@@ -763,8 +698,9 @@ bool rd_supported(const DecodeArgs& a) {
     return false;
   const RdLayout L = rd_layout(d);
   const int G = ds::sm_count();
-  const int n_tasks = (sh ? 4 * (d.shared_inter / 8) : 0) + std::min(d.top_k, d.n_experts) * (d.inter / 8);
-  if ((n_tasks + G - 1) / G + 1 > kMaxTasksPerCta) return false;
+  const int n_sh = sh ? 4 * (d.shared_inter / 8) : 0, n_rt = std::min(d.top_k, d.n_experts) * (d.inter / 8);
+  if ((n_sh + G - 1) / G + (n_rt + G - 1) / G > kMaxTasksPerCta) return false;
+  if (d.hidden < G) return false;   // every CTA owns at least one output row
   return L.smem <= 200 * 1024;
 }
 
@@ -793,11 +729,7 @@ int launch_rd(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   p.ids = a.ids;
   p.gates = a.gates;
   p.out = a.out;
-  p.h_r = reinterpret_cast<float*>(ws + L.h_r);
-  p.hq8 = reinterpret_cast<uint8_t*>(ws + L.hq8);
-  p.hsc = reinterpret_cast<float*>(ws + L.hsc);
-  p.h_s = reinterpret_cast<float*>(ws + L.h_s);
-  p.hsp = reinterpret_cast<__nv_bfloat16*>(ws + L.hsp);
+  p.hq = reinterpret_cast<__half*>(ws + L.hq);
   p.part_sh = reinterpret_cast<float2*>(ws + L.part_sh);
   p.ctl = reinterpret_cast<unsigned*>(ws + L.ctl);
   p.err = a.err;
@@ -810,7 +742,6 @@ int launch_rd(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   p.limit = d.swiglu_limit;
   p.smem_a_part = L.a_part;
   p.smem_b_hq = L.b_hq;
-  p.smem_b_hsc = L.b_hsc;
   p.smem_b_hsp = L.b_hsp;
   p.smem_b_part = L.b_part;
   static const cudaError_t attr_rc =

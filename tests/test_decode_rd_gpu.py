@@ -33,9 +33,9 @@ def test_layer_vs_oracle(H, I, E, k, Is, std, cuda):
     assert rel_l2(out, ref) < TOL
 
 
-def test_f32_output_and_no_clamp(cuda):
+def test_f32_output(cuda):
     H, I, E, k = 2048, 1024, 16, 4
-    layer = layer_rd(H, I, E, seed=8, shared=1024, limit=None, std=0.05)
+    layer = layer_rd(H, I, E, seed=8, shared=1024, std=0.05)
     ids, wts = routing(1, E, k, seed=9)
     x = torch.randn(1, H, generator=torch.Generator().manual_seed(10)).to(torch.bfloat16)
     out = moe.moe_decode(x.cuda(), layer, ids.cuda(), wts.cuda(), out_f32=True)
@@ -44,8 +44,20 @@ def test_f32_output_and_no_clamp(cuda):
     # expert's output is rounded to bf16 in both, as in the reference)
     bf = moe.moe_decode(x.cuda(), layer, ids.cuda(), wts.cuda())
     assert torch.equal(out.to(torch.bfloat16), bf)
-    ref = oracle_out(x, ids, wts, layer, None)
-    assert rel_l2(bf, ref) < TOL
+    assert rel_l2(bf, oracle_out(x, ids, wts, layer, 10.0)) < TOL
+
+
+def test_no_clamp_one_token_takes_the_tcgen05_kernels(cuda):
+    """Without the SwiGLU clamp there is no bound for h, so one token of a
+    layer with scale atoms runs on the tcgen05 kernels; f32 output too."""
+    H, I, E, k = 2048, 1024, 16, 4
+    layer = layer_rd(H, I, E, seed=8, shared=1024, limit=None, std=0.05).prepare_tc()
+    ids, wts = routing(1, E, k, seed=9)
+    x = torch.randn(1, H, generator=torch.Generator().manual_seed(10)).to(torch.bfloat16)
+    bf = moe.moe_decode(x.cuda(), layer, ids.cuda(), wts.cuda())
+    f32 = moe.moe_decode(x.cuda(), layer, ids.cuda(), wts.cuda(), out_f32=True)
+    assert torch.equal(f32.to(torch.bfloat16), bf)
+    assert rel_l2(bf, oracle_out(x, ids, wts, layer, None)) < TOL
 
 
 def test_dropped_duplicate_and_out_of_range_slots(cuda):
