@@ -1113,15 +1113,13 @@ def run_decode(args) -> dict:
                          "launch_frac": round(launch_achieved / pk["hbm_gbs"], 4),
                          "traffic": traffic,
                          "kernel": "route_topk + ds_moe_decode: " + (
-                             ("rd_kernel (one cooperative launch: gate/up, grid barrier, down + combine)"
-                              if tokens == 1 else
-                              "t5_prep + t5_gemm(gate/up) + t5_h + t5_gemm(down) + t5_combine")
+                             "t5_prep + t5_gemm(gate/up) + t5_h + t5_gemm(down) + t5_combine"
                              if fmt == "fp4" else "q3_gate_up + q3_down + q3_combine"),
                          "bytes_per_launch": step_bytes, "peak_kind": kind},
             "e2e": {"value": round(world * tokens * args.steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * (H * 2 + E * 4), "d2h_bytes_per_step": tokens * H * 2},
             # router + the layer's decode kernels, per step
-            "gpu_launches": (1 + (1 if tokens == 1 else 5) if fmt == "fp4" else 1 + 3) * args.steps,
+            "gpu_launches": (1 + 5 if fmt == "fp4" else 1 + 3) * args.steps,
             "clocks": clocks,
         }
     if dist is not None:

@@ -788,24 +788,22 @@ int dispatch_tokens(const DecodeArgs& a, cudaStream_t st) {
 // caller provides (workspace_bytes); ds_moe_decode and ds_moe_decode_noalloc
 // both come through here, so a given (layer, tokens, scratch size) always runs
 // the same kernels:
-//   one token, FP4 banks, bf16 x         -> register-dequant kernel (moe_decode_rd.cu)
 //   FP4 banks with scale atoms, bf16 x  -> tcgen05 kernels (moe_decode_t5.cu)
+//   one token, FP4 banks, bf16 x         -> register-dequant kernel (moe_decode_rd.cu)
 //   Q3 banks, bf16 x                    -> dp2a CUDA-core kernels (moe_decode_q3.cu)
-//   single-token FP4 without atoms      -> mma.sync kernels (moe_decode_tc.cu)
 //   anything else (f32 x, ...)          -> the generic kernels above
-// A path whose scratch does not fit in workspace_bytes is skipped.
-// `uncached`: encode tensor maps on the stack for this call only.
-int dispatch(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t s, bool uncached) {
-  if (ds::decode::rd_supported(a) && workspace_bytes >= ds::decode::rd_workspace_bytes(a.d))
-    return ds::decode::launch_rd(a, workspace, workspace_bytes, s);
+// A path whose scratch does not fit in workspace_bytes is skipped.  (At one
+// token the tcgen05 kernels stream config 2's layer faster than the
+// register-dequant kernel, measured; the latter serves banks without atoms.)
+int dispatch(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t s) {
   if (ds::decode::t5_supported(a) && workspace_bytes >= ds::decode::t5_workspace_bytes(a.d, a.tokens))
     return ds::decode::launch_t5(a, workspace, workspace_bytes, s);
+  if (ds::decode::rd_supported(a) && workspace_bytes >= ds::decode::rd_workspace_bytes(a.d))
+    return ds::decode::launch_rd(a, workspace, workspace_bytes, s);
   if (ds::decode::q3_supported(a) && workspace_bytes >= ds::decode::q3_workspace_bytes(a.d, a.tokens))
     return ds::decode::launch_q3(a, workspace, workspace_bytes, s);
   DS_REQUIRE(!a.d.out_f32 || a.x_f32, DS_ENOTSUP,
-             "moe_decode: out_f32 with bf16 x needs FP4 banks with scale atoms or Q3 banks");
-  if (ds::decode::tc_supported(a))
-    return uncached ? ds::decode::launch_tc_uncached(a, s) : ds::decode::launch_tc(a, s);
+             "moe_decode: out_f32 with bf16 x needs FP4 banks (with scale atoms above one token) or Q3 banks");
   return a.d.w1.format == DS_FMT_FP4 ? dispatch_tokens<DS_FMT_FP4>(a, s) : dispatch_tokens<DS_FMT_Q3>(a, s);
 }
 
@@ -849,7 +847,7 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
   a.max_slots = w.max_slots;
   a.h_stride = w.h_stride;
   a.err = reinterpret_cast<int*>(static_cast<char*>(workspace) + w.err_off);
-  return dispatch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), false);
+  return dispatch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 // ============================================================== qmm host side
@@ -914,7 +912,7 @@ extern "C" int ds_qmm(const DsExpertBank* w, const void* x, int x_dtype, int64_t
 // allocation, implicit or not.  ds_moe_decode_noalloc takes its scratch
 // from a file-scope __device__ array instead: the CUDA runtime reserves it
 // when the module is loaded, so the call itself allocates no device memory
-// (tensor maps live in fixed static tables or on the stack).
+// (tensor maps live in fixed static tables).
 
 namespace {
 
@@ -991,7 +989,7 @@ extern "C" int ds_moe_decode_noalloc(const DsMoeDesc* desc, const void* x, int x
   a.max_slots = w.max_slots;
   a.h_stride = w.h_stride;
   a.err = static_cast<int*>(scratch);
-  return dispatch(a, scratch, kNoAllocScratchBytes, s, true);
+  return dispatch(a, scratch, kNoAllocScratchBytes, s);
 }
 
 extern "C" int ds_moe_decode_noalloc_status(int32_t* err, void* stream) {

@@ -1,5 +1,6 @@
-// Shared definitions of the decode MoE kernels (moe_decode.cu: generic path,
-// moe_decode_tc.cu: single-token tensor-core pipeline).
+// Shared definitions of the decode MoE kernels (moe_decode.cu: kernel
+// selection and generic path, moe_decode_rd.cu: single-token register
+// dequant, moe_decode_t5.cu: tcgen05, moe_decode_q3.cu: q3 banks).
 #pragma once
 
 #include "ds_common.cuh"
@@ -106,14 +107,6 @@ __device__ inline void build_slots(const DecodeArgs& a, Slots& s) {
   __syncthreads();
 }
 
-
-// Single-token tensor-core pipeline (moe_decode_tc.cu).  Returns true and
-// launches when the geometry is supported; false means "use the generic path".
-bool tc_supported(const DecodeArgs& a);
-int launch_tc(const DecodeArgs& a, cudaStream_t st);
-// Same launch, tensor maps encoded on the stack for this call only (no cache,
-// so no host heap either).
-int launch_tc_uncached(const DecodeArgs& a, cudaStream_t st);
 
 // Single-token register-dequant pipeline (moe_decode_rd.cu): FP4 banks (no
 // scale atoms needed), bf16 x, one cooperative kernel per layer.  Its

@@ -168,8 +168,9 @@ typedef struct DsMoeDesc {
   int32_t out_f32;       /* ds_moe_decode with bf16 x: 1 writes the layer
                             output in f32 without the final rounding (partial
                             sums that another rank adds to), 0 = x's dtype.
-                            Needs the tensor-core decode kernels (FP4 banks
-                            with scale atoms); DS_ENOTSUP otherwise.         */
+                            Served by FP4 banks with scale atoms, by one
+                            token over FP4 banks with swiglu_limit > 0, and
+                            by Q3 banks; DS_ENOTSUP otherwise.               */
 } DsMoeDesc;
 
 /* Workspace bytes ds_moe_decode needs for `tokens` rows.  The first 4096
@@ -286,7 +287,9 @@ int ds_dense_swiglu(const float* x, int64_t tokens, int hidden, int inter, int n
  * of ds_moe_decode_noalloc_max_scratch() bytes (8 MiB) per device.
  *   - Kernels: exactly those ds_moe_decode runs when given a workspace of
  *     that size (the fastest path whose scratch fits: tcgen05 for FP4 banks
- *     with scale atoms, the q3 kernels for Q3 banks, else the generic ones),
+ *     with scale atoms, the single-token register-dequant kernel for one
+ *     token over FP4 banks without them, the q3 kernels for Q3 banks, else
+ *     the generic ones),
  *     so results equal ds_moe_decode's bit for bit whenever
  *     ds_moe_decode_workspace_size() <= the limit, and stay within the
  *     decode tolerance (rel-L2 <= 1e-3 of the f32 oracle) otherwise.
@@ -296,8 +299,9 @@ int ds_dense_swiglu(const float* x, int64_t tokens, int hidden, int inter, int n
  *   - The first call on each device resolves the array's address (setup,
  *     cudaGetSymbolAddress with that device current); make that first call
  *     before any stream capture and before any latency-sensitive phase.
- *   - Each call clears the array's error word on `stream` (cudaMemsetAsync);
- *     nothing else has to start at zero.  ds_moe_decode_noalloc_status reads
+ *   - Each call clears the array's 4096-byte reserved head (error word and
+ *     control words) on `stream` (cudaMemsetAsync); nothing else has to start
+ *     at zero.  ds_moe_decode_noalloc_status reads
  *     the word back: bit 0 = an expert id >= n_experts was skipped, bit 1 = a
  *     bounded device wait gave up (outputs of that call are then undefined).
  *   - All calls on one device share the array: two calls that may overlap

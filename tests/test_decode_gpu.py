@@ -153,13 +153,13 @@ def test_invalid_arguments(cuda):
         moe.moe_decode(x[:1, :64].contiguous(), layer, ids[:1], torch.ones(1, 2, device="cuda"))
 
 
-# ---------------------------------------------------------------- single-token tensor-core path
+# ---------------------------------------------------------------- single token, FP4 banks without scale atoms
 
 @pytest.mark.parametrize("k,shared", [(4, True), (3, True), (5, False), (1, True)])
-def test_tc_path_single_token(k, shared, cuda):
-    """H % 1024 == 0 and I % 512 == 0 route single-token bf16 FP4 layers to the
-    pipelined tensor-core kernels; odd slot counts, no shared expert and top-1
-    exercise the pair / unit bookkeeping."""
+def test_single_token_path(k, shared, cuda):
+    """One bf16 token over FP4 banks without scale atoms runs on the
+    register-dequant kernel; odd slot counts, no shared expert and top-1
+    exercise its task bookkeeping."""
     H, I, E = 1024, 512, 16
     layer = synthetic.make_layer("fp4", H, I, E, seed=40 + k, shared_inter=1024 if shared else None, std=0.05)
     for seed in range(3):
@@ -170,7 +170,7 @@ def test_tc_path_single_token(k, shared, cuda):
         assert rel_l2(out, ref) < TOL, (seed, rel_l2(out, ref))
 
 
-def test_tc_path_dropped_and_duplicate_slots(cuda):
+def test_single_token_dropped_and_duplicate_slots(cuda):
     H, I, E = 2048, 1024, 8
     layer = synthetic.make_layer("fp4", H, I, E, seed=77, shared_inter=1024, std=0.05)
     ids = torch.tensor([[6, -1, 2, 6]], dtype=torch.int32)     # dropped slot, duplicate expert
@@ -185,7 +185,7 @@ def test_tc_path_dropped_and_duplicate_slots(cuda):
     assert rel_l2(out, ref) < TOL
 
 
-def test_tc_path_matches_generic_path(cuda):
+def test_single_token_matches_generic_path(cuda):
     """Token 0 through the single-token FP4 kernels (one-token call) and through
     the generic kernels (the same token as row 0 of a two-token call, FP4
     banks without scale atoms) agrees to well inside the tolerance."""
@@ -198,7 +198,7 @@ def test_tc_path_matches_generic_path(cuda):
     assert rel_l2(one[0], two[0]) < 2e-3
 
 
-def test_tc_path_no_routes_no_shared_is_zero(cuda):
+def test_single_token_no_routes_no_shared_is_zero(cuda):
     layer = synthetic.make_layer("fp4", 1024, 512, 8, seed=9, shared_inter=None, std=0.05)
     ids = torch.full((1, 2), -1, dtype=torch.int32, device="cuda")
     out = torch.full((1, 1024), 7.0, dtype=torch.bfloat16, device="cuda")
