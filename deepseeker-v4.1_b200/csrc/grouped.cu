@@ -28,13 +28,10 @@
 // lane quarter), warps 6-9 drain the double-buffered accumulators.
 // Every wait is bounded; a timeout sets an error bit and an abort flag that
 // makes every other role leave its loop.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 
 #include "align.cuh"
-#include "ptx.cuh"
+#include "grouped.cuh"
 #include "tc5.cuh"
 
 namespace ds {
@@ -43,19 +40,13 @@ namespace {
 
 using namespace ds::ptx;
 
-constexpr int kBlock = 16;      // expert runs are padded to this many rows (MMA N step)
 constexpr int kTileRows = 64;   // token rows per tile (MMA N <= 64)
 constexpr int kWarps = 10;
 constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarp0 = 6;  // warps 2..5 stage scales, 6..9 run the epilogue
-constexpr int kSfAtom = 512;                  // 128 rows x 4 ue8m0 bytes (one 128-wide K chunk)
 constexpr int kSfStage = 4 * kSfAtom;         // scale atoms of one stage
 constexpr int kHPieces = 3, kXPieces = 2;
 constexpr uint32_t kTxBytes = 34816;          // per stage, both modes (see Cfg)
-constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s
-constexpr int kErrTimeout = 2;
-
-enum { GATEUP = 0, DOWN = 1 };
 
 template <int MODE>
 struct Cfg;
@@ -103,53 +94,6 @@ struct Params {
   float limit;
   int gate_in_h;              // route weight applied to h (before the down projection)
 };
-
-// Bounded mbarrier wait that also gives up when another role has aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = 0;
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0u) {
-      if (*abort) return false;
-      const uint64_t now = globaltimer_ns();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > kWaitNs) {
-        *abort = 1;
-        atomicOr(err, kErrTimeout);
-        return false;
-      }
-    }
-  }
-}
-
-// Warp-uniform version: lane 0 waits, the verdict is broadcast, and every lane
-// then observes the completed phase itself (it cannot advance without us).
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = wait_or_abort(bar, parity, abort, err) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  if (ok) (void)mbar_try_wait(bar, parity);
-  return ok != 0;
-}
-
-__device__ __forceinline__ float silu_glu(float g, float u, float limit) {
-  if (limit > 0.0f) {
-    g = fminf(g, limit);
-    u = fminf(fmaxf(u, -limit), limit);
-  }
-  return (g / (1.0f + expf(-g))) * u;
-}
-
-// ue8m0 byte for piece `pc` of a block whose maximum has f32 exponent field
-// `ef`: piece 0 maps the maximum into [128, 256), each later piece is 2^5 finer.
-__device__ __forceinline__ int piece_scale(int ef, int pc) { return min(max(ef - 7 - 5 * pc, 1), 253); }
-__device__ __forceinline__ float scale_of(int sfb) { return __uint_as_float((uint32_t)sfb << 23); }
-__device__ __forceinline__ float inv_scale_of(int sfb) { return __uint_as_float((uint32_t)(254 - sfb) << 23); }
-
-// Offset of (row r, k-block kb of the chunk) inside a 512-byte scale atom.
-__device__ __forceinline__ int atom_off(int r, int kb) { return (r & 31) * 16 + (r >> 5) * 4 + kb; }
 
 template <int MODE>
 __device__ __forceinline__ void epilogue(const Params& p, uint32_t dacc, int N, int row0, int tile, int mt, int q,
@@ -448,42 +392,6 @@ __global__ void __launch_bounds__(256) xquant_kernel(const __nv_bfloat16* __rest
   }
 }
 
-// out[t] = sum over slots (top-k order) of [w] * y[row of the pair].
-// An expert id out of range makes the align step report n_pad = -1 and leave
-// the pair positions unwritten: the output is then NaN and error bit 1 is set.
-template <typename OutT>
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
-                                                      const float* __restrict__ topk_w, const int32_t* n_pad, int* err,
-                                                      int k, int H, int route_after, OutT* __restrict__ out) {
-  const int t = blockIdx.x;
-  if (*n_pad < 0) {
-    if (t == 0 && threadIdx.x == 0) atomicOr(err, 1);
-    for (int h = threadIdx.x; h < H; h += blockDim.x) out[(size_t)t * H + h] = (OutT)__int_as_float(0x7FC00000);
-    return;
-  }
-  for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < k; ++s) {
-      const int ps = pos[t * k + s];
-      if (ps < 0) continue;
-      const float w = route_after ? topk_w[t * k + s] : 1.0f;
-      const float4 v = *reinterpret_cast<const float4*>(y + (size_t)ps * H + h);
-      acc.x = fmaf(w, v.x, acc.x);
-      acc.y = fmaf(w, v.y, acc.y);
-      acc.z = fmaf(w, v.z, acc.z);
-      acc.w = fmaf(w, v.w, acc.w);
-    }
-    OutT* o = out + (size_t)t * H + h;
-    if constexpr (sizeof(OutT) == 4) {
-      *reinterpret_cast<float4*>(o) = acc;
-    } else {
-      __nv_bfloat162 a = __floats2bfloat162_rn(acc.x, acc.y), b = __floats2bfloat162_rn(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(o) =
-          make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-    }
-  }
-}
-
 // Scale re-layout: [E][rows][K/32] ue8m0 -> [E][rows/128][K/128][mats][512-byte atom],
 // atom byte (r%32)*16 + (r/32)*4 + kb holds k-block kb of row r.  With two
 // matrices (W1, W3) their atoms of the same (tile, chunk) are adjacent.
@@ -508,18 +416,6 @@ __global__ void prep_scales_kernel(const uint8_t* __restrict__ s0, const uint8_t
 
 // ---------------------------------------------------------------- host side
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      f = nullptr;
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  }();
-  return fn;
-}
-
 // FP4 weights [rows][K/2] as e2m1 codes with 16U4_ALIGN16B (16 codes -> 16
 // bytes of shared memory), viewed as {128 codes, rows, K/128 chunks}.
 bool map_fp4(CUtensorMap* m, const void* base, uint64_t rows, uint64_t K, uint32_t box_rows) {
@@ -531,19 +427,6 @@ bool map_fp4(CUtensorMap* m, const void* base, uint64_t rows, uint64_t K, uint32
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-
-// e4m3 pieces [rows][pieces * K] viewed as {128 B, rows, pieces * K / 128}.
-bool map_pieces(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
-  const cuuint64_t dims[3] = {128, rows, row_bytes / 128};
-  const cuuint64_t strides[2] = {row_bytes, 128};
-  const cuuint32_t box[3] = {128, box_rows, 1};
-  const cuuint32_t es[3] = {1, 1, 1};
-  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-size_t up(size_t v, size_t a = 1024) { return (v + a - 1) / a * a; }
 
 struct Layout {
   int64_t mk, cap, max_tiles;
@@ -571,12 +454,15 @@ Layout layout(const DsMoeDesc* d, int64_t T) {
   return L;
 }
 
+bool is_q3(const DsMoeDesc* d) { return d != nullptr && d->w1.format == DS_FMT_Q3; }
+
 int validate(const DsMoeDesc* d, int64_t T) {
   DS_REQUIRE(d != nullptr, DS_EINVAL, "grouped_ffn: null descriptor");
   DS_REQUIRE(T >= 1 && d->top_k >= 1 && T * d->top_k < ((int64_t)1 << 30), DS_EINVAL,
              "grouped_ffn: tokens and top_k must be >= 1");
+  if (is_q3(d)) return q3_validate(d);
   DS_REQUIRE(d->w1.format == DS_FMT_FP4 && d->w3.format == DS_FMT_FP4 && d->w2.format == DS_FMT_FP4, DS_ENOTSUP,
-             "grouped_ffn: expert banks must be FP4");
+             "grouped_ffn: expert banks must be all FP4 or all Q3");
   DS_REQUIRE(d->n_experts >= 1 && d->n_experts <= align::kMaxExperts, DS_ENOTSUP,
              "grouped_ffn: n_experts must be in [1, %d]", align::kMaxExperts);
   DS_REQUIRE(d->hidden % 128 == 0 && d->inter % 128 == 0 && d->hidden > 0 && d->inter > 0, DS_EINVAL,
@@ -598,6 +484,41 @@ int validate(const DsMoeDesc* d, int64_t T) {
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+bool map_pieces(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
+  const cuuint64_t dims[3] = {128, rows, row_bytes / 128};
+  const cuuint64_t strides[2] = {row_bytes, 128};
+  const cuuint32_t box[3] = {128, box_rows, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_combine(const float* y, const int32_t* pos, const float* topk_w, const int32_t* n_pad, int* err, int k,
+                   int H, int route_after, void* out, int out_dtype, int64_t tokens, cudaStream_t s) {
+  if (out_dtype == DS_F32)
+    combine_kernel<float><<<(unsigned)tokens, 256, 0, s>>>(y, pos, topk_w, n_pad, err, k, H, route_after,
+                                                            static_cast<float*>(out));
+  else
+    combine_kernel<__nv_bfloat16><<<(unsigned)tokens, 256, 0, s>>>(y, pos, topk_w, n_pad, err, k, H, route_after,
+                                                                    static_cast<__nv_bfloat16*>(out));
+  DS_CHECK_LAUNCH("combine_kernel");
+  return DS_OK;
+}
+
 }  // namespace grouped
 }  // namespace ds
 
@@ -607,6 +528,10 @@ extern "C" int ds_grouped_scales_size(const DsMoeDesc* desc, size_t* w13_bytes, 
   int st = validate(desc, 1);
   if (st != DS_OK) return st;
   DS_REQUIRE(w13_bytes && w2_bytes, DS_EINVAL, "grouped_scales_size: null output");
+  if (is_q3(desc)) {   // q3 banks are read as stored
+    *w13_bytes = *w2_bytes = 0;
+    return DS_OK;
+  }
   const size_t E = desc->n_experts, H = desc->hidden, I = desc->inter;
   *w13_bytes = E * (I / 128) * (H / 128) * 2 * kSfAtom;
   *w2_bytes = E * (H / 128) * (I / 128) * kSfAtom;
@@ -616,6 +541,7 @@ extern "C" int ds_grouped_scales_size(const DsMoeDesc* desc, size_t* w13_bytes, 
 extern "C" int ds_grouped_prepare_scales(const DsMoeDesc* desc, void* w13_sf, void* w2_sf, void* stream) {
   int st = validate(desc, 1);
   if (st != DS_OK) return st;
+  if (is_q3(desc)) return DS_OK;
   DS_REQUIRE(w13_sf && w2_sf && ds::aligned(w13_sf, 16) && ds::aligned(w2_sf, 16), DS_EALIGN,
              "grouped_prepare_scales: outputs must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -651,7 +577,7 @@ extern "C" int ds_grouped_ffn_workspace_size(const DsMoeDesc* desc, int64_t toke
   int st = validate(desc, tokens);
   if (st != DS_OK) return st;
   DS_REQUIRE(bytes != nullptr, DS_EINVAL, "grouped_ffn_workspace_size: null output");
-  *bytes = layout(desc, tokens).total;
+  *bytes = is_q3(desc) ? q3_workspace_bytes(desc, tokens) : layout(desc, tokens).total;
   return DS_OK;
 }
 
@@ -662,6 +588,9 @@ extern "C" int ds_grouped_ffn(const DsMoeDesc* desc, const void* w13_sf, const v
   if (st != DS_OK) return st;
   DS_REQUIRE(x_dtype == DS_BF16, DS_ENOTSUP, "grouped_ffn: x must be bf16");
   DS_REQUIRE(out_dtype == DS_BF16 || out_dtype == DS_F32, DS_EINVAL, "grouped_ffn: out_dtype must be bf16 or f32");
+  if (is_q3(desc))
+    return q3_ffn(desc, x, tokens, topk_ids, topk_w, out, out_dtype, workspace, workspace_bytes,
+                  static_cast<cudaStream_t>(stream));
   DS_REQUIRE(w13_sf && w2_sf && x && topk_ids && topk_w && out && workspace, DS_EINVAL,
              "grouped_ffn: null pointer");
   DS_REQUIRE(ds::aligned(x, 16) && ds::aligned(out, 16) && ds::aligned(workspace, 256) &&
@@ -739,13 +668,6 @@ extern "C" int ds_grouped_ffn(const DsMoeDesc* desc, const void* w13_sf, const v
   gemm_kernel<DOWN><<<grid_b, kThreads, smem_bytes<DOWN>(), s>>>(p);
   DS_CHECK_LAUNCH("gemm_kernel<down>");
 
-  if (out_dtype == DS_F32)
-    combine_kernel<float><<<(unsigned)tokens, 256, 0, s>>>(y, pos, topk_w, ints, ints + 2, k, H,
-                                                            desc->route_before_down ? 0 : 1, static_cast<float*>(out));
-  else
-    combine_kernel<__nv_bfloat16><<<(unsigned)tokens, 256, 0, s>>>(y, pos, topk_w, ints, ints + 2, k, H,
-                                                                    desc->route_before_down ? 0 : 1,
-                                                                    static_cast<__nv_bfloat16*>(out));
-  DS_CHECK_LAUNCH("combine_kernel");
-  return DS_OK;
+  return launch_combine(y, pos, topk_w, ints, ints + 2, k, H, desc->route_before_down ? 0 : 1, out, out_dtype,
+                        tokens, s);
 }

@@ -44,6 +44,12 @@ __device__ __forceinline__ uint32_t idesc_e2m1_e4m3(int n, uint32_t sf_id) {
          (sf_id << 29);
 }
 
+// Same, A = B = E4M3 (MXFP8).
+__device__ __forceinline__ uint32_t idesc_e4m3_e4m3(int n, uint32_t sf_id) {
+  return (sf_id << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | (8u << 24) |
+         (sf_id << 29);
+}
+
 __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                              uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
   asm volatile(

@@ -134,28 +134,17 @@ class ExpertParallelMoE:
 # ---------------------------------------------------------------- GPU defaults
 
 def gpu_local_ffn(local_layer) -> LocalFFN:
-    """Owner-side expert FFN on the B200 kernels: FP4 shards run ds_grouped_ffn
-    (top_k = 1, f32 rows); Q3 shards run the decode kernels on 8-row chunks."""
-    from . import _abi, grouped, moe
+    """Owner-side expert FFN on the B200 kernels: FP4 and q3 shards both run
+    ds_grouped_ffn (top_k = 1, f32 rows), so every local expert's weights
+    stream once per call whatever the number of rows routed to it."""
+    from . import grouped
 
-    if local_layer.w1.fmt == _abi.DS_FMT_FP4:
-        ffn = grouped.GroupedFFN(local_layer, 1)
+    ffn = grouped.GroupedFFN(local_layer, 1)
 
-        def run(xr, expert, gate):
-            return ffn(xr.to(torch.bfloat16).contiguous(), expert.view(-1, 1).contiguous(),
-                       gate.view(-1, 1).contiguous(), route_before_down=True, out_dtype=torch.float32)
-        return run
-
-    def run_q3(xr, expert, gate):
-        R, H = xr.shape
-        out = torch.zeros(R, H, dtype=torch.float32, device=xr.device)
-        for r0 in range(0, R, moe.MAX_DECODE_TOKENS):
-            r1 = min(R, r0 + moe.MAX_DECODE_TOKENS)
-            out[r0:r1] = moe.moe_decode(xr[r0:r1].float().contiguous(), local_layer,
-                                        expert[r0:r1].view(-1, 1).contiguous(),
-                                        gate[r0:r1].view(-1, 1).contiguous())
-        return out
-    return run_q3
+    def run(xr, expert, gate):
+        return ffn(xr.to(torch.bfloat16).contiguous(), expert.view(-1, 1).contiguous(),
+                   gate.view(-1, 1).contiguous(), route_before_down=True, out_dtype=torch.float32)
+    return run
 
 
 def gpu_shared_fn(local_layer) -> SharedFn | None:

@@ -8,10 +8,13 @@ Drop-in for ``deepseeker.grouped`` (src/deepseeker/grouped.py):
     per-expert weights ``weights[e] = (gate [H, I], up [H, I], down [I, H])``
     (grouped.py:34-81), executed by ``ds_dense_swiglu`` in f32 with the
     reference's addition order;
-plus the FP4 bank path the batched workloads use:
+plus the resident-bank path the batched workloads use (the batched expert
+loop of ``moe_layer`` / ``gather_pinned_contributions``, mlx_forward.py:159-210):
   * ``GroupedFFN(layer)`` / ``grouped_ffn(x, layer, topk_ids, topk_w)`` --
     pairs sorted by expert on the device and pushed through tcgen05
-    block-scaled MMAs (``ds_grouped_ffn``, grouped.cu).
+    block-scaled MMAs (``ds_grouped_ffn``): FP4 banks as e2m1 operands
+    (grouped.cu), q3 banks dequantised in shared memory to exact e4m3 codes
+    with the per-64 scale and bias applied per group (grouped_q3.cu).
 """
 from __future__ import annotations
 
@@ -110,12 +113,13 @@ def naive_swiglu(x: torch.Tensor, weights: dict, topk_ids: list[list[int]],
 
 
 class GroupedFFN:
-    """FP4 expert layer prepared for the batched grouped path: holds the
-    re-laid-out scales (same bytes as the bank scales) and a workspace."""
+    """Expert layer prepared for the batched grouped path: FP4 banks hold
+    their re-laid-out scales (same bytes as the bank scales), q3 banks are
+    read as stored; plus a workspace."""
 
     def __init__(self, layer: MoEWeights, top_k: int):
-        if layer.w1.fmt != _abi.DS_FMT_FP4:
-            raise NotImplementedError("grouped_ffn needs FP4 expert banks")
+        if layer.w1.fmt not in (_abi.DS_FMT_FP4, _abi.DS_FMT_Q3):
+            raise NotImplementedError("grouped_ffn needs FP4 or q3 expert banks")
         self.layer = layer
         self.top_k = top_k
         self._desc = self._routed_desc(top_k)
