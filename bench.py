@@ -505,7 +505,9 @@ def run_stack(args) -> dict:
     """a decode step through a 40-layer stack (layers 0-19
     FP4, 20-39 q3, each a config-2 layer), --batch tokens per GPU per step,
     each layer's output feeding the next.  N = 1: all 256 experts of every
-    layer on the GPU (131 GB resident), the whole step one CUDA graph.
+    layer on the GPU (131 GB resident), the whole step one CUDA graph (batch
+    <= 8: the decode kernels; above: the grouped kernels for the routed
+    experts and bf16 GEMMs for the shared expert).
     N > 1: rank g holds experts [g E/N, (g+1) E/N) of every layer; with
     N * batch <= 8 the layers exchange through ds_ep_decode (NVLink peer
     memory, one CUDA graph per step), otherwise through NCCL all-to-all."""
@@ -513,7 +515,7 @@ def run_stack(args) -> dict:
 
     import torch
 
-    from deepseeker import ep, moe, synthetic
+    from deepseeker import ep, grouped, moe, synthetic
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -547,7 +549,32 @@ def run_stack(args) -> dict:
     stream = torch.cuda.current_stream(dev)
     graph = None
     comm = None
-    if world == 1:
+    if world == 1 and b > 8:
+        # one graph: for every layer, routing + the grouped FFN over the
+        # routed experts (each used expert's weights once per step) + the
+        # shared expert as bf16 GEMMs, ping-pong activation buffers
+        ffns = [grouped.GroupedFFN(layer, K_TOP) for layer in layers]
+        bufs = [torch.zeros(b, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        wbuf = torch.empty(b, K_TOP, dtype=torch.float32, device=dev)
+        ibuf = torch.empty(b, K_TOP, dtype=torch.int32, device=dev)
+        rout = torch.empty(b, H, dtype=torch.float32, device=dev)
+
+        def body():
+            cur = stage_x
+            for l, layer in enumerate(layers):
+                nxt = bufs[l % 2]
+                moe.route_softmax_topk(stage_l[l], K_TOP, out=(wbuf, ibuf))
+                ffns[l](cur, ibuf, wbuf, out=rout, route_before_down=True)
+                rout.add_(ep.shared_dense(layer.shared_w1, layer.shared_w3, layer.shared_w2, cur))
+                nxt.copy_(rout)
+                cur = nxt
+            return cur
+        out_buf = body()                          # eager once: workspaces, attributes
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out_buf = body()
+    elif world == 1:
         # one graph: for every layer, routing + the decode kernels over
         # chunks of 8 tokens, ping-pong activation buffers
         bufs = [torch.zeros(b, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
@@ -675,7 +702,9 @@ def run_stack(args) -> dict:
         dist.all_gather_into_tensor(gathered, ids_all.contiguous())
         ids_all = gathered.permute(1, 2, 0, 3, 4).reshape(args.steps, NL, -1)
     ids_all = ids_all.reshape(args.steps, NL, -1).cpu()
-    shared_b = 3 * IS * H * 2 // world if (peer and IS % (256 * world) == 0) else 3 * IS * H * 2 * ((b + 7) // 8)
+    # the shared expert streams once per step (decode kernels up to 8 rows, one
+    # set of GEMMs above), split over the ranks on the peer path
+    shared_b = 3 * IS * H * 2 // world if (peer and IS % (256 * world) == 0) else 3 * IS * H * 2
     tot = 0.0
     for st_ in range(args.steps):
         for l in range(NL):
@@ -710,7 +739,9 @@ def run_stack(args) -> dict:
                        "resident_gb_per_gpu": round(sum(sum(bk.nbytes() for bk in (ly.w1, ly.w3, ly.w2)) +
                                                         3 * IS * H * 2 for ly in layers) / 1e9, 1),
                        "l2": "each step streams every layer's experts once (the stack is far above L2)",
-                       "parallelism": ("single GPU, the step in one CUDA graph" if world == 1 else
+                       "parallelism": ((f"single GPU, the step in one CUDA graph ("
+                                        + ("grouped routed FFN + bf16 GEMM shared expert" if b > 8 else
+                                           "decode kernels") + ")") if world == 1 else
                                        f"ep{world} over NVLink peer memory (ds_ep_decode), the step in one CUDA graph"
                                        if peer else f"ep{world} over NCCL all_to_all_single")},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -720,12 +751,11 @@ def run_stack(args) -> dict:
             "e2e": {"value": round(world * b * max(e2e_steps, 1) / (e2e_ms * 1e-3), 2) if e2e_steps else None,
                     "unit": "tokens/s", "h2d_bytes_per_step": b * (H * 2 + NL * E * 4),
                     "d2h_bytes_per_step": b * H * 2},
-            # ours per layer: router + the single-token kernel (FP4, b = 1, one GPU)
-            # or prep/gemm/h/gemm/combine (FP4, tcgen05) or gate_up/down/combine
-            # (q3) per 8-token chunk, + 2 exchange kernels (peer)
+            # ours per layer: router + prep/gemm/h/gemm/combine (FP4, tcgen05) or
+            # gate_up/down/combine (q3), + 2 exchange kernels (peer); above 8
+            # tokens on one GPU: router + align/xquant/gemm/gemm/combine
             "gpu_launches": args.steps * sum(
-                1 + ((1 if (b == 1 and world == 1) else 5) if f == "fp4" else 3)
-                * (((b + 7) // 8) if world == 1 else 1) + (2 if peer else 0)
+                1 + ((5 if f == "fp4" else 3) + (2 if peer else 0) if b <= 8 else 5)
                 for f in fmts) if (world == 1 or peer) else None,
             "clocks": clocks,
         }

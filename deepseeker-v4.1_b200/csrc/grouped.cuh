@@ -22,22 +22,20 @@ constexpr int kErrTimeout = 2;
 enum { GATEUP = 0, DOWN = 1 };
 
 // Bounded mbarrier wait that also gives up when another role has aborted.
+// Between checks the thread is suspended in try_wait (it resumes when the
+// phase completes), so waiting roles leave the issue slots to the warps
+// that convert and drain.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
   using namespace ds::ptx;
-  if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = 0;
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0u) {
-      if (*abort) return false;
-      const uint64_t now = globaltimer_ns();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > kWaitNs) {
-        *abort = 1;
-        atomicOr(err, kErrTimeout);
-        return false;
-      }
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      *abort = 1;
+      atomicOr(err, kErrTimeout);
+      return false;
     }
   }
 }
@@ -48,7 +46,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   int ok = 0;
   if ((threadIdx.x & 31) == 0) ok = wait_or_abort(bar, parity, abort, err) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
-  if (ok) (void)ds::ptx::mbar_try_wait(bar, parity);
+  if (ok) (void)ds::ptx::mbar_test_wait(bar, parity);
   return ok != 0;
 }
 

@@ -13,24 +13,28 @@
 // which equals sum_k (s q + b) a with the weights never rounded.
 //
 // Launch sequence (one stream, no host sync):
-//   1. align   : expert runs padded to 16 rows, cut into tiles of <= 32 rows;
+//   1. align   : expert runs padded to 16 rows, cut into tiles of 16 rows;
 //   2. xquant  : every padded row's x as two e4m3 pieces (hi + lo reproduce a
 //                bf16 value), per-32 ue8m0 scales, and per-64 sums of x;
 //   3. gate/up : per (tile, 128 rows of I): W1 and W3 codes converted to e4m3
-//                in shared memory, one accumulator pair per 64-group; the
-//                epilogue adds s * D + b * X per group into f32 sums, then
+//                in shared memory, one accumulator per 64-group and matrix;
+//                the epilogue adds s * D + b * X per group into f32 sums, then
 //                writes h = silu(min(g, L)) * clip(u, +-L) [* route weight]
 //                as three e4m3 pieces with per-32 scales and h's 32-row sums;
 //   4. down    : the same over W2 with h's three pieces, f32 rows out;
 //   5. combine : shared with the FP4 path.
 //
-// Persistent GEMM kernels, one CTA per SM, 320 threads: warp 0 issues TMA
+// Persistent GEMM kernels, one CTA per SM, 448 threads: warp 0 issues TMA
 // copies into a ring (each weight row's 48 code bytes per 128-wide K stage,
 // the tile's activation pieces, their scale atom), warp 1 issues the MMAs and
-// owns tensor memory, warps 2-5 convert codes to e4m3 in the 128-byte-swizzled
-// operand layout and stage the activation scale atom in tensor memory, warps
-// 6-9 run the epilogue.  B operand row `pieces * t + p` holds piece p of the
-// tile's token t, so one MMA covers every piece.  Every wait is bounded; a
+// owns tensor memory, warps 2-9 convert codes to e4m3 in the 128-byte-swizzled
+// operand layout (two per scheduler: the conversion is ALU work with short
+// dependency chains) and warps 2-5 also stage the activation scale atom in
+// tensor memory, warps 10-13 run the epilogue.  B operand row `pieces * t + p` holds piece p of the
+// tile's token t, so one MMA covers every piece.  The accumulators of a whole
+// stage (both groups) form one tensor-memory buffer with one commit / wait /
+// release, and three or four such buffers let the MMAs run ahead of the
+// epilogue: the group-by-group handshake was what paced the pipeline.  Every wait is bounded; a
 // timeout sets an error bit and an abort flag that ends every role.
 #include <algorithm>
 
@@ -44,31 +48,35 @@ namespace {
 
 using namespace ds::ptx;
 
-constexpr int kQR = 32;              // token rows per tile
-constexpr int kQThreads = 320;       // 10 warps
+constexpr int kQR = 16;              // token rows per tile
+constexpr int kQThreads = 448;       // 14 warps
+constexpr int kConvWarps = 8;        // warps 2..9
+constexpr int kEpiWarp0 = 10;        // warps 10..13
 constexpr int kRowBytes = 48;        // code bytes of one weight row per 128-wide K stage (2 groups x 24 B)
 constexpr int kConv = 16384;         // one matrix's converted stage: 128 rows x 128 e4m3 bytes
-constexpr int kCS = 2;               // converted stages
+constexpr int kCS = 3;               // converted stages
 constexpr int kXP = 2, kHP = 3;      // pieces per x row, per h row
 constexpr int kSmemMax = 227 * 1024;
 
 template <int MODE>
 struct QC;
-// gate/up: A = 128 rows of W1 and of W3, B = x pieces of 32 tokens (64 rows).
+// gate/up: A = 128 rows of W1 and of W3, B = x pieces of 16 tokens (32 rows).
 template <>
 struct QC<GATEUP> {
-  static constexpr int kMats = 2, kPieces = kXP, kStages = 5, kNB = 3;
-  static constexpr int kB = kPieces * kQR * 128;            // 8 KB
+  static constexpr int kMats = 2, kPieces = kXP, kStages = 6, kNB = 3;
+  static constexpr int kB = kPieces * kQR * 128;            // 4 KB
   static constexpr int kW = kMats * 128 * kRowBytes;        // 12 KB
-  static constexpr int kAccCols = kMats * kPieces * kQR;    // 128 tensor-memory columns per group buffer
+  static constexpr int kGroupCols = kMats * kPieces * kQR;  // 64 tensor-memory columns per 64-group
+  static constexpr int kAccCols = 2 * kGroupCols;           // 128 per stage buffer (two groups)
 };
-// down: A = 128 rows of W2, B = h pieces of 32 tokens (96 rows).
+// down: A = 128 rows of W2, B = h pieces of 16 tokens (48 rows).
 template <>
 struct QC<DOWN> {
-  static constexpr int kMats = 1, kPieces = kHP, kStages = 6, kNB = 4;
-  static constexpr int kB = kPieces * kQR * 128;            // 12 KB
+  static constexpr int kMats = 1, kPieces = kHP, kStages = 8, kNB = 4;
+  static constexpr int kB = kPieces * kQR * 128;            // 6 KB
   static constexpr int kW = kMats * 128 * kRowBytes;        // 6 KB
-  static constexpr int kAccCols = kMats * kPieces * kQR;    // 96
+  static constexpr int kGroupCols = kMats * kPieces * kQR;  // 48
+  static constexpr int kAccCols = 2 * kGroupCols;           // 96
 };
 static_assert(QC<GATEUP>::kNB * QC<GATEUP>::kAccCols <= 384 && QC<DOWN>::kNB * QC<DOWN>::kAccCols <= 384,
               "accumulators overlap the scale columns");
@@ -223,15 +231,15 @@ __global__ void __launch_bounds__(256) q3_xquant_kernel(const __nv_bfloat16* __r
   }
 }
 
-// Epilogue of one item (tile x 128 weight rows) for a tile of Z token rows
-// (16 or 32).  Thread = one weight row of the item (lane quarter q, lane).
-// Per 64-group: read the group's accumulators (pieces summed), add
-// s * D + b * A with the row's f16 scale / bias and the tile's activation
-// sums `asm_` ([G][32] in shared memory).  `grp` counts groups over the
-// CTA's items (accumulator buffer grp % kNB).  Returns false on abort.
+// Epilogue of one item (tile x 128 weight rows) for a tile of Z = 16 token
+// rows.  Thread = one weight row of the item (lane quarter q, lane).  Per
+// stage (two 64-groups, one accumulator buffer `stage % kNB`): read each
+// group's accumulators (pieces summed), add s * D + b * A with the row's f16
+// scale / bias and the tile's activation sums `asm_` ([G][16] in shared
+// memory).  `stage` counts stages over the CTA's items.  Returns false on abort.
 template <int MODE, int Z>
 __device__ bool q3_epilogue(const QParams& p, const float* asm_, int tile, int mt, int4 td, int q, int lane, int KC,
-                            uint32_t tb, int& grp, uint64_t* accfull, uint64_t* accempty, volatile int* abort) {
+                            uint32_t tb, int& stage, uint64_t* accfull, uint64_t* accempty, volatile int* abort) {
   using C = QC<MODE>;
   constexpr int NB = C::kNB, MATS = C::kMats;
   if (*abort) return false;
@@ -262,13 +270,13 @@ __device__ bool q3_epilogue(const QParams& p, const float* asm_, int tile, int m
   float acc0[Z], acc1[Z];
 #pragma unroll
   for (int t = 0; t < Z; ++t) acc0[t] = acc1[t] = 0.0f;
-  for (int kc = 0; kc < KC; ++kc) {
+  for (int kc = 0; kc < KC; ++kc, ++stage) {
+    const int a = stage % NB;
+    if (!warp_wait(&accfull[a], (stage / NB) & 1, abort, p.err)) return false;
+    tc5::fence_after();
 #pragma unroll
-    for (int gg = 0; gg < 2; ++gg, ++grp) {
-      const int a = grp % NB;
-      if (!warp_wait(&accfull[a], (grp / NB) & 1, abort, p.err)) return false;
-      tc5::fence_after();
-      const uint32_t dacc = tc5::lane_quarter(tb + a * C::kAccCols, q);
+    for (int gg = 0; gg < 2; ++gg) {
+      const uint32_t dacc = tc5::lane_quarter(tb + a * C::kAccCols + gg * C::kGroupCols, q);
       const float* X = asm_ + (2 * kc + gg) * kQR;
       const float s0 = f16_half(cur[0], gg), b0 = f16_half(cur[1], gg);
       if (MODE == GATEUP) {
@@ -287,22 +295,19 @@ __device__ bool q3_epilogue(const QParams& p, const float* asm_, int tile, int m
           }
         }
       } else {
+        float v[48];
+        tc5::ld_x16_nowait(dacc, *reinterpret_cast<float(*)[16]>(v));
+        tc5::ld_x16_nowait(dacc + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+        tc5::ld_x16_nowait(dacc + 32, *reinterpret_cast<float(*)[16]>(v + 32));
+        tc5::wait_ld();
 #pragma unroll
-        for (int t0 = 0; t0 < Z; t0 += 16) {
-          float v[48];
-          tc5::ld_x16_nowait(dacc + 3 * t0, *reinterpret_cast<float(*)[16]>(v));
-          tc5::ld_x16_nowait(dacc + 3 * t0 + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-          tc5::ld_x16_nowait(dacc + 3 * t0 + 32, *reinterpret_cast<float(*)[16]>(v + 32));
-          tc5::wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            acc0[t0 + j] = fmaf(s0, (v[3 * j] + v[3 * j + 1]) + v[3 * j + 2], fmaf(b0, X[t0 + j], acc0[t0 + j]));
-        }
+        for (int j = 0; j < Z; ++j)
+          acc0[j] = fmaf(s0, (v[3 * j] + v[3 * j + 1]) + v[3 * j + 2], fmaf(b0, X[j], acc0[j]));
       }
-      tc5::fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&accempty[a]);
     }
+    tc5::fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&accempty[a]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       cur[i] = nx1[i];
@@ -396,7 +401,7 @@ __global__ void __launch_bounds__(kQThreads, 1) q3_gemm_kernel(const __grid_cons
       mbar_init(&empty[s], 1);
     }
     for (int c = 0; c < kCS; ++c) {
-      mbar_init(&cfull[c], 4);
+      mbar_init(&cfull[c], kConvWarps);
       mbar_init(&cempty[c], 1);
     }
     for (int b = 0; b < NB; ++b) {
@@ -439,11 +444,18 @@ __global__ void __launch_bounds__(kQThreads, 1) q3_gemm_kernel(const __grid_cons
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Per stage (K = 128, two 64-groups): for each group a fresh accumulator
-    // buffer (grp % NB), two K steps of 32 per matrix.
-    if (lane == 0) {
-      int g = 0, grp = 0;
+    // Per stage (K = 128, two 64-groups): accumulator buffer g % NB, one
+    // fresh accumulator per group and matrix, two K steps of 32 each.  The
+    // whole warp runs the loop (warp-uniform waits and operands); one
+    // elected lane issues.
+    {
+      int g = 0;
       const uint32_t conv0 = smem_u32(conv), b0 = smem_u32(bsm);
+      // descriptors: a K step of 32 advances the start address by 32 B = 2
+      // units of the descriptor's address field (no carry: shared memory
+      // addresses stay below 256 KB)
+      const uint64_t ad_base = tc5::sdesc_sw128(conv0), bd_base = tc5::sdesc_sw128(b0);
+      const uint32_t sfa = tb + kTmemA;
       for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const int N = PC * p.tiles[item / MT].z;
         uint32_t idesc[4];
@@ -451,63 +463,92 @@ __global__ void __launch_bounds__(kQThreads, 1) q3_gemm_kernel(const __grid_cons
         for (int kk = 0; kk < 4; ++kk) idesc[kk] = tc5::idesc_e4m3_e4m3(N, kk);
         for (int kc = 0; kc < KC; ++kc, ++g) {
           const int s = g % S, c = g % kCS;
-          if (!wait_or_abort(&full[s], (g / S) & 1, abort, p.err) ||
-              !wait_or_abort(&cfull[c], (g / kCS) & 1, abort, p.err))
+          if (!warp_wait(&full[s], (g / S) & 1, abort, p.err) || !warp_wait(&cfull[c], (g / kCS) & 1, abort, p.err))
             goto mma_out;
           tc5::fence_after();
-          const uint32_t sb = b0 + s * C::kB;
-          for (int gg = 0; gg < 2; ++gg, ++grp) {
-            const int a = grp % NB;
-            if (grp >= NB) {
-              if (!wait_or_abort(&accempty[a], ((grp / NB) - 1) & 1, abort, p.err)) goto mma_out;
-              tc5::fence_after();
-            }
-            const uint32_t dacc = tb + a * C::kAccCols;
+          const int a = g % NB;
+          if (g >= NB) {
+            if (!warp_wait(&accempty[a], ((g / NB) - 1) & 1, abort, p.err)) goto mma_out;
+            tc5::fence_after();
+          }
+          if (elect_one()) {
+            const uint64_t ad = ad_base + (uint64_t)((c * MATS * kConv) >> 4);
+            const uint64_t bd = bd_base + (uint64_t)((s * C::kB) >> 4);
+            const uint32_t d0 = tb + a * C::kAccCols, sfb = tb + kTmemB + 4 * c;
 #pragma unroll
-            for (int m = 0; m < MATS; ++m)
+            for (int gg = 0; gg < 2; ++gg)
 #pragma unroll
-              for (int ks = 0; ks < 2; ++ks) {
-                const int kk = 2 * gg + ks;
-                tc5::mma_mxf8f6f4(dacc + m * PC * kQR, tc5::sdesc_sw128(conv0 + (c * MATS + m) * kConv + kk * 32),
-                                  tc5::sdesc_sw128(sb + kk * 32), idesc[kk], tb + kTmemA, tb + kTmemB + 4 * c, ks);
-              }
+              for (int m = 0; m < MATS; ++m)
+#pragma unroll
+                for (int ks = 0; ks < 2; ++ks) {
+                  const int kk = 2 * gg + ks;
+                  tc5::mma_mxf8f6f4(d0 + gg * C::kGroupCols + m * PC * kQR, ad + (m * kConv >> 4) + 2 * kk,
+                                    bd + 2 * kk, idesc[kk], sfa, sfb, ks);
+                }
             tc5::commit(&accfull[a]);
           }
-          tc5::commit(&empty[s]);
-          tc5::commit(&cempty[c]);
+          __syncwarp();
+          if (elect_one()) {
+            tc5::commit(&empty[s]);
+            tc5::commit(&cempty[c]);
+          }
+          __syncwarp();
         }
       }
     mma_out:
       // all issued MMAs complete before the tensor memory is released
-      tc5::commit(&done);
-      mbar_wait_bounded(&done, 0, 1000000000ull);
+      if (elect_one()) {
+        tc5::commit(&done);
+        mbar_wait_bounded(&done, 0, 1000000000ull);
+      }
+      __syncwarp();
     }
-  } else if (warp < 6) {
+  } else if (warp < kEpiWarp0) {
     // ------------------------------------------------------------ converters
+    // warp 2 + cw: rows (cw % 4) * 32 + lane of the 128-row tile; gate/up:
+    // matrix cw / 4 (W1, W3); down: group cw / 4 of the stage (chunks 4 part
+    // .. 4 part + 3).  Warps 2-5 (one per lane quarter) also write the scale
+    // atoms into tensor memory.
+    const int cw = warp - 2, part = cw >> 2;
     const int q = warp & 3;
-    const int r = q * 32 + lane;   // weight row of the 128-row tile
-    tc5::st_x4(tc5::lane_quarter(tb + kTmemA, q), 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
-    tc5::wait_st();
+    const int r = (cw & 3) * 32 + lane;
+    const bool stager = cw < 4;
+    if (stager) {
+      tc5::st_x4(tc5::lane_quarter(tb + kTmemA, q), 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+      tc5::wait_st();
+    }
     int g = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       for (int kc = 0; kc < KC; ++kc, ++g) {
         const int s = g % S, c = g % kCS;
         if (!warp_wait(&full[s], (g / S) & 1, abort, p.err)) goto cv_out;
         if (g >= kCS && !warp_wait(&cempty[c], ((g / kCS) - 1) & 1, abort, p.err)) goto cv_out;
-#pragma unroll
-        for (int m = 0; m < MATS; ++m) {
+        {
+          const int m = MATS > 1 ? part : 0;
           const uint4* src = reinterpret_cast<const uint4*>(wsm + s * C::kW + (m * 128 + r) * kRowBytes);
-          const uint4 u0 = src[0], u1 = src[1], u2 = src[2];
-          const uint32_t wd[12] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w, u2.x, u2.y, u2.z, u2.w};
           uint8_t* dst = conv + (c * MATS + m) * kConv + r * 128;
+          if (MATS > 1) {   // the whole row: both groups
+            const uint4 u0 = src[0], u1 = src[1], u2 = src[2];
+            const uint32_t wd[12] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w, u2.x, u2.y, u2.z, u2.w};
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {   // 16 codes each: group ch / 4, low word ch % 4
-            const int gg = ch >> 2, w = ch & 3;
-            const uint32_t Hh = wd[gg * 6 + 4 + (w >> 1)] >> (8 * (w & 1));
-            *reinterpret_cast<uint4*>(dst + ((ch ^ (r & 7)) << 4)) = codes16_to_e4m3(wd[gg * 6 + w], Hh);
+            for (int ch = 0; ch < 8; ++ch) {   // 16 codes each: group ch / 4, low word ch % 4
+              const int gg = ch >> 2, w = ch & 3;
+              const uint32_t Hh = wd[gg * 6 + 4 + (w >> 1)] >> (8 * (w & 1));
+              *reinterpret_cast<uint4*>(dst + ((ch ^ (r & 7)) << 4)) = codes16_to_e4m3(wd[gg * 6 + w], Hh);
+            }
+          } else {          // one group of the row: six words at byte 24 * part
+            const uint2* s2 = reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(src) + 24 * part);
+            const uint2 a0 = s2[0], a1 = s2[1], a2 = s2[2];
+            const uint32_t wd[6] = {a0.x, a0.y, a1.x, a1.y, a2.x, a2.y};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const int ch = 4 * part + w;
+              const uint32_t Hh = wd[4 + (w >> 1)] >> (8 * (w & 1));
+              *reinterpret_cast<uint4*>(dst + ((ch ^ (r & 7)) << 4)) = codes16_to_e4m3(wd[w], Hh);
+            }
           }
         }
-        {
+        if (stager) {
           const uint4 v = reinterpret_cast<const uint4*>(sfs + s * kSfAtom)[lane];
           tc5::st_x4(tc5::lane_quarter(tb + kTmemB + 4 * c, q), v.x, v.y, v.z, v.w);
           tc5::wait_st();
@@ -522,8 +563,8 @@ __global__ void __launch_bounds__(kQThreads, 1) q3_gemm_kernel(const __grid_cons
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int et = threadIdx.x - 6 * 32;   // 0..127
-    int grp = 0, li = 0;
+    const int et = threadIdx.x - kEpiWarp0 * 32;   // 0..127
+    int stage = 0, li = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
       const int tile = item / MT, mt = item % MT;
       const int4 td = p.tiles[tile];
@@ -534,7 +575,7 @@ __global__ void __launch_bounds__(kQThreads, 1) q3_gemm_kernel(const __grid_cons
         const float4* src = reinterpret_cast<const float4*>(p.asum + (size_t)tile * G * kQR);
         for (int i = et; i < G * kQR / 4; i += 128) reinterpret_cast<float4*>(sm)[i] = src[i];
       } else {
-        const float* src = p.asum + (size_t)tile * (2 * G) * kQR;   // 32-row sums of h
+        const float* src = p.asum + (size_t)tile * (2 * G) * kQR;   // 32-row block sums of h
         for (int i = et; i < G * kQR; i += 128) {
           const int gq = i / kQR, t = i % kQR;
           sm[i] = src[(2 * gq) * kQR + t] + src[(2 * gq + 1) * kQR + t];
@@ -543,10 +584,7 @@ __global__ void __launch_bounds__(kQThreads, 1) q3_gemm_kernel(const __grid_cons
       bar_sync(1, 128);
       // after an abort every item returns at once, but the loop goes on so
       // that the four warps meet the same number of item barriers
-      if (td.z <= 16)
-        q3_epilogue<MODE, 16>(p, sm, tile, mt, td, q, lane, KC, tb, grp, accfull, accempty, abort);
-      else
-        q3_epilogue<MODE, 32>(p, sm, tile, mt, td, q, lane, KC, tb, grp, accfull, accempty, abort);
+      q3_epilogue<MODE, kQR>(p, sm, tile, mt, td, q, lane, KC, tb, stage, accfull, accempty, abort);
     }
   }
   tc5::fence_before();
@@ -627,7 +665,8 @@ int q3_validate(const DsMoeDesc* d) {
   DS_REQUIRE((int64_t)E * I < ((int64_t)1 << 31) && (int64_t)E * H < ((int64_t)1 << 31), DS_EINVAL,
              "grouped_ffn: bank too large");
   DS_REQUIRE(q3_smem<GATEUP>(H) <= (size_t)kSmemMax && q3_smem<DOWN>(I) <= (size_t)kSmemMax, DS_ENOTSUP,
-             "grouped_ffn: q3 banks need hidden and inter <= %d", (int)((kSmemMax - q3_smem<GATEUP>(0)) / 8));
+             "grouped_ffn: q3 banks need hidden <= %d and inter <= %d", (int)((kSmemMax - q3_smem<GATEUP>(0)) / 2),
+             (int)((kSmemMax - q3_smem<DOWN>(0)) / 2));
   return DS_OK;
 }
 

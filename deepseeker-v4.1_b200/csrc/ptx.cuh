@@ -45,6 +45,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase (no suspension, little fixed cost): the fast
+// path of the waits below when the phase is usually complete already.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // try_wait that lets the hardware suspend the thread for up to `hint_ns`
 // (it resumes as soon as the phase completes), so waiting warps do not
 // compete for issue slots with the warps doing the work.
@@ -58,6 +72,20 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
       : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
+}
+
+// True in exactly one lane of the (fully active) warp.  Code that issues
+// tcgen05 instructions from the whole warp with the issue guarded by this
+// keeps warp-uniform operands (descriptors, tensor-memory addresses) in
+// uniform registers.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, 0xffffffff;\n\t"
+      "@px mov.s32 %0, 1;\n\t}"
+      : "+r"(pred));
+  return pred != 0;
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

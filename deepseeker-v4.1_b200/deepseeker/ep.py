@@ -147,24 +147,41 @@ def gpu_local_ffn(local_layer) -> LocalFFN:
     return run
 
 
+def shared_dense(w1: torch.Tensor, w3: torch.Tensor, w2: torch.Tensor, x: torch.Tensor,
+                 limit: float = 10.0) -> torch.Tensor:
+    """Shared expert for a batch of rows as plain bf16 GEMMs (cuBLAS, f32
+    output): g = min(x W1^T, L), u = clip(x W3^T, +-L), h = silu(g) u in f32,
+    then h W2^T with h split into bf16 hi + lo (16 significant bits), so the
+    weights stream once for the whole batch.  Returns f32 [b, H], rounded to
+    x's dtype first as the reference does (mlx_runner.py:776-781)."""
+    xb = x.to(torch.bfloat16)
+    g = torch.mm(xb, w1.t(), out_dtype=torch.float32).clamp_(max=limit)
+    u = torch.mm(xb, w3.t(), out_dtype=torch.float32).clamp_(-limit, limit)
+    h = g / (1.0 + torch.exp(-g)) * u
+    hi = h.to(torch.bfloat16)
+    lo = (h - hi.float()).to(torch.bfloat16)
+    y = torch.mm(hi, w2.t(), out_dtype=torch.float32) + torch.mm(lo, w2.t(), out_dtype=torch.float32)
+    return y.to(x.dtype).float()
+
+
 def gpu_shared_fn(local_layer) -> SharedFn | None:
-    """Shared expert on the decode kernels (no routed slot), f32 math, output
-    rounded to the activation dtype before it is added (reference order)."""
+    """Shared expert: up to 8 rows on the fused decode kernels (no routed
+    slot); more rows as one set of bf16 GEMMs (``shared_dense``), so the
+    shared weights stream once per call, not once per 8 rows.  f32 math,
+    output rounded to the activation dtype before it is added."""
     from . import moe
 
     if local_layer.shared_w1 is None:
         return None
+    w1, w3, w2 = local_layer.shared_w1, local_layer.shared_w3, local_layer.shared_w2
 
     def run(x):
         b, H = x.shape
-        out = torch.empty(b, H, dtype=torch.float32, device=x.device)
-        for t0 in range(0, b, moe.MAX_DECODE_TOKENS):
-            t1 = min(b, t0 + moe.MAX_DECODE_TOKENS)
-            n = t1 - t0
-            ids = torch.full((n, 1), -1, dtype=torch.int32, device=x.device)
-            w = torch.zeros(n, 1, dtype=torch.float32, device=x.device)
-            out[t0:t1] = moe.moe_decode(x[t0:t1].float().contiguous(), local_layer, ids, w)
-        return out.to(x.dtype).float()
+        if b > moe.MAX_DECODE_TOKENS:
+            return shared_dense(w1, w3, w2, x)
+        ids = torch.full((b, 1), -1, dtype=torch.int32, device=x.device)
+        w = torch.zeros(b, 1, dtype=torch.float32, device=x.device)
+        return moe.moe_decode(x.float().contiguous(), local_layer, ids, w).to(x.dtype).float()
     return run
 
 

@@ -33,6 +33,42 @@ def test_ep_single_rank_matches_decode(cuda):
     assert rel_l2(out, ref) <= 1e-3
 
 
+@pytest.mark.parametrize("fmt", ["fp4", "q3"])
+def test_ep_single_rank_batch_above_8_vs_oracle(fmt, cuda):
+    """b = 16 and 64 rows (config 5's batches): routed experts on the grouped
+    kernels (FP4 or q3 banks), the shared expert as bf16 GEMMs over the whole
+    batch; against the CPU oracle (dequant + moe_combine)."""
+    import numpy as np
+
+    from deepseeker import ep, metal_fp4, synthetic
+    from oracle import moe as omoe
+    from oracle import q3 as oq3
+
+    H, I, E, K, Is = 512, 256, 16, 4, 384
+    layer = synthetic.make_layer(fmt, H, I, E, seed=3, shared_inter=Is, std=0.05, device=cuda)
+    lay = ep.gpu_layer(layer, E, K)
+
+    def ew(e):
+        out = []
+        for b in (layer.w1, layer.w3, layer.w2):
+            if b.fmt == 0:
+                out.append(metal_fp4.dequant(b.data[e], b.scales[e]).view(b.rows, b.cols).cpu())
+            else:
+                out.append(torch.from_numpy(oq3.dequant(b.data[e].cpu().numpy().view(np.uint32),
+                                                        b.scales[e].cpu().numpy(), b.biases[e].cpu().numpy())))
+        return tuple(out)
+    shared = (layer.shared_w1.cpu(), layer.shared_w3.cpu(), layer.shared_w2.cpu())
+    for b in (16, 64):
+        g = torch.Generator().manual_seed(b)
+        x = torch.randn(b, H, generator=g).to(torch.bfloat16)
+        w, ids = omoe.route_softmax_topk(torch.randn(b, E, generator=g), K)
+        ids = ids.to(torch.int32)
+        out = lay(x.to(cuda), ids.to(cuda), w.float().to(cuda))
+        ref = omoe.moe_combine(x, ids.long(), w.float(), ew, shared=shared, limit=10.0)
+        assert out.dtype == torch.bfloat16
+        assert rel_l2(out, ref) <= 1e-3, (b, rel_l2(out, ref))
+
+
 def test_ep_decode_scheme_single_rank_matches_decode(cuda):
     from deepseeker import ep, moe
 
