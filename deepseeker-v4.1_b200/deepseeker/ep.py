@@ -15,11 +15,16 @@ Rank g owns global experts [g * E_l, (g + 1) * E_l), E_l = E / G; the shared
 expert is replicated.  One layer step for the b tokens a rank holds (its
 "home" tokens):
 
-  1. dispatch: every (token, slot) pair with expert e goes to rank e // E_l.
-     Each rank sends a fixed-capacity block of b * k rows to every peer
-     (unused rows carry expert -1), so the exchange needs no host sync and is
-     one all_to_all_single of 32-bit words: the activation row followed by
-     (local expert id, route weight).
+  1. dispatch: every (token, slot) pair with expert e goes to rank e // E_l,
+     as 32-bit words: the activation row followed by (local expert id, route
+     weight).  Two forms: counted -- the ranks first exchange how many rows
+     each sends to each (one all_to_all of G counts, read on the host), then
+     send exactly those rows with one uneven all_to_all_single; fixed
+     capacity -- a block of b * k rows to every peer (unused rows carry
+     expert -1), nothing read on the host, so the host queues the next
+     layers while the GPU works (and a step could be captured in a CUDA
+     graph), at up to G times the exchanged bytes.  ``fixed_capacity=None``
+     (default) picks fixed capacity while G * b * k <= 1024 rows.
   2. experts: the owner runs its local experts over the received rows -- route
      weight applied before the down projection, SwiGLU clamp -- producing f32
      rows (GPU: ds_grouped_ffn with top_k = 1, rows of expert -1 skipped).
@@ -40,6 +45,9 @@ from typing import Callable
 import torch
 import torch.distributed as dist
 
+# the fixed-capacity exchange is used up to this many rows (G * b * k) when not chosen explicitly
+FIXED_CAPACITY_ROWS = 1024
+
 # local_ffn(x_rows [R, H] (activation dtype), expert [R] int32 (-1 = none), gate [R] f32) -> f32 [R, H]
 LocalFFN = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 # shared_fn(x [b, H]) -> f32 [b, H], already rounded to the activation dtype
@@ -48,7 +56,8 @@ SharedFn = Callable[[torch.Tensor], torch.Tensor]
 
 class ExpertParallelMoE:
     def __init__(self, n_experts: int, top_k: int, local_ffn: LocalFFN, shared_fn: SharedFn | None = None,
-                 group: dist.ProcessGroup | None = None):
+                 group: dist.ProcessGroup | None = None, fixed_capacity: bool | None = None):
+        self.fixed_capacity = fixed_capacity
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -76,23 +85,81 @@ class ExpertParallelMoE:
         gate = buf[:, n + 1].contiguous().view(torch.float32)
         return x[:, :H], expert, gate
 
-    def _all_to_all(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+    def _all_to_all(self, out: torch.Tensor, inp: torch.Tensor, out_splits=None, in_splits=None) -> None:
         if self.world == 1:
             out.copy_(inp)
         else:
-            dist.all_to_all_single(out, inp, group=self.group)
+            dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
+                                   group=self.group)
 
     def dispatch_plan(self, ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """(dest rank, slot index inside the block for that rank, valid) per pair, [b*k] each."""
         flat = ids.reshape(-1).to(torch.int64)
         valid = flat >= 0
         dest = torch.where(valid, flat // self.local_experts, torch.zeros_like(flat))
-        onehot = torch.nn.functional.one_hot(dest, self.world) * valid[:, None]
+        onehot = torch.zeros(flat.shape[0], self.world, dtype=torch.int64, device=ids.device)
+        onehot.scatter_(1, dest[:, None], valid[:, None].to(torch.int64))   # no host-side bounds check
         index = (torch.cumsum(onehot, dim=0) - 1).gather(1, dest[:, None]).view(-1)
         return dest, index, valid
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor, gates: torch.Tensor) -> torch.Tensor:
         """x [b, H], ids [b, k] global expert ids (-1 = dropped slot), gates [b, k] -> [b, H] of x.dtype."""
+        if (x.shape[1] * x.element_size()) % 4:
+            raise ValueError("rows must be a whole number of 32-bit words")
+        fixed = self.fixed_capacity
+        if fixed is None:
+            fixed = self.world * ids.numel() <= FIXED_CAPACITY_ROWS
+        return self._forward_fixed(x, ids, gates) if fixed else self._forward_counted(x, ids, gates)
+
+    @staticmethod
+    def _combine(back: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+        """Each token's k contributions (rows of `back`, src [b, k]) summed in slot order."""
+        acc = back[src[:, 0]]
+        for s_ in range(1, src.shape[1]):
+            acc = acc + back[src[:, s_]]
+        return acc
+
+    def _forward_counted(self, x: torch.Tensor, ids: torch.Tensor, gates: torch.Tensor) -> torch.Tensor:
+        """Exact-size exchange: counts first, then only the routed rows."""
+        b, H = x.shape
+        k = ids.shape[1]
+        G = self.world
+        flat = ids.reshape(-1).to(torch.int64)
+        valid = flat >= 0
+        dest = torch.where(valid, flat // self.local_experts, torch.full_like(flat, G))   # G: dropped
+        order = torch.sort(dest, stable=True).indices          # pairs grouped by owner, pair order kept
+        counts = torch.bincount(dest, minlength=G + 1)[:G]
+        recv_counts = torch.empty_like(counts)
+        self._all_to_all(recv_counts, counts)
+        host = torch.cat([counts, recv_counts]).cpu().tolist()   # the one host read of the step
+        send_c, recv_c = host[:G], host[G:]
+        n_send, n_recv = sum(send_c), sum(recv_c)
+        sel = order[:n_send]
+        token = sel // k
+        rows = self._pack(x[token], flat[sel] - dest[sel] * self.local_experts, gates.reshape(-1)[sel])
+        words = rows.shape[1]
+        recv = torch.empty(n_recv, words, dtype=torch.int32, device=x.device)
+        self._all_to_all(recv, rows, recv_c, send_c)
+        if n_recv:
+            rx, rexp, rgate = self._unpack(recv, x.dtype, H)
+            y = self.local_ffn(rx, rexp, rgate)
+            if y.dtype != torch.float32 or y.shape != (n_recv, H):
+                raise ValueError("local_ffn must return f32 [rows, H]")
+        else:
+            y = torch.empty(0, H, dtype=torch.float32, device=x.device)
+        back = torch.empty(n_send + 1, H, dtype=torch.float32, device=x.device)
+        back[n_send].zero_()
+        self._all_to_all(back[:n_send], y.contiguous(), send_c, recv_c)
+        # pair -> its row in send order (dropped pairs -> the zero row), then
+        # each token's k contributions in slot order
+        src = torch.full((b * k,), n_send, dtype=torch.int64, device=x.device)
+        src[sel] = torch.arange(n_send, device=x.device)
+        acc = self._combine(back, src.view(b, k))
+        if self.shared_fn is not None:
+            acc = acc + self.shared_fn(x)
+        return acc.to(x.dtype)
+
+    def _forward_fixed(self, x: torch.Tensor, ids: torch.Tensor, gates: torch.Tensor) -> torch.Tensor:
         b, H = x.shape
         k = ids.shape[1]
         cap = b * k
@@ -100,15 +167,15 @@ class ExpertParallelMoE:
         dest, index, valid = self.dispatch_plan(ids)
         flat = ids.reshape(-1).to(torch.int64)
         token = torch.arange(cap, device=x.device) // k
-        # 1. dispatch
-        if (H * x.element_size()) % 4:
-            raise ValueError("rows must be a whole number of 32-bit words")
+        # 1. dispatch (no host read: every pair is written, dropped ones to a
+        # spare row past the blocks)
         words = H * x.element_size() // 4
-        send = torch.zeros(G * cap, words + 2, dtype=torch.int32, device=x.device)
+        send = torch.zeros(G * cap + 1, words + 2, dtype=torch.int32, device=x.device)
         send[:, words] = -1  # expert -1: unused row
-        slot = dest * cap + index
-        rows = self._pack(x[token[valid]], flat[valid] - dest[valid] * self.local_experts, gates.reshape(-1)[valid])
-        send[slot[valid]] = rows
+        slot = torch.where(valid, dest * cap + index, torch.full_like(dest, G * cap))
+        send[slot] = self._pack(x[token], torch.where(valid, flat - dest * self.local_experts, -1),
+                                gates.reshape(-1))
+        send = send[:G * cap]
         recv = torch.empty_like(send)
         self._all_to_all(recv, send)
         # 2. local experts
@@ -116,14 +183,11 @@ class ExpertParallelMoE:
         y = self.local_ffn(rx, rexp, rgate)
         if y.dtype != torch.float32 or y.shape != (G * cap, H):
             raise ValueError("local_ffn must return f32 [rows, H]")
-        back = torch.empty_like(y)
-        self._all_to_all(back, y.contiguous())
+        back = torch.empty(G * cap + 1, H, dtype=torch.float32, device=x.device)
+        back[G * cap].zero_()
+        self._all_to_all(back[:G * cap], y.contiguous())
         # 3. combine in slot order (+ shared), cast
-        back = torch.cat([back, torch.zeros(1, H, dtype=back.dtype, device=back.device)])
-        src = torch.where(valid, slot, torch.full_like(slot, G * cap)).view(b, k)
-        acc = back[src[:, 0]]
-        for s in range(1, k):
-            acc = acc + back[src[:, s]]
+        acc = self._combine(back, slot.view(b, k))
         if self.shared_fn is not None:
             acc = acc + self.shared_fn(x)
         return acc.to(x.dtype)

@@ -35,7 +35,7 @@ def cpu_problem(seed: int = 0):
     return w1, w3, w2, sh, x, ids, (w / w.sum(-1, keepdim=True)).float()
 
 
-def cpu_ep(world: int, rank: int, seed: int = 0):
+def cpu_ep(world: int, rank: int, seed: int = 0, fixed_capacity: bool = False):
     """ExpertParallelMoE with row-by-row f32 experts (batch-independent results)."""
     from deepseeker.ep import ExpertParallelMoE
     from oracle import moe as omoe
@@ -57,7 +57,7 @@ def cpu_ep(world: int, rank: int, seed: int = 0):
     def shared_fn(xx):
         return omoe.shared_expert(xx.float(), *sh, limit=LIMIT).to(xx.dtype).float()
 
-    return ExpertParallelMoE(E, K, local_ffn, shared_fn), x, ids, w
+    return ExpertParallelMoE(E, K, local_ffn, shared_fn, fixed_capacity=fixed_capacity), x, ids, w
 
 
 def cpu_ep_decode(world: int, rank: int, seed: int = 0):
@@ -96,7 +96,8 @@ def rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
                 q.put((rank, "left"))           # leaves between steps: never joins the exchange
                 dist.destroy_process_group()
                 return
-            ep, x, ids, w = cpu_ep_decode(world, rank) if mode == "cpu_decode" else cpu_ep(world, rank)
+            ep, x, ids, w = (cpu_ep_decode(world, rank) if mode == "cpu_decode" else
+                             cpu_ep(world, rank, fixed_capacity=(mode == "cpu_fixed")))
             try:
                 out = ep(x, ids, w)
             except RuntimeError as e:

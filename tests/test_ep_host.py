@@ -46,7 +46,7 @@ def spawn(world: int, mode: str, timeout: float = 120.0) -> dict:
 def test_dispatch_plan_blocks():
     from deepseeker.ep import ExpertParallelMoE
 
-    ep = ExpertParallelMoE(8, 3, lambda *a: None)
+    ep = ExpertParallelMoE(8, 3, lambda *a: None, fixed_capacity=True)
     ep.world, ep.local_experts = 2, 4
     ids = torch.tensor([[0, 5, 3], [7, -1, 1]])
     dest, index, valid = ep.dispatch_plan(ids)
@@ -71,6 +71,19 @@ def test_two_ranks_equal_one_rank_bitwise():
     ep1, x, ids, w = ep_worker.cpu_ep(1, 0)
     single = ep1(x, ids, w)
     res = spawn(2, "cpu")
+    for r in (0, 1):
+        assert isinstance(res[r], torch.Tensor), res[r]
+        assert torch.equal(res[r], single), f"rank {r} differs"
+
+
+def test_two_ranks_fixed_capacity_equal_one_rank_bitwise():
+    """The fixed-capacity exchange (no host read, graph-capturable) gives the
+    same bits as the counted one."""
+    ep1, x, ids, w = ep_worker.cpu_ep(1, 0)
+    single = ep1(x, ids, w)
+    ep1f = ep_worker.cpu_ep(1, 0, fixed_capacity=True)[0]
+    assert torch.equal(ep1f(x, ids, w), single)
+    res = spawn(2, "cpu_fixed")
     for r in (0, 1):
         assert isinstance(res[r], torch.Tensor), res[r]
         assert torch.equal(res[r], single), f"rank {r} differs"
