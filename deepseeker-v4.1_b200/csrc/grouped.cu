@@ -233,47 +233,61 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop (warp-uniform waits and operands); one
+    // elected lane issues.  Descriptors are formed once: a K step of 32
+    // advances a start address by 32 B = 2 units of the descriptor's
+    // address field (shared memory addresses stay below 256 KB: no carry).
+    {
       int g = 0, li = 0;
+      const uint64_t ops_desc = tc5::sdesc_sw128(smem_u32(ops));
       for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
         const int tile = item / MT;
         const int N = p.tiles[tile].z;
+        uint32_t idesc[4];
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) idesc[sub] = tc5::idesc_e2m1_e4m3(N, sub);
         const int b = li & 1;
-        if (li >= 2 && !wait_or_abort(&accempty[b], ((li >> 1) - 1) & 1, abort, p.err)) break;
+        if (li >= 2 && !warp_wait(&accempty[b], ((li >> 1) - 1) & 1, abort, p.err)) break;
         tc5::fence_after();
         const uint32_t dacc = tb + b * C::kAcc;
         for (int kc = 0; kc < KC; ++kc, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          if (!wait_or_abort(&full[s], ph, abort, p.err) || !wait_or_abort(&sfready[s], ph, abort, p.err))
-            goto mma_out;
+          if (!warp_wait(&full[s], ph, abort, p.err) || !warp_wait(&sfready[s], ph, abort, p.err)) goto mma_out;
           tc5::fence_after();
-          const uint32_t sa = smem_u32(ops + s * C::kStage), sb = sa + C::kAStage;
-          const uint32_t tsf = tsf0 + s * 16;
+          if (elect_one()) {
+            const uint64_t ad = ops_desc + (uint64_t)((s * C::kStage) >> 4);
+            const uint64_t bd = ad + (uint64_t)(C::kAStage >> 4);
+            const uint32_t tsf = tsf0 + s * 16;
 #pragma unroll
-          for (int sub = 0; sub < 4; ++sub) {
-            const uint32_t idesc = tc5::idesc_e2m1_e4m3(N, sub);
+            for (int sub = 0; sub < 4; ++sub) {
 #pragma unroll
-            for (int pc = 0; pc < C::kPieces; ++pc) {
-              const uint64_t bd = tc5::sdesc_sw128(sb + pc * C::kBPiece + sub * 32);
-              const uint32_t acc = (kc | sub | pc) != 0;
-              if (MODE == GATEUP) {
-                tc5::mma_mxf8f6f4(dacc, tc5::sdesc_sw128(sa + sub * 32), bd, idesc, tsf, tsf + 8 + 4 * pc, acc);
-                tc5::mma_mxf8f6f4(dacc + kTileRows, tc5::sdesc_sw128(sa + 16384 + sub * 32), bd, idesc, tsf + 4,
-                                  tsf + 8 + 4 * pc, acc);
-              } else {
-                tc5::mma_mxf8f6f4(dacc, tc5::sdesc_sw128(sa + sub * 32), bd, idesc, tsf, tsf + 4 + 4 * pc, acc);
+              for (int pc = 0; pc < C::kPieces; ++pc) {
+                const uint64_t bdp = bd + (uint64_t)((pc * C::kBPiece) >> 4) + 2 * sub;
+                const uint32_t acc = (kc | sub | pc) != 0;
+                if (MODE == GATEUP) {
+                  tc5::mma_mxf8f6f4(dacc, ad + 2 * sub, bdp, idesc[sub], tsf, tsf + 8 + 4 * pc, acc);
+                  tc5::mma_mxf8f6f4(dacc + kTileRows, ad + (16384 >> 4) + 2 * sub, bdp, idesc[sub], tsf + 4,
+                                    tsf + 8 + 4 * pc, acc);
+                } else {
+                  tc5::mma_mxf8f6f4(dacc, ad + 2 * sub, bdp, idesc[sub], tsf, tsf + 4 + 4 * pc, acc);
+                }
               }
             }
+            tc5::commit(&empty[s]);
           }
-          tc5::commit(&empty[s]);
+          __syncwarp();
         }
-        tc5::commit(&accfull[b]);
+        if (elect_one()) tc5::commit(&accfull[b]);
+        __syncwarp();
       }
     mma_out:
       // all issued MMAs complete before the tensor memory is released
-      tc5::commit(&done);
-      mbar_wait_bounded(&done, 0, 1000000000ull);
+      if (elect_one()) {
+        tc5::commit(&done);
+        mbar_wait_bounded(&done, 0, 1000000000ull);
+      }
+      __syncwarp();
     }
   } else if (warp < kEpiWarp0) {
     // ------------------------------------------------------------ scale staging

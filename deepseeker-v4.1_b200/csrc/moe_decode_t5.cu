@@ -452,16 +452,19 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
     // thread starts waiting on stage g only after it has seen stage g - 3
     // staged (its previous item), and the stagers stage in ring order, so
     // with S >= 3 the slot's previous phase (stage g - S) has completed and
-    // the parity wait cannot alias.
-    if (lane == 0) {
+    // the parity wait cannot alias.  Each issuer warp runs its loop
+    // warp-uniformly and one elected lane issues, with the descriptors
+    // formed once per stage: a K step of 32 B adds 2 to the descriptor's
+    // 16-byte address field (shared memory stays below 256 KB: no carry).
+    {
       const int par = warp == 1 ? 0 : 1;
       int li = 0;
-      const uint32_t ring0 = smem_u32(ring);
+      const uint64_t ring_desc = tc5::sdesc_sw128(smem_u32(ring));
       const uint32_t idesc_sh = tc5::idesc_bf16(16);
       uint32_t idesc_r[2];
       idesc_r[0] = tc5::idesc_mxf4(p.N_r, 0);
       idesc_r[1] = tc5::idesc_mxf4(p.N_r, 2);
-      const uint32_t bchunk = (uint32_t)p.N_r * 128;
+      const uint32_t bchunk16 = ((uint32_t)p.N_r * 128) >> 4;
       for (int item = blockIdx.x;; item += gridDim.x, ++li) {
         if (item >= n_items) {
           know_routed();
@@ -470,38 +473,45 @@ __global__ void __launch_bounds__(kThreads, 1) t5_gemm_kernel(const __grid_const
         if ((li & 1) != par) continue;
         const bool shared = item < p.n_sh_items;
         const int b = li % kAcc;
-        if (li >= kAcc && !wait_or_abort(&accempty[b], ((li / kAcc) - 1) & 1, abort, p.err)) break;
+        if (li >= kAcc && !warp_wait(&accempty[b], ((li / kAcc) - 1) & 1, abort, p.err)) break;
         const uint32_t dacc = tb + b * 64;
         for (int j = 0; j < kStagesPerItem; ++j) {
           const int g = li * kStagesPerItem + j, s = g % S, ph = (g / S) & 1;
-          if (!wait_or_abort(&staged[s], ph, abort, p.err)) goto mma_out;
+          if (!warp_wait(&staged[s], ph, abort, p.err)) goto mma_out;
           tc5::fence_after();
-          const uint32_t sa = ring0 + s * p.stage_bytes, sb = sa + kASlot;
-          const uint32_t tsf = tsf0 + s * 32;
-          if (shared) {
+          if (elect_one()) {
+            const uint64_t ad = ring_desc + (uint64_t)(((uint32_t)s * p.stage_bytes) >> 4);
+            const uint64_t bd = ad + (uint64_t)(kASlot >> 4);
+            const uint32_t tsf = tsf0 + s * 32;
+            if (shared) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+              for (int c = 0; c < 2; ++c)
 #pragma unroll
-              for (int sub = 0; sub < 4; ++sub)
-                tc5::mma_bf16(dacc, tc5::sdesc_sw128(sa + c * 16384 + sub * 32),
-                              tc5::sdesc_sw128(sb + c * 16 * 128 + sub * 32), idesc_sh, (j | c | sub) != 0);
-          } else {
-            // each 128-byte row chunk = 256 codes = 4 MMAs of K = 64; scale word 2c + kk/2, byte pair kk%2
+                for (int sub = 0; sub < 4; ++sub)
+                  tc5::mma_bf16(dacc, ad + (c * 16384 >> 4) + 2 * sub, bd + (c * 16 * 128 >> 4) + 2 * sub, idesc_sh,
+                                (j | c | sub) != 0);
+            } else {
+              // each 128-byte row chunk = 256 codes = 4 MMAs of K = 64; scale word 2c + kk/2, byte pair kk%2
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+              for (int c = 0; c < 2; ++c)
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                tc5::mma_mxf4(dacc, tc5::sdesc_sw128(sa + c * 16384 + kk * 32),
-                              tc5::sdesc_sw128(sb + c * bchunk + kk * 32), idesc_r[kk & 1],
-                              tsf + 4 * (2 * c + (kk >> 1)), tsf + 16 + 4 * (2 * c + (kk >> 1)), (j | c | kk) != 0);
+                for (int kk = 0; kk < 4; ++kk)
+                  tc5::mma_mxf4(dacc, ad + (c * 16384 >> 4) + 2 * kk, bd + c * bchunk16 + 2 * kk, idesc_r[kk & 1],
+                                tsf + 4 * (2 * c + (kk >> 1)), tsf + 16 + 4 * (2 * c + (kk >> 1)), (j | c | kk) != 0);
+            }
+            tc5::commit(&empty[s]);
           }
-          tc5::commit(&empty[s]);
+          __syncwarp();
         }
-        tc5::commit(&accfull[b]);
+        if (elect_one()) tc5::commit(&accfull[b]);
+        __syncwarp();
       }
     mma_out:
-      tc5::commit(&done[par]);
-      mbar_wait_bounded(&done[par], 0, 1000000000ull);
+      if (elect_one()) {
+        tc5::commit(&done[par]);
+        mbar_wait_bounded(&done[par], 0, 1000000000ull);
+      }
+      __syncwarp();
     }
   } else if (warp < 6) {
     // ---------------------------------------------------------------- stagers
