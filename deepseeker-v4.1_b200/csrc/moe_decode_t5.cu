@@ -233,7 +233,19 @@ __device__ void tail_h_routed(const T5Params& p, int slot, int r0, int lane) {
   uint8_t* sf = p.sfh + ((size_t)slot * (I / 128) + r0 / 128) * kAtom;
 #pragma unroll 1
   for (int t = 0; t < kT; ++t) {
-    float r = silu_glu(g[t], u[t], p.limit) * p.slot_gate[slot * kMaxT + t];
+    const float gate = p.slot_gate[slot * kMaxT + t];   // uniform over the warp
+    if (gate == 0.0f) {
+      // a token not routed to this slot: h = 0 exactly, i.e. zero codes in
+      // every piece and the scale byte e2m1_scale(0) = 127
+#pragma unroll 1
+      for (int pc = 0; pc < kPieces; ++pc) {
+        const int row = t * kPieces + pc;
+        if ((lane & 1) == 0) hq[(size_t)row * (I / 2) + i / 2] = 0;
+        if (lane == 0) sf[atom_off(row, (r0 & 127) >> 5)] = (uint8_t)127;
+      }
+      continue;
+    }
+    float r = silu_glu(g[t], u[t], p.limit) * gate;
 #pragma unroll 1
     for (int pc = 0; pc < kPieces; ++pc) {
       float am = fabsf(r);
@@ -649,9 +661,12 @@ __global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
   launch_dependents();
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
   if (blockIdx.x == 0 && threadIdx.x < 32) {
-    // distinct valid experts, ascending; one warp, at most 128 entries
+    // distinct valid experts, ascending; one warp, at most 128 entries.
+    // ids and gates go to shared memory first (independent loads), so the
+    // loops below wait on no global load
     const int lane = threadIdx.x, n = a.T * a.k;
     __shared__ int ids[kMaxEntries];
+    __shared__ float gts[kMaxEntries];
     __shared__ int first[kMaxEntries];
     for (int j = lane; j < n; j += 32) {
       int e = a.ids[j];
@@ -660,16 +675,21 @@ __global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
         e = -1;
       }
       ids[j] = e;
-    }
-    __syncwarp();
-    for (int j = lane; j < n; j += 32) {
-      int f = ids[j] >= 0;
-      for (int i = 0; i < j && f; ++i) f = ids[i] != ids[j];
-      first[j] = f;
+      gts[j] = a.gates[j];
     }
     __syncwarp();
     int count = 0;
-    for (int j = 0; j < n; ++j) count += first[j];
+    for (int base = 0; base < n; base += 32) {
+      const int j = base + lane;
+      int f = 0;
+      if (j < n) {
+        f = ids[j] >= 0;
+        for (int i = 0; i < j && f; ++i) f = ids[i] != ids[j];
+        first[j] = f;
+      }
+      count += __popc(__ballot_sync(0xffffffffu, f));
+    }
+    __syncwarp();
     for (int j = lane; j < n; j += 32) {
       if (!first[j]) continue;
       int rank = 0;
@@ -679,7 +699,7 @@ __global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
         float gt = 0.0f;
         for (int c = 0; c < a.k; ++c)
           if (ids[t * a.k + c] == ids[j]) {
-            gt = a.gates[t * a.k + c];
+            gt = gts[t * a.k + c];
             break;
           }
         a.slot_gate[rank * kMaxT + t] = gt;
