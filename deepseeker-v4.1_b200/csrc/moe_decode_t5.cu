@@ -661,13 +661,16 @@ __global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
   launch_dependents();
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
   if (blockIdx.x == 0 && threadIdx.x < 32) {
-    // distinct valid experts, ascending; one warp, at most 128 entries.
-    // ids and gates go to shared memory first (independent loads), so the
-    // loops below wait on no global load
+    // distinct valid experts, ascending; one warp, at most 128 entries, no
+    // serial scan: a bitmap of the experts present (E <= 1024: 32 words),
+    // a warp scan of its word counts gives every expert's slot, and each
+    // entry writes its gate if it is its token's first slot for that expert
     const int lane = threadIdx.x, n = a.T * a.k;
     __shared__ int ids[kMaxEntries];
-    __shared__ float gts[kMaxEntries];
-    __shared__ int first[kMaxEntries];
+    __shared__ uint32_t present[32];
+    __shared__ int word_base[32];
+    present[lane] = 0u;
+    __syncwarp();
     for (int j = lane; j < n; j += 32) {
       int e = a.ids[j];
       if (e >= a.E) {
@@ -675,35 +678,33 @@ __global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
         e = -1;
       }
       ids[j] = e;
-      gts[j] = a.gates[j];
+      if (e >= 0) atomicOr(&present[e >> 5], 1u << (e & 31));
     }
     __syncwarp();
-    int count = 0;
-    for (int base = 0; base < n; base += 32) {
-      const int j = base + lane;
-      int f = 0;
-      if (j < n) {
-        f = ids[j] >= 0;
-        for (int i = 0; i < j && f; ++i) f = ids[i] != ids[j];
-        first[j] = f;
-      }
-      count += __popc(__ballot_sync(0xffffffffu, f));
+    const uint32_t word = present[lane];
+    int incl = __popc(word);
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += v;
     }
+    word_base[lane] = incl - __popc(word);
+    const int count = __shfl_sync(0xffffffffu, incl, 31);
+    for (uint32_t w = word; w; w &= w - 1) {
+      const int b = __ffs(w) - 1;
+      a.slot_expert[word_base[lane] + __popc(word & ((1u << b) - 1u))] = lane * 32 + b;
+    }
+    for (int q = lane; q < count * a.T; q += 32) a.slot_gate[(q / a.T) * kMaxT + q % a.T] = 0.0f;
     __syncwarp();
     for (int j = lane; j < n; j += 32) {
-      if (!first[j]) continue;
-      int rank = 0;
-      for (int i = 0; i < n; ++i) rank += first[i] && ids[i] < ids[j];
-      a.slot_expert[rank] = ids[j];
-      for (int t = 0; t < a.T; ++t) {
-        float gt = 0.0f;
-        for (int c = 0; c < a.k; ++c)
-          if (ids[t * a.k + c] == ids[j]) {
-            gt = gts[t * a.k + c];
-            break;
-          }
-        a.slot_gate[rank * kMaxT + t] = gt;
-      }
+      const int e = ids[j];
+      if (e < 0) continue;
+      const int t = j / a.k, c = j % a.k;
+      bool first_in_token = true;
+      for (int c2 = 0; c2 < c; ++c2) first_in_token &= ids[t * a.k + c2] != e;
+      if (!first_in_token) continue;
+      const int rank = word_base[e >> 5] + __popc(present[e >> 5] & ((1u << (e & 31)) - 1u));
+      a.slot_gate[rank * kMaxT + t] = a.gates[j];
     }
     if (lane == 0) *a.n_slots = count;
   }
@@ -839,7 +840,7 @@ bool t5_supported(const DecodeArgs& a) {
   if (a.x_f32 || d.w1.format != DS_FMT_FP4 || a.tokens < 1 || a.tokens > kMaxT) return false;
   if (!d.w1.scales_tc || !d.w3.scales_tc || !d.w2.scales_tc) return false;
   if (d.hidden % 1024 != 0 || d.inter % 1024 != 0) return false;
-  if (d.top_k > 16 || a.max_slots > kMaxSlots5) return false;
+  if (d.top_k > 16 || a.max_slots > kMaxSlots5 || d.n_experts > 1024) return false;   // prep's 1024-bit expert map
   if ((uint64_t)d.n_experts * d.inter >= (1ull << 31) || (uint64_t)d.n_experts * d.hidden >= (1ull << 31)) return false;
   const bool sh = d.shared_w1 != nullptr;
   if (sh && (d.shared_inter % 256 != 0)) return false;
