@@ -231,9 +231,12 @@ __device__ void tail_h_routed(const T5Params& p, int slot, int r0, int lane) {
               (size_t)I * kT, KP, g, u);
   uint8_t* hq = p.hq + (size_t)slot * kPieceRows * (I / 2);
   uint8_t* sf = p.sfh + ((size_t)slot * (I / 128) + r0 / 128) * kAtom;
+  float gates[kT];   // the slot's gates, loaded together (uniform over the warp)
+#pragma unroll
+  for (int t = 0; t < kT; ++t) gates[t] = p.slot_gate[slot * kMaxT + t];
 #pragma unroll 1
   for (int t = 0; t < kT; ++t) {
-    const float gate = p.slot_gate[slot * kMaxT + t];   // uniform over the warp
+    const float gate = gates[t];
     if (gate == 0.0f) {
       // a token not routed to this slot: h = 0 exactly, i.e. zero codes in
       // every piece and the scale byte e2m1_scale(0) = 127
