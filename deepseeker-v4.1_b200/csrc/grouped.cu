@@ -253,7 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         for (int kc = 0; kc < KC; ++kc, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          if (!warp_wait(&full[s], ph, abort, p.err) || !warp_wait(&sfready[s], ph, abort, p.err)) goto mma_out;
+          // the stagers arrive on sfready after they have seen the stage's
+          // copies land, so waiting for sfready covers the copies too
+          if (!warp_wait(&sfready[s], ph, abort, p.err)) goto mma_out;
           tc5::fence_after();
           if (elect_one()) {
             const uint64_t ad = ops_desc + (uint64_t)((s * C::kStage) >> 4);

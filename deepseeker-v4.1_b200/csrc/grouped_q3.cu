@@ -463,8 +463,9 @@ __global__ void __launch_bounds__(kQThreads, 1) q3_gemm_kernel(const __grid_cons
         for (int kk = 0; kk < 4; ++kk) idesc[kk] = tc5::idesc_e4m3_e4m3(N, kk);
         for (int kc = 0; kc < KC; ++kc, ++g) {
           const int s = g % S, c = g % kCS;
-          if (!warp_wait(&full[s], (g / S) & 1, abort, p.err) || !warp_wait(&cfull[c], (g / kCS) & 1, abort, p.err))
-            goto mma_out;
+          // the converters arrive on cfull after they have seen the stage's
+          // copies land, so waiting for cfull covers the copies too
+          if (!warp_wait(&cfull[c], (g / kCS) & 1, abort, p.err)) goto mma_out;
           tc5::fence_after();
           const int a = g % NB;
           if (g >= NB) {
