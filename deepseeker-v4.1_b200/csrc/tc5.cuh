@@ -85,6 +85,17 @@ __device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
   return r;
 }
 
+// ue8m0 byte of the block scale that maps a block maximum `amax` into
+// (3, 6], the top of the e2m1 range: 2^(E-2) when the maximum's mantissa is
+// <= 1.5, else 2^(E-1) (E its exponent); zero blocks get scale 1.
+__device__ __forceinline__ int e2m1_block_scale(float amax) {
+  const uint32_t b = __float_as_uint(amax);
+  const int ef = (int)(b >> 23);
+  if (ef == 0) return 127;
+  const int s = (b & 0x7FFFFFu) <= 0x400000u ? ef - 2 : ef - 1;
+  return min(max(s, 1), 253);
+}
+
 // e2m1 pair (bits 0..7) -> two f32 (exact).
 __device__ __forceinline__ void e2m1x2_to_f32x2(uint32_t b, float& lo, float& hi) {
   uint32_t h2;

@@ -58,6 +58,9 @@ SIGNATURES: dict[str, tuple] = {
     "ds_grouped_ffn_workspace_size": (c_int, [POINTER(DsMoeDesc), c_int64, POINTER(c_size_t)]),
     "ds_grouped_ffn": (c_int, [POINTER(DsMoeDesc), c_void_p, c_void_p, c_void_p, c_int, c_int64, c_void_p,
                                c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "ds_grouped_ffn_fp4_workspace_size": (c_int, [POINTER(DsMoeDesc), c_int64, POINTER(c_size_t)]),
+    "ds_grouped_ffn_fp4": (c_int, [POINTER(DsMoeDesc), c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p,
+                                   c_int, c_void_p, c_size_t, c_void_p]),
     "ds_dense_swiglu_workspace_size": (c_int, [c_int64, c_int, POINTER(c_size_t)]),
     "ds_dense_swiglu": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64,
                                 c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_size_t,

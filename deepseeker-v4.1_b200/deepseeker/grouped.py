@@ -117,19 +117,32 @@ class GroupedFFN:
     their re-laid-out scales (same bytes as the bank scales), q3 banks are
     read as stored; plus a workspace."""
 
-    def __init__(self, layer: MoEWeights, top_k: int):
+    def __init__(self, layer: MoEWeights, top_k: int, activations: str = "exact"):
+        """activations="exact": x and h enter the MMAs exactly (the parity
+        mode); "fp4": FP4 banks only, x and h rounded to FP4 with per-32
+        scales (the throughput mode, ds_grouped_ffn_fp4; its result carries
+        that rounding)."""
         if layer.w1.fmt not in (_abi.DS_FMT_FP4, _abi.DS_FMT_Q3):
             raise NotImplementedError("grouped_ffn needs FP4 or q3 expert banks")
+        if activations not in ("exact", "fp4"):
+            raise ValueError('activations must be "exact" or "fp4"')
+        if activations == "fp4":
+            if layer.w1.fmt != _abi.DS_FMT_FP4:
+                raise NotImplementedError("the FP4 activation mode needs FP4 banks")
+            layer.prepare_tc()                     # the mode reads the tensor-core scale atoms
+        self.activations = activations
         self.layer = layer
         self.top_k = top_k
         self._desc = self._routed_desc(top_k)
         a, b = ctypes.c_size_t(0), ctypes.c_size_t(0)
-        _abi.call("ds_grouped_scales_size", ctypes.byref(self._desc), ctypes.byref(a), ctypes.byref(b))
+        if activations == "exact":                 # the FP4 activation mode reads the scale atoms instead
+            _abi.call("ds_grouped_scales_size", ctypes.byref(self._desc), ctypes.byref(a), ctypes.byref(b))
         dev = layer.w1.data.device
         self.w13_sf = torch.empty(a.value, dtype=torch.uint8, device=dev)
         self.w2_sf = torch.empty(b.value, dtype=torch.uint8, device=dev)
-        _abi.call("ds_grouped_prepare_scales", ctypes.byref(self._desc), ptr(self.w13_sf), ptr(self.w2_sf),
-                  stream_handle(dev))
+        if activations == "exact":
+            _abi.call("ds_grouped_prepare_scales", ctypes.byref(self._desc), ptr(self.w13_sf), ptr(self.w2_sf),
+                      stream_handle(dev))
         self._ws: torch.Tensor | None = None
 
     def _routed_desc(self, top_k: int, route_before_down: bool | None = None) -> _abi.DsMoeDesc:
@@ -142,7 +155,8 @@ class GroupedFFN:
 
     def workspace_bytes(self, tokens: int) -> int:
         n = ctypes.c_size_t(0)
-        _abi.call("ds_grouped_ffn_workspace_size", ctypes.byref(self._desc), tokens, ctypes.byref(n))
+        fn = "ds_grouped_ffn_fp4_workspace_size" if self.activations == "fp4" else "ds_grouped_ffn_workspace_size"
+        _abi.call(fn, ctypes.byref(self._desc), tokens, ctypes.byref(n))
         return n.value
 
     def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor,
@@ -165,6 +179,10 @@ class GroupedFFN:
         if out.dtype not in (torch.bfloat16, torch.float32) or out.shape != (T, H) or not out.is_contiguous():
             raise ValueError("out must be a contiguous [T, H] bf16 or f32 tensor")
         odt = _abi.DS_F32 if out.dtype == torch.float32 else _abi.DS_BF16
+        if self.activations == "fp4":
+            _abi.call("ds_grouped_ffn_fp4", ctypes.byref(d), ptr(x), _abi.DS_BF16, T, ptr(topk_ids), ptr(topk_w),
+                      ptr(out), odt, ptr(self._ws), self._ws.numel(), stream_handle(x.device))
+            return out
         _abi.call("ds_grouped_ffn", ctypes.byref(d), ptr(self.w13_sf), ptr(self.w2_sf), ptr(x), _abi.DS_BF16, T,
                   ptr(topk_ids), ptr(topk_w), ptr(out), odt, ptr(self._ws), self._ws.numel(),
                   stream_handle(x.device))

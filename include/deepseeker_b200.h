@@ -251,19 +251,38 @@ int ds_grouped_ffn_workspace_size(const DsMoeDesc* desc, int64_t tokens, size_t*
 
 /* Routed-expert SwiGLU FFN for a batch of tokens (prefill / MTP verify):
  * pairs sorted by expert on the device, gate/up and down projections as
- * tcgen05 block-scaled MMAs (FP4 weights, activations as exact e4m3 pieces),
- * f32 accumulate, combine in top-k order.  Replaces grouped_swiglu and the
- * moe_layer expert loop for FP4 banks (src/deepseeker/grouped.py:34-56,
- * src/deepseeker/mlx_forward.py:388-419).  FP4 banks only, hidden and inter
- * multiples of 128, x bf16 [tokens, hidden], no shared expert (add it
- * separately); topk_ids [tokens, k] (-1 = dropped slot); out [tokens, hidden]
- * of out_dtype (DS_BF16, or DS_F32 for partial sums that are combined later,
- * as the expert-parallel path does).  desc->route_before_down selects where
- * the route weight is applied. */
+ * tcgen05 block-scaled MMAs, f32 accumulate, combine in top-k order.
+ * Replaces grouped_swiglu and the moe_layer expert loop / banked gather
+ * (src/deepseeker/grouped.py:34-56, src/deepseeker/mlx_forward.py:159-210,
+ * 388-419).  FP4 banks: weights as e2m1 operands, activations as exact e4m3
+ * pieces.  Q3 banks: the 3-bit codes become exact e4m3 operands in shared
+ * memory and each 64-group's f16 scale and bias are applied after the MMA
+ * (w13_sf / w2_sf unused, may be null).  Hidden and inter multiples of 128,
+ * x bf16 [tokens, hidden], no shared expert (add it separately); topk_ids
+ * [tokens, k] (-1 = dropped slot); out [tokens, hidden] of out_dtype (DS_BF16,
+ * or DS_F32 for partial sums that are combined later, as the
+ * expert-parallel path does).  desc->route_before_down selects where the
+ * route weight is applied. */
 int ds_grouped_ffn(const DsMoeDesc* desc, const void* w13_sf, const void* w2_sf,
                    const void* x, int x_dtype, int64_t tokens, const int32_t* topk_ids,
                    const float* topk_w, void* out, int out_dtype, void* workspace,
                    size_t workspace_bytes, void* stream);
+
+/* FP4 throughput mode of the grouped FFN: FP4 banks with their scale atoms
+ * (DsExpertBank.scales_tc, ds_fp4_scale_atoms) times activations rounded to
+ * FP4 as well -- x and h become one e2m1 value per element with a per-32
+ * ue8m0 scale that maps the block maximum into (3, 6] -- on tcgen05
+ * kind::mxf4 MMAs (K = 64 per instruction, one MMA per weight byte instead of
+ * one per activation piece).  The result carries the FP4 rounding of x and h
+ * (relative L2 of order 0.1 against the exact layer); it equals, to f32
+ * accumulation order, the layer evaluated on the FP4-rounded x and h.  No
+ * reference counterpart: the reference's grouped path keeps f32 / bf16
+ * activations (src/deepseeker/grouped.py:34-56).  Hidden and inter multiples
+ * of 256; other arguments as ds_grouped_ffn. */
+int ds_grouped_ffn_fp4_workspace_size(const DsMoeDesc* desc, int64_t tokens, size_t* bytes);
+int ds_grouped_ffn_fp4(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens,
+                       const int32_t* topk_ids, const float* topk_w, void* out, int out_dtype,
+                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- dense-weight pair FFN (grouped_swiglu / naive_swiglu with dense experts) */
 
