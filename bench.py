@@ -7,7 +7,8 @@ softmax-renormalised gates from router logits ~ N(0,1), one bf16 shared
 expert (inter 2048), bf16 activations, all experts resident.
 
 One step = router (softmax top-8 over the step's logits) + the fused decode
-layer for one token.  Steps rotate over L distinct resident layer instances
+layer for one token, one routed-decode call (on the tcgen05 kernels the
+first kernel routes).  Steps rotate over L distinct resident layer instances
 (8 x 3.47 GB) with fresh logits each step, so every step streams its 157 MB
 cold from HBM (the working set per step exceeds the 126 MB L2 and the next
 step touches different memory).
@@ -576,7 +577,8 @@ def run_stack(args) -> dict:
             out_buf = body()
     elif world == 1:
         # one graph: for every layer, routing + the decode kernels over
-        # chunks of 8 tokens, ping-pong activation buffers
+        # chunks of 8 tokens (up to 8 tokens: one routed-decode call, whose
+        # tcgen05 prep kernel routes), ping-pong activation buffers
         bufs = [torch.zeros(b, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
         wbuf = torch.empty(b, K_TOP, dtype=torch.float32, device=dev)
         ibuf = torch.empty(b, K_TOP, dtype=torch.int32, device=dev)
@@ -587,6 +589,11 @@ def run_stack(args) -> dict:
             cur = stage_x
             for l, layer in enumerate(layers):
                 nxt = bufs[l % 2]
+                if b <= 8:
+                    moe.moe_decode_routed(cur, layer, stage_l[l], K_TOP, out=nxt, route_out=(wbuf, ibuf),
+                                          workspace=ws)
+                    cur = nxt
+                    continue
                 moe.route_softmax_topk(stage_l[l], K_TOP, out=(wbuf, ibuf))
                 for r0 in range(0, b, 8):
                     r1 = min(b, r0 + 8)
@@ -751,11 +758,13 @@ def run_stack(args) -> dict:
             "e2e": {"value": round(world * b * max(e2e_steps, 1) / (e2e_ms * 1e-3), 2) if e2e_steps else None,
                     "unit": "tokens/s", "h2d_bytes_per_step": b * (H * 2 + NL * E * 4),
                     "d2h_bytes_per_step": b * H * 2},
-            # ours per layer: router + prep/gemm/h/gemm/combine (FP4, tcgen05) or
+            # ours per layer: router + prep/gemm/h/gemm/combine (FP4, tcgen05;
+            # on one GPU the prep kernel routes: no router launch) or
             # gate_up/down/combine (q3), + 2 exchange kernels (peer); above 8
             # tokens on one GPU: router + align/xquant/gemm/gemm/combine
             "gpu_launches": args.steps * sum(
-                1 + ((5 if f == "fp4" else 3) + (2 if peer else 0) if b <= 8 else 5)
+                (5 if (f == "fp4" and not peer) else
+                 1 + (5 if f == "fp4" else 3) + (2 if peer else 0)) if b <= 8 else 1 + 5
                 for f in fmts) if (world == 1 or peer) else None,
             "clocks": clocks,
         }
@@ -1153,14 +1162,15 @@ def run_decode(args) -> dict:
                          "launch_achieved": round(launch_achieved, 1),
                          "launch_frac": round(launch_achieved / pk["hbm_gbs"], 4),
                          "traffic": traffic,
-                         "kernel": "route_topk + ds_moe_decode: " + (
-                             "t5_prep + t5_gemm(gate/up) + t5_h + t5_gemm(down) + t5_combine"
-                             if fmt == "fp4" else "q3_gate_up + q3_down + q3_combine"),
+                         "kernel": ("ds_moe_decode_route: t5_prep (routing, slot list, x pieces) + t5_gemm(gate/up)"
+                                    " + t5_h + t5_gemm(down) + t5_combine" if fmt == "fp4" else
+                                    "route_topk + ds_moe_decode: q3_gate_up + q3_down + q3_combine"),
                          "bytes_per_launch": step_bytes, "peak_kind": kind},
             "e2e": {"value": round(world * tokens * args.steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * (H * 2 + E * 4), "d2h_bytes_per_step": tokens * H * 2},
-            # router + the layer's decode kernels, per step
-            "gpu_launches": (1 + 5 if fmt == "fp4" else 1 + 3) * args.steps,
+            # the layer's decode kernels per step (FP4: the prep kernel routes;
+            # q3: the router launch first)
+            "gpu_launches": (5 if fmt == "fp4" else 1 + 3) * args.steps,
             "clocks": clocks,
         }
     if dist is not None:

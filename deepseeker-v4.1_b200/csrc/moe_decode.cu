@@ -823,9 +823,11 @@ extern "C" int ds_moe_decode_workspace_size(const DsMoeDesc* desc, int64_t token
   return DS_OK;
 }
 
-extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens, const int32_t* topk_ids,
-                             const float* topk_w, void* out, void* workspace, size_t workspace_bytes,
-                             void* stream) {
+namespace {
+
+// Checks shared by ds_moe_decode and ds_moe_decode_route; fills the decode arguments.
+int decode_args(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens, const int32_t* topk_ids,
+                const float* topk_w, void* out, void* workspace, size_t workspace_bytes, DecodeArgs& a) {
   int st = validate(desc, tokens);
   if (st != DS_OK) return st;
   DS_REQUIRE(x && topk_ids && topk_w && out && workspace, DS_EINVAL, "moe_decode: null pointer");
@@ -835,7 +837,6 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
   const WsLayout w = ws_layout(desc, tokens);
   DS_REQUIRE(workspace_bytes >= w.total, DS_EINVAL, "moe_decode: workspace %zu bytes < required %zu",
              workspace_bytes, w.total);
-  DecodeArgs a;
   a.d = *desc;
   a.x = x;
   a.x_f32 = x_dtype == DS_F32;
@@ -847,7 +848,44 @@ extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, 
   a.max_slots = w.max_slots;
   a.h_stride = w.h_stride;
   a.err = reinterpret_cast<int*>(static_cast<char*>(workspace) + w.err_off);
+  return DS_OK;
+}
+
+}  // namespace
+
+extern "C" int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens, const int32_t* topk_ids,
+                             const float* topk_w, void* out, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  DecodeArgs a;
+  const int st = decode_args(desc, x, x_dtype, tokens, topk_ids, topk_w, out, workspace, workspace_bytes, a);
+  if (st != DS_OK) return st;
   return dispatch(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ds_moe_decode_route(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens,
+                                   const float* logits, const float* route_bias, int route_kind, float route_scale,
+                                   int32_t* topk_ids, float* topk_w, void* out, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  DecodeArgs a;
+  int st = decode_args(desc, x, x_dtype, tokens, topk_ids, topk_w, out, workspace, workspace_bytes, a);
+  if (st != DS_OK) return st;
+  DS_REQUIRE(logits != nullptr, DS_EINVAL, "moe_decode_route: null logits");
+  DS_REQUIRE(desc->n_experts <= 1024 && desc->top_k <= 32, DS_EINVAL,
+             "moe_decode_route: n_experts <= 1024 and top_k <= 32 (the router's limits)");
+  DS_REQUIRE(route_kind == DS_ROUTE_SOFTMAX || route_kind == DS_ROUTE_SQRTSOFTPLUS || route_kind == DS_ROUTE_SCORES,
+             DS_EINVAL, "moe_decode_route: unknown route kind %d", route_kind);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (ds::decode::t5_supported(a) && workspace_bytes >= ds::decode::t5_workspace_bytes(a.d, a.tokens)) {
+    a.logits = logits;                 // the tcgen05 prep kernel routes in its own launch
+    a.route_bias = route_bias;
+    a.route_kind = route_kind;
+    a.route_scale = route_scale;
+    return ds::decode::launch_t5(a, workspace, workspace_bytes, s);
+  }
+  st = ds_route_topk(logits, route_bias, tokens, desc->n_experts, desc->top_k, route_kind, route_scale, topk_ids,
+                     topk_w, stream);
+  if (st != DS_OK) return st;
+  return dispatch(a, workspace, workspace_bytes, s);
 }
 
 // ============================================================== qmm host side

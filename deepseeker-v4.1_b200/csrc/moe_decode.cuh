@@ -45,6 +45,12 @@ struct DecodeArgs {
   // slice)
   int sh_w2_ld = 0;
   float* out_sh = nullptr;
+  // tcgen05 path only: route inside the decode (ds_moe_decode_route).  With
+  // logits [T, E] set, ids / gates are outputs the prep kernel writes.
+  const float* logits = nullptr;
+  const float* route_bias = nullptr;
+  int route_kind = DS_ROUTE_SOFTMAX;
+  float route_scale = 1.0f;
 };
 
 // Routed slots of a decode call, built per CTA in shared memory (blockDim >=

@@ -47,6 +47,7 @@
 
 #include "moe_decode.cuh"
 #include "ptx.cuh"
+#include "route.cuh"
 #include "tc5.cuh"
 
 namespace ds {
@@ -648,8 +649,14 @@ __global__ void __launch_bounds__(128) t5_combine_kernel(const __grid_constant__
 
 struct PrepArgs {
   const __nv_bfloat16* x;
-  const int32_t* ids;
-  const float* gates;
+  const int32_t* ids;     // [T, k] routing (written here when the kernel routes)
+  const float* gates;     // [T, k]
+  // routing inside the kernel (template kRoutePer > 0): logits [T, E], the
+  // score bias (or null), the router kind and scale
+  const float* logits;
+  const float* route_bias;
+  int route_kind;
+  float route_scale;
   int T, k, H, E;
   int32_t* n_slots;
   int32_t* slot_expert;   // [kMaxSlots5]
@@ -659,23 +666,50 @@ struct PrepArgs {
   int* err;
 };
 
+// Block 0 builds the slot list; blocks 1.. make the x pieces, in parallel.
+// kRoutePer > 0: block 0 first routes the T tokens itself (warp t routes
+// token t from its logits, ds::route::route_row_warp, with the router
+// kernel's results bit for bit) and writes ids / gates for the caller;
+// 0: it reads the caller's routing.
+template <int kRoutePer>
 __global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
   wait_prior_grid();
   launch_dependents();
-  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
-  if (blockIdx.x == 0 && threadIdx.x < 32) {
+  if (blockIdx.x == 0) {
+    __shared__ int ids[kMaxEntries];
+    __shared__ float gts[kMaxEntries];
+    __shared__ uint32_t present[32];
+    __shared__ int word_base[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, n = a.T * a.k;
+    if constexpr (kRoutePer > 0) {
+      if (warp < a.T) {
+        int e;
+        float g;
+        ds::route::route_row_warp<kRoutePer>(a.logits + (size_t)warp * a.E, a.route_bias, a.E, a.k, a.route_kind,
+                                             a.route_scale, lane, e, g);
+        if (lane < a.k) {
+          ids[warp * a.k + lane] = e;
+          gts[warp * a.k + lane] = g;
+          const_cast<int32_t*>(a.ids)[warp * a.k + lane] = e;
+          const_cast<float*>(a.gates)[warp * a.k + lane] = g;
+        }
+      }
+    } else {
+      for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        ids[j] = a.ids[j];
+        gts[j] = a.gates[j];
+      }
+    }
+    __syncthreads();
+    if (warp != 0) return;
     // distinct valid experts, ascending; one warp, at most 128 entries, no
     // serial scan: a bitmap of the experts present (E <= 1024: 32 words),
     // a warp scan of its word counts gives every expert's slot, and each
     // entry writes its gate if it is its token's first slot for that expert
-    const int lane = threadIdx.x, n = a.T * a.k;
-    __shared__ int ids[kMaxEntries];
-    __shared__ uint32_t present[32];
-    __shared__ int word_base[32];
     present[lane] = 0u;
     __syncwarp();
     for (int j = lane; j < n; j += 32) {
-      int e = a.ids[j];
+      int e = ids[j];
       if (e >= a.E) {
         atomicOr(a.err, kErrExpertRange);
         e = -1;
@@ -707,15 +741,17 @@ __global__ void __launch_bounds__(256) t5_prep_kernel(PrepArgs a) {
       for (int c2 = 0; c2 < c; ++c2) first_in_token &= ids[t * a.k + c2] != e;
       if (!first_in_token) continue;
       const int rank = word_base[e >> 5] + __popc(present[e >> 5] & ((1u << (e & 31)) - 1u));
-      a.slot_gate[rank * kMaxT + t] = a.gates[j];
+      a.slot_gate[rank * kMaxT + t] = gts[j];
     }
     if (lane == 0) *a.n_slots = count;
+    return;
   }
-  // x pieces: 8 threads per (token, 32-block), 4 consecutive elements each
-  // (the block maximum by three xor shuffles inside the aligned 8-lane
-  // group); piece rows t * kPieces + p
+  // x pieces (blocks 1..): 8 threads per (token, 32-block), 4 consecutive
+  // elements each (the block maximum by three xor shuffles inside the
+  // aligned 8-lane group); piece rows t * kPieces + p
   const int nb = a.H / 32;
-  for (int w = tid; w < a.T * nb * 8; w += gridDim.x * blockDim.x) {
+  const int tid = (blockIdx.x - 1) * blockDim.x + threadIdx.x;
+  for (int w = tid; w < a.T * nb * 8; w += (gridDim.x - 1) * blockDim.x) {
     const int grp = w >> 3, sub = w & 7;
     const int t = grp / nb, blk = grp % nb;
     float v[4];
@@ -895,6 +931,10 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   pa.x = static_cast<const __nv_bfloat16*>(a.x);
   pa.ids = a.ids;
   pa.gates = a.gates;
+  pa.logits = a.logits;
+  pa.route_bias = a.route_bias;
+  pa.route_kind = a.route_kind;
+  pa.route_scale = a.route_scale;
   pa.T = T;
   pa.k = d.top_k;
   pa.H = H;
@@ -905,10 +945,19 @@ int launch_t5(const DecodeArgs& a, void* workspace, size_t workspace_bytes, cuda
   pa.xq = xq;
   pa.sfx = sfx;
   pa.err = err;
-  cfg.gridDim = dim3(std::max(1, (T * (H / 4) + 255) / 256));
+  cfg.gridDim = dim3(1 + std::max(1, (T * (H / 4) + 255) / 256));   // slot-list block + piece blocks
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
-  DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel, pa));
+  if (!a.logits) {
+    DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel<0>, pa));
+  } else {
+    const int per = (E + 31) / 32;     // experts per lane of a routing warp (E <= 1024)
+    if (per <= 2) DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel<2>, pa));
+    else if (per <= 4) DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel<4>, pa));
+    else if (per <= 8) DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel<8>, pa));
+    else if (per <= 16) DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel<16>, pa));
+    else DS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, t5_prep_kernel<32>, pa));
+  }
 
   // 2. gate/up
   T5Params p;

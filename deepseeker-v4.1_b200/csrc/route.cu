@@ -14,12 +14,13 @@
 #include <math.h>
 
 #include "ds_common.cuh"
+#include "route.cuh"
 
 namespace {
 
-constexpr int kMaxExperts = 1024;
-constexpr int kMaxTopK = 32;
-constexpr int kRouteThreads = 256;
+using ds::route::kMaxExperts;
+using ds::route::kMaxTopK;
+constexpr int kRouteThreads = ds::route::kRowThreads;
 
 // Block-wide reduction in a fixed order (warp xor tree, then warps 0..7 in
 // order), so every thread gets the same value bit for bit.
@@ -39,15 +40,6 @@ __device__ __forceinline__ float block_reduce(float v, float* red) {
   return r;
 }
 
-// Order-preserving map of a float key to u32 (larger key -> larger code);
-// -0.0 is folded onto +0.0 (they compare equal) and NaN maps to 0, which no
-// valid key takes.
-__device__ __forceinline__ uint32_t key_code(float k) {
-  if (k != k) return 0u;
-  const uint32_t u = __float_as_uint(k + 0.0f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
 // kPer = keys per lane of the selecting warp (n_experts <= 32 * kPer).  The
 // kernel first lets the next kernel on the stream (launched with
 // programmatic stream serialisation) start its prologue; that kernel waits
@@ -65,11 +57,10 @@ route_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bi
   __shared__ uint32_t scode[kMaxExperts];
   __shared__ float sval[kMaxExperts];
   __shared__ float red[kRouteThreads / 32];
-  __shared__ int sel[kMaxTopK];
   const int row = blockIdx.x, tid = threadIdx.x;
   const float* lg = logits + (int64_t)row * n_experts;
   const bool ties_high = (kind != DS_ROUTE_SOFTMAX);
-  constexpr int kPerThread = kMaxExperts / kRouteThreads;
+  constexpr int kPerThread = ds::route::kPerThread;
   float key[kPerThread], val[kPerThread];
   float mx = -INFINITY;
 #pragma unroll
@@ -83,10 +74,7 @@ route_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bi
         val[j] = l;
         mx = fmaxf(mx, l);
       } else {
-        // softplus(l) = logaddexp(l, 0) = max(l, 0) + log1p(exp(-|l|))
-        const float sc = (kind == DS_ROUTE_SCORES) ? l : sqrtf(fmaxf(l, 0.0f) + log1pf(expf(-fabsf(l))));
-        val[j] = sc;
-        key[j] = sc + (bias ? bias[e] : 0.0f);
+        ds::route::score_key(l, kind, bias, e, val[j], key[j]);
       }
     }
   }
@@ -111,49 +99,26 @@ route_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bi
   for (int j = 0; j < kPerThread; ++j) {
     const int e = tid + kRouteThreads * j;
     if (e < n_experts) {
-      scode[e] = key_code(key[j]);
+      scode[e] = ds::route::key_code(key[j]);
       sval[e] = val[j];
     }
   }
   __syncthreads();
   if (tid >= 32) return;
-  // ---- selection, one warp: lane l holds experts l + 32 j as packed
-  // (key code << 32 | tie bits); tie bits order equal keys by the tie rule
+  // ---- selection, one warp: lane l holds experts l + 32 j
   const int lane = tid;
   uint64_t pk[kPer];
+  float vv[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int e = lane + 32 * j;
-    const uint32_t c = e < n_experts ? scode[e] : 0u;
-    const uint32_t tb = ties_high ? (uint32_t)e : (uint32_t)(0xFFFFu - e);
-    pk[j] = c ? (((uint64_t)c << 32) | tb) : 0ull;
+    pk[j] = e < n_experts ? ds::route::pack_key(scode[e], e, ties_high) : 0ull;
+    vv[j] = e < n_experts ? sval[e] : 0.0f;
   }
-  int chosen = -1;
-  for (int r = 0; r < top_k; ++r) {
-    uint64_t best = 0ull;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) best = pk[j] > best ? pk[j] : best;
-    const uint32_t hi = (uint32_t)(best >> 32);
-    const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
-    if (mhi == 0u) break;                                  // no valid key left (warp-uniform)
-    const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? (uint32_t)best : 0u);
-    const int e = ties_high ? (int)mlo : (int)(0xFFFFu - mlo);
-    const int jt = (e & 31) == lane ? (e >> 5) : -1;       // this lane's taken key, if any
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) pk[j] = j == jt ? 0ull : pk[j];
-    if (lane == r) chosen = e;
-  }
-  if (lane < top_k) sel[lane] = chosen;
-  __syncwarp();
+  int chosen;
+  float w;
+  ds::route::select_topk<kPer>(pk, vv, top_k, kind, route_scale, ties_high, lane, chosen, w);
   if (lane < top_k) {
-    float total = 0.0f;                    // chosen values summed in slot order
-    for (int r = 0; r < top_k; ++r)
-      if (sel[r] >= 0) total += sval[sel[r]];
-    float w = 0.0f;
-    if (chosen >= 0) {
-      const float v = sval[chosen];
-      w = (kind == DS_ROUTE_SOFTMAX) ? v / total : (v / (total + 1e-20f)) * route_scale;
-    }
     ids[(int64_t)row * top_k + lane] = chosen;
     weights[(int64_t)row * top_k + lane] = w;
   }

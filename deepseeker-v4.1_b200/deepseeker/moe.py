@@ -256,26 +256,15 @@ def decode_workspace_bytes(weights: MoEWeights, tokens: int, top_k: int) -> int:
     return weights.decode_workspace_bytes(tokens, top_k)
 
 
-def moe_decode(x: torch.Tensor, weights: MoEWeights, topk_ids: torch.Tensor, topk_w: torch.Tensor,
-               out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
-               out_f32: bool = False) -> torch.Tensor:
-    """Fused routed-expert MoE for up to 8 tokens: x [T, H] bf16 (or f32) -> [T, H] of x's dtype.
-
-    topk_ids [T, k] int32 (-1 = dropped slot), topk_w [T, k] f32.  out_f32
-    (bf16 x, FP4 banks with prepared scale atoms): f32 output without the final
-    rounding, for partial sums that are added across ranks.
-    """
+def _decode_call(x: torch.Tensor, weights: MoEWeights, k: int, out: torch.Tensor | None,
+                 workspace: torch.Tensor | None, out_f32: bool):
+    """Checks and arguments shared by moe_decode and moe_decode_routed."""
     x = require_cuda(x, "x", (torch.bfloat16, torch.float32))
     if x.dim() != 2 or x.shape[1] != weights.hidden:
         raise ValueError(f"x must be [T, {weights.hidden}]")
     T = x.shape[0]
     if not 1 <= T <= MAX_DECODE_TOKENS:
         raise ValueError(f"moe_decode handles 1..{MAX_DECODE_TOKENS} tokens, got {T}")
-    topk_ids = require_cuda(topk_ids, "topk_ids", torch.int32)
-    topk_w = require_cuda(topk_w, "topk_w", torch.float32)
-    k = topk_ids.shape[1]
-    if topk_ids.shape != (T, k) or topk_w.shape != (T, k):
-        raise ValueError("topk_ids / topk_w must be [T, k]")
     d = weights.cached_desc(k)
     if (bool(d.route_before_down) != bool(weights.route_before_down)
             or d.swiglu_limit != ctypes.c_float(weights.swiglu_limit or 0.0).value):
@@ -292,9 +281,70 @@ def moe_decode(x: torch.Tensor, weights: MoEWeights, topk_ids: torch.Tensor, top
     elif out.dtype != odt or out.shape != x.shape or not out.is_contiguous():
         raise ValueError(f"out must be a contiguous {tuple(x.shape)} {odt} tensor")
     xdt = _abi.DS_F32 if x.dtype == torch.float32 else _abi.DS_BF16
+    return x, T, d, ws, out, xdt
+
+
+def moe_decode(x: torch.Tensor, weights: MoEWeights, topk_ids: torch.Tensor, topk_w: torch.Tensor,
+               out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+               out_f32: bool = False) -> torch.Tensor:
+    """Fused routed-expert MoE for up to 8 tokens: x [T, H] bf16 (or f32) -> [T, H] of x's dtype.
+
+    topk_ids [T, k] int32 (-1 = dropped slot), topk_w [T, k] f32.  out_f32
+    (bf16 x, FP4 banks with prepared scale atoms): f32 output without the final
+    rounding, for partial sums that are added across ranks.
+    """
+    topk_ids = require_cuda(topk_ids, "topk_ids", torch.int32)
+    topk_w = require_cuda(topk_w, "topk_w", torch.float32)
+    k = topk_ids.shape[1]
+    x, T, d, ws, out, xdt = _decode_call(x, weights, k, out, workspace, out_f32)
+    if topk_ids.shape != (T, k) or topk_w.shape != (T, k):
+        raise ValueError("topk_ids / topk_w must be [T, k]")
     _abi.call("ds_moe_decode", ctypes.byref(d), ptr(x), xdt, T, ptr(topk_ids), ptr(topk_w), ptr(out), ptr(ws),
               ws.numel() * ws.element_size(), stream_handle(x.device))
     return out
+
+
+ROUTE_KINDS = {"softmax": _abi.DS_ROUTE_SOFTMAX, "sqrtsoftplus": _abi.DS_ROUTE_SQRTSOFTPLUS,
+               "scores": _abi.DS_ROUTE_SCORES}
+
+
+def moe_decode_routed(x: torch.Tensor, weights: MoEWeights, logits: torch.Tensor, top_k: int,
+                      kind: str = "softmax", bias: torch.Tensor | None = None, route_scale: float = 1.0,
+                      out: torch.Tensor | None = None,
+                      route_out: tuple[torch.Tensor, torch.Tensor] | None = None,
+                      workspace: torch.Tensor | None = None, out_f32: bool = False
+                      ) -> tuple[torch.Tensor, tuple[torch.Tensor, torch.Tensor]]:
+    """Router + fused decode in one C call (``ds_moe_decode_route``).
+
+    logits [T, E] f32 -> (out [T, H], (weights [T, k] f32, ids [T, k] int32)):
+    the same results as ``route_*`` followed by ``moe_decode``, bit for bit
+    (route_topk / the softmax router, mlx_forward.py:62-81).  On the tcgen05
+    kernels the routing is computed inside the decode's first kernel, one
+    launch fewer per layer.  kind: "softmax" (route_scale unused),
+    "sqrtsoftplus" (scores + bias, the reference's route_topk) or "scores".
+    """
+    if kind not in ROUTE_KINDS:
+        raise ValueError(f"kind must be one of {sorted(ROUTE_KINDS)}")
+    logits = require_cuda(logits, "logits", torch.float32)
+    x, T, d, ws, out, xdt = _decode_call(x, weights, top_k, out, workspace, out_f32)
+    if logits.shape != (T, weights.n_experts) or not logits.is_contiguous():
+        raise ValueError(f"logits must be a contiguous [T, {weights.n_experts}] f32 tensor")
+    if bias is not None:
+        bias = require_cuda(bias.float().contiguous(), "bias")
+        if bias.shape != (weights.n_experts,):
+            raise ValueError(f"bias must be [{weights.n_experts}]")
+    if route_out is not None:
+        w, ids = route_out
+        if (w.shape != (T, top_k) or ids.shape != (T, top_k) or w.dtype != torch.float32
+                or ids.dtype != torch.int32 or not (w.is_contiguous() and ids.is_contiguous())):
+            raise ValueError("route_out must be (weights f32 [T, k], ids int32 [T, k]), contiguous")
+    else:
+        w = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
+        ids = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+    _abi.call("ds_moe_decode_route", ctypes.byref(d), ptr(x), xdt, T, ptr(logits), ptr(bias), ROUTE_KINDS[kind],
+              ctypes.c_float(route_scale), ptr(ids), ptr(w), ptr(out), ptr(ws), ws.numel() * ws.element_size(),
+              stream_handle(x.device))
+    return out, (w, ids)
 
 
 # ------------------------------------------------------------------ qmm (mlx_forward.py:84-156)
@@ -689,8 +739,8 @@ class DecodeGraph:
                 self.out_host.copy_(self.out, non_blocking=True)
 
     def _step(self) -> None:
-        route_softmax_topk(self.logits, self.top_k, out=(self.w, self.ids))
-        moe_decode(self.x, self.weights, self.ids, self.w, out=self.out, workspace=self.workspace)
+        moe_decode_routed(self.x, self.weights, self.logits, self.top_k, out=self.out, route_out=(self.w, self.ids),
+                          workspace=self.workspace)
 
     def replay(self) -> torch.Tensor:
         self.graph.replay()

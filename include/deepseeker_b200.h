@@ -197,6 +197,21 @@ int ds_moe_decode(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tok
                   const int32_t* topk_ids, const float* topk_w, void* out,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* Router + decode layer in one call: ds_route_topk(logits, route_bias, tokens,
+ * n_experts, top_k, route_kind, route_scale) into topk_ids / topk_w (OUTPUTS
+ * here, [tokens, k]), then ds_moe_decode with that routing.  Same results as
+ * the two calls, bit for bit.  On the tcgen05 kernels (FP4 banks with scale
+ * atoms, bf16 x) the routing is computed inside the decode's first kernel
+ * (one launch fewer per layer); otherwise the router runs first.
+ * Replaces route_topk + the moe_layer expert loop
+ *   (src/deepseeker/mlx_forward.py:62-81, 388-419).
+ *   logits [tokens, n_experts] f32, route_bias [n_experts] f32 or NULL;
+ *   n_experts <= 1024, top_k <= 32; workspace as for ds_moe_decode. */
+int ds_moe_decode_route(const DsMoeDesc* desc, const void* x, int x_dtype, int64_t tokens,
+                        const float* logits, const float* route_bias, int route_kind,
+                        float route_scale, int32_t* topk_ids, float* topk_w, void* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 /* One compressed matrix times a batch of activations: out[r, n] =
  * sum_k x[r, k] * W[n, k], W dequantised in registers (exactly: FP4 codes times
  * their ue8m0 scale; Q3 as f32(scale)*q + f32(bias)), f32 accumulate.
