@@ -25,7 +25,8 @@
 // warp-specialised: warp 0 issues TMA loads into a stage ring, warp 1 issues
 // the MMAs (one thread) and owns the tensor memory, warps 2-5 copy the stage's
 // scale atoms from shared memory into tensor memory (tcgen05.st, one warp per
-// lane quarter), warps 6-9 drain the double-buffered accumulators.
+// lane quarter), warps 6-17 drain the double-buffered accumulators (three
+// warps per lane quarter, every third group of 16 token columns).
 // Every wait is bounded; a timeout sets an error bit and an abort flag that
 // makes every other role leave its loop.
 #include <algorithm>
@@ -41,9 +42,11 @@ namespace {
 using namespace ds::ptx;
 
 constexpr int kTileRows = 64;   // token rows per tile (MMA N <= 64)
-constexpr int kWarps = 10;
+constexpr int kEpiPerQ = 3;    // epilogue warps per tensor-memory lane quarter
+constexpr int kEpiWarps = 4 * kEpiPerQ;
+constexpr int kEpiWarp0 = 6;  // warps 2..5 stage scales, 6..17 run the epilogue
+constexpr int kWarps = kEpiWarp0 + kEpiWarps;
 constexpr int kThreads = kWarps * 32;
-constexpr int kEpiWarp0 = 6;  // warps 2..5 stage scales, 6..9 run the epilogue
 constexpr int kSfStage = 4 * kSfAtom;         // scale atoms of one stage
 constexpr int kHPieces = 3, kXPieces = 2;
 constexpr uint32_t kTxBytes = 34816;          // per stage, both modes (see Cfg)
@@ -95,22 +98,35 @@ struct Params {
   int gate_in_h;              // route weight applied to h (before the down projection)
 };
 
+// Route weights of an epilogue warp's token columns (route weight inside h),
+// loaded before the accumulator wait: column (part + kEpiPerQ gi) * 16 + c of
+// the warp's column group gi (0 or 1) is lane gi * 16 + c of the result.
+static_assert(kTileRows <= 2 * 16 * kEpiPerQ, "at most two 16-column groups per epilogue warp");
+__device__ __forceinline__ float route_weights(const Params& p, int N, int row0, int part, int lane) {
+  if (!p.gate_in_h) return 1.0f;
+  const int c = (part + kEpiPerQ * (lane >> 4)) * 16 + (lane & 15);
+  if (c >= N) return 1.0f;
+  const int pr = p.sorted_ids[row0 + c];
+  return pr < p.mk ? p.topk_w[pr] : 0.0f;
+}
+
+// Epilogue of one item, thread = one weight row (lane quarter q, lane); the
+// kEpiPerQ warps of a quarter take every kEpiPerQ-th group of 16 token
+// columns (part).  gate/up: the block maximum of |h| over the warp's 32
+// consecutive intermediate rows by one warp max-reduction of its bits
+// (non-negative floats order as their bits; a NaN counts as 0, as a maximum
+// tree of fmaxf would skip it).
 template <int MODE>
 __device__ __forceinline__ void epilogue(const Params& p, uint32_t dacc, int N, int row0, int tile, int mt, int q,
-                                         int lane) {
+                                         int lane, int part, float wa) {
   if (MODE == GATEUP) {
     const int KC2 = p.I / 128;
     const int i = mt * 128 + q * 32 + lane;  // intermediate index held by this lane
-    for (int n0 = 0; n0 < N; n0 += 16) {
+    for (int n0 = 16 * part, gi = 0; n0 < N; n0 += 16 * kEpiPerQ, ++gi) {
       float gv[16], uv[16];
       tc5::ld_x16_nowait(dacc + n0, gv);
       tc5::ld_x16_nowait(dacc + kTileRows + n0, uv);
       tc5::wait_ld();
-      float wl = 1.0f;
-      if (p.gate_in_h && lane < 16) {
-        const int pr = p.sorted_ids[row0 + n0 + lane];
-        wl = pr < p.mk ? p.topk_w[pr] : 0.0f;
-      }
 #pragma unroll
       for (int j = 0; j < 16; j += 2) {
         float h[2];
@@ -118,11 +134,9 @@ __device__ __forceinline__ void epilogue(const Params& p, uint32_t dacc, int N, 
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           h[c] = silu_glu(gv[j + c], uv[j + c], p.limit);
-          if (p.gate_in_h) h[c] *= __shfl_sync(0xffffffffu, wl, j + c);
-          float a = fabsf(h[c]);
-#pragma unroll
-          for (int d = 16; d; d >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, d));
-          ef[c] = (int)(__float_as_uint(a) >> 23);
+          if (p.gate_in_h) h[c] *= __shfl_sync(0xffffffffu, wa, gi * 16 + j + c);
+          const float a = fabsf(h[c]);
+          ef[c] = (int)(__reduce_max_sync(0xffffffffu, a == a ? __float_as_uint(a) : 0u) >> 23);
         }
         const int n = n0 + j;
         uint8_t* dst0 = p.hq + (size_t)(row0 + n) * kHPieces * p.I + i;
@@ -148,7 +162,7 @@ __device__ __forceinline__ void epilogue(const Params& p, uint32_t dacc, int N, 
     }
   } else {
     const int hrow = mt * 128 + q * 32 + lane;
-    for (int n0 = 0; n0 < N; n0 += 16) {
+    for (int n0 = 16 * part; n0 < N; n0 += 16 * kEpiPerQ) {
       float v[16];
       tc5::ld_x16_nowait(dacc + n0, v);
       tc5::wait_ld();
@@ -182,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accfull[b], 1);
-      mbar_init(&accempty[b], 4);
+      mbar_init(&accempty[b], kEpiWarps);
     }
     mbar_init(&done, 1);
     abort_flag = 0;
@@ -315,15 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   sf_out:;
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
+    const int q = warp & 3, part = (warp - kEpiWarp0) >> 2;
     int li = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
       const int tile = item / MT, mt = item % MT;
       const int4 td = p.tiles[tile];
       const int b = li & 1;
+      const float wa = MODE == GATEUP ? route_weights(p, td.z, td.y, part, lane) : 1.0f;
       if (!warp_wait(&accfull[b], (li >> 1) & 1, abort, p.err)) break;
       tc5::fence_after();
-      epilogue<MODE>(p, tc5::lane_quarter(tb + b * C::kAcc, q), td.z, td.y, tile, mt, q, lane);
+      epilogue<MODE>(p, tc5::lane_quarter(tb + b * C::kAcc, q), td.z, td.y, tile, mt, q, lane, part, wa);
       tc5::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[b]);

@@ -13,15 +13,16 @@
 // src/deepseeker/mlx_forward.py:388-419 with route_before_down; grouped.py:
 // 34-56 without).
 //
-// Launch sequence (one stream): align (tiles of <= 64 rows) -> xquant (each
+// Launch sequence (one stream): align (tiles of <= 96 rows) -> xquant (each
 // padded row's x as packed e2m1 + scale atoms) -> gate/up GEMM (epilogue:
 // SwiGLU, route weight, h as packed e2m1 + scale atoms) -> down GEMM (f32
 // rows) -> combine (grouped.cuh).  GEMM roles per CTA (persistent, one CTA
-// per SM, 320 threads): warp 0 TMA producer (one 128-byte K chunk = 256
+// per SM, 576 threads): warp 0 TMA producer (one 128-byte K chunk = 256
 // codes per stage: weight tiles of 128 rows, the tile's activation rows,
 // six or four scale atoms), warp 1 MMA issuer (an elected lane of a
 // warp-uniform loop), warps 2-5 stage the scale atoms into tensor memory,
-// warps 6-9 drain the double-buffered accumulators.  Every wait is bounded.
+// warps 6-17 drain the double-buffered accumulators (three warps per lane
+// quarter, every third 16-column group).  Every wait is bounded.
 #include <algorithm>
 
 #include "align.cuh"
@@ -34,24 +35,29 @@ namespace {
 
 using namespace ds::ptx;
 
-constexpr int kFR = 64;              // token rows per tile (MMA N <= 64)
-constexpr int kFThreads = 320;       // 10 warps
-constexpr int kFEpi0 = 6;            // warps 6..9: epilogue
+// Token rows per tile (MMA N <= 96): the widest tile whose two accumulator
+// buffers (gate and up: 2 x 96 columns each) and the scale ring (4 stages x 6
+// atoms x 4 columns) fit in the 512 tensor-memory columns of an SM.
+constexpr int kFR = 96;
+constexpr int kFEpiPerQ = 3;         // epilogue warps per tensor-memory lane quarter
+constexpr int kFEpiWarps = 4 * kFEpiPerQ;
+constexpr int kFEpi0 = 6;            // warps 6..17: epilogue
+constexpr int kFThreads = 32 * (kFEpi0 + kFEpiWarps);
 constexpr int kChunkBytes = 16384;   // one weight tile chunk: 128 rows x 128 B (256 codes)
 
 template <int MODE>
 struct FC;
-// gate/up: A = W1 and W3 tiles, B = x (64 rows), atoms: W1 x2, W3 x2, x x2.
+// gate/up: A = W1 and W3 tiles, B = x (kFR rows), atoms: W1 x2, W3 x2, x x2.
 template <>
 struct FC<GATEUP> {
   static constexpr int kMats = 2, kStages = 4, kAtoms = 6;
   static constexpr int kA = kMats * kChunkBytes;            // 32 KB
-  static constexpr int kB = kFR * 128;                      // 8 KB
+  static constexpr int kB = kFR * 128;                      // 12 KB
   static constexpr int kStage = kA + kB;
   static constexpr int kAcc = kMats * kFR;                  // tensor-memory columns per accumulator buffer
   static constexpr int kTmemCols = 512;
 };
-// down: A = W2 tile, B = h (64 rows), atoms: W2 x2, h x2.
+// down: A = W2 tile, B = h (kFR rows), atoms: W2 x2, h x2.
 template <>
 struct FC<DOWN> {
   static constexpr int kMats = 1, kStages = 6, kAtoms = 4;
@@ -59,13 +65,21 @@ struct FC<DOWN> {
   static constexpr int kB = kFR * 128;
   static constexpr int kStage = kA + kB;
   static constexpr int kAcc = kFR;
-  static constexpr int kTmemCols = 256;
+  static constexpr int kTmemCols = 512;
 };
+static_assert(2 * FC<GATEUP>::kAcc + FC<GATEUP>::kStages * FC<GATEUP>::kAtoms * 4 <= FC<GATEUP>::kTmemCols,
+              "gate/up tensor memory");
+static_assert(2 * FC<DOWN>::kAcc + FC<DOWN>::kStages * FC<DOWN>::kAtoms * 4 <= FC<DOWN>::kTmemCols,
+              "down tensor memory");
+static_assert(kFR % 16 == 0 && kFR <= 128, "tile rows: a multiple of 16 within one scale atom");
+static_assert(FC<GATEUP>::kStage % 1024 == 0 && FC<DOWN>::kStage % 1024 == 0 && FC<GATEUP>::kA % 1024 == 0,
+              "128-byte swizzled tiles start on 1024-byte boundaries");
 
 template <int MODE>
 constexpr size_t f_smem() {
   return 1024 + (size_t)FC<MODE>::kStages * (FC<MODE>::kStage + FC<MODE>::kAtoms * kSfAtom);
 }
+static_assert(f_smem<GATEUP>() <= 225 * 1024 && f_smem<DOWN>() <= 225 * 1024, "dynamic shared memory");
 
 struct FParams {
   CUtensorMap a0, a1, b;      // packed FP4 weights (gate/up: W1, W3; down: W2), packed activations
@@ -142,33 +156,42 @@ __global__ void __launch_bounds__(256) fp4x_quant_kernel(const __nv_bfloat16* __
 }
 
 // Epilogue of one item (tile x 128 weight rows), thread = one weight row
-// (lane quarter q, lane).  gate/up: the 32 lanes are 32 consecutive
+// (lane quarter q, lane); the kFEpiPerQ warps of a quarter take every
+// kFEpiPerQ-th group of 16 token columns (part = 0 .. kFEpiPerQ - 1).  gate/up: the 32 lanes are 32 consecutive
 // intermediate rows = one 32-block of the down projection's K, so h of each
-// token is quantised to e2m1 across the warp.
+// token is quantised to e2m1 across the warp (block maximum by one warp
+// max-reduction of |h|'s bits: non-negative floats order as their bits; a
+// NaN counts as 0, as a maximum tree of fmaxf would skip it).
+// Route weights of an epilogue warp's token columns (route weight inside h),
+// loaded before the accumulator wait: column (part + kFEpiPerQ gi) * 16 + c
+// of the warp's group gi (0 or 1) is lane gi * 16 + c of the result.
+static_assert(kFR <= 2 * 16 * kFEpiPerQ, "at most two 16-column groups per epilogue warp");
+__device__ __forceinline__ float f_route_weights(const FParams& p, int N, int row0, int part, int lane) {
+  if (!p.gate_in_h) return 1.0f;
+  const int c = (part + kFEpiPerQ * (lane >> 4)) * 16 + (lane & 15);
+  if (c >= N) return 1.0f;
+  const int pr = p.sorted_ids[row0 + c];
+  return pr < p.mk ? p.topk_w[pr] : 0.0f;
+}
+
 template <int MODE>
 __device__ __forceinline__ void f_epilogue(const FParams& p, uint32_t dacc, int N, int row0, int tile, int mt, int q,
-                                           int lane) {
+                                           int lane, int part, float wa) {
   if (MODE == GATEUP) {
     const int I = p.I;
     const int i = mt * 128 + q * 32 + lane;
     uint8_t* sf = p.sfh + ((size_t)tile * (I / 128) + mt) * kSfAtom;
-    for (int n0 = 0; n0 < N; n0 += 16) {
+    for (int n0 = 16 * part, gi = 0; n0 < N; n0 += 16 * kFEpiPerQ, ++gi) {
       float gv[16], uv[16];
       tc5::ld_x16_nowait(dacc + n0, gv);
       tc5::ld_x16_nowait(dacc + kFR + n0, uv);
       tc5::wait_ld();
-      float wl = 1.0f;
-      if (p.gate_in_h && lane < 16) {
-        const int pr = p.sorted_ids[row0 + n0 + lane];
-        wl = pr < p.mk ? p.topk_w[pr] : 0.0f;
-      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         float h = silu_glu(gv[j], uv[j], p.limit);
-        if (p.gate_in_h) h *= __shfl_sync(0xffffffffu, wl, j);
-        float am = fabsf(h);
-#pragma unroll
-        for (int d = 16; d; d >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, d));
+        if (p.gate_in_h) h *= __shfl_sync(0xffffffffu, wa, gi * 16 + j);
+        const float ah = fabsf(h);
+        const float am = __uint_as_float(__reduce_max_sync(0xffffffffu, ah == ah ? __float_as_uint(ah) : 0u));
         const int sc = tc5::e2m1_block_scale(am);
         const uint32_t code = tc5::f32x2_to_e2m1x2(h * inv_scale_of(sc), 0.0f) & 0xFu;
         const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
@@ -178,7 +201,7 @@ __device__ __forceinline__ void f_epilogue(const FParams& p, uint32_t dacc, int 
     }
   } else {
     const int hrow = mt * 128 + q * 32 + lane;
-    for (int n0 = 0; n0 < N; n0 += 16) {
+    for (int n0 = 16 * part; n0 < N; n0 += 16 * kFEpiPerQ) {
       float v[16];
       tc5::ld_x16_nowait(dacc + n0, v);
       tc5::wait_ld();
@@ -213,7 +236,7 @@ __global__ void __launch_bounds__(kFThreads, 1) fp4_gemm_kernel(const __grid_con
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accfull[b], 1);
-      mbar_init(&accempty[b], 4);
+      mbar_init(&accempty[b], kFEpiWarps);
     }
     mbar_init(&done, 1);
     abort_flag = 0;
@@ -330,15 +353,16 @@ __global__ void __launch_bounds__(kFThreads, 1) fp4_gemm_kernel(const __grid_con
   sf_out:;
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
+    const int q = warp & 3, part = (warp - kFEpi0) >> 2;
     int li = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
       const int tile = item / MT, mt = item % MT;
       const int4 td = p.tiles[tile];
       const int b = li & 1;
+      const float wa = MODE == GATEUP ? f_route_weights(p, td.z, td.y, part, lane) : 1.0f;
       if (!warp_wait(&accfull[b], (li >> 1) & 1, abort, p.err)) break;
       tc5::fence_after();
-      f_epilogue<MODE>(p, tc5::lane_quarter(tb + b * C::kAcc, q), td.z, td.y, tile, mt, q, lane);
+      f_epilogue<MODE>(p, tc5::lane_quarter(tb + b * C::kAcc, q), td.z, td.y, tile, mt, q, lane, part, wa);
       tc5::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[b]);
