@@ -252,9 +252,11 @@ __device__ void tail_h_routed(const T5Params& p, int slot, int r0, int lane) {
     float r = silu_glu(g[t], u[t], p.limit) * gate;
 #pragma unroll 1
     for (int pc = 0; pc < kPieces; ++pc) {
-      float am = fabsf(r);
-#pragma unroll
-      for (int d = 16; d; d >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, d));
+      // block maximum of |r| over the warp's 32 rows: one max-reduction of
+      // the bits (non-negative floats order as their bits; NaN counts as 0,
+      // as a maximum tree of fmaxf would skip it)
+      const float ar = fabsf(r);
+      const float am = __uint_as_float(__reduce_max_sync(0xffffffffu, ar == ar ? __float_as_uint(ar) : 0u));
       const int sc = e2m1_scale(am);
       const uint32_t code = tc5::f32x2_to_e2m1x2(r * inv_scale_of(sc), 0.0f) & 0xFu;
       float q0, q1;
