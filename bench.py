@@ -257,6 +257,7 @@ def time_reference(steps: int, warmup: int, budget_s: float | None = None) -> tu
 # ------------------------------------------------------------------ our arm
 
 def run_ours(args) -> dict:
+    import numpy as np
     if args.config == "c4":
         return run_grouped(args)
     if args.config == "c5":
@@ -409,14 +410,21 @@ def run_ep(args) -> dict:
     pin_o = torch.empty(b, H, dtype=torch.bfloat16).pin_memory()
     dx = torch.empty(b, H, dtype=torch.bfloat16, device=dev)
     dl = torch.empty(b, E, dtype=torch.float32, device=dev)
+    # numpy views of the pinned buffers (bf16 as int16): a step's input lands
+    # in the graph's staging buffers by a plain memory copy
+    np_x, np_l, np_o = pin_x.view(torch.int16).numpy(), pin_l.numpy(), pin_o.view(torch.int16).numpy()
+    np_io = [(g_.x_host.view(torch.int16).numpy(), g_.logits_host.numpy(), g_.out_host.view(torch.int16).numpy())
+             for g_ in graphs] if graphs is not None else None
 
     def e2e_step(s_):
         if graphs is not None:
-            # host in -> one graph launch (copies, router, exchange, decode) -> host out
+            # host in -> one graph launch (staging, router, exchange, decode) -> host out
             gr = graphs[s_ % L]
-            gr.x_host.copy_(pin_x[s_])
-            gr.logits_host.copy_(pin_l[s_])
-            pin_o.copy_(gr.replay_host())
+            xv, lv, ov = np_io[s_ % L]
+            np.copyto(xv, np_x[s_])
+            np.copyto(lv, np_l[s_])
+            gr.replay_host()
+            np.copyto(np_o, ov)
             return
         else:
             dx.copy_(pin_x[s_], non_blocking=True)
@@ -944,6 +952,7 @@ def run_grouped(args) -> dict:
 
 
 def run_decode(args) -> dict:
+    import numpy as np
     import torch
 
     from deepseeker import moe, synthetic
@@ -1085,13 +1094,22 @@ def run_decode(args) -> dict:
     dl = torch.empty(tokens, E, dtype=torch.float32, device=dev)
     do = torch.empty(tokens, H, dtype=torch.bfloat16, device=dev)
 
+    # numpy views of the pinned buffers (bf16 as int16): a step's input lands
+    # in the graph's staging buffers by a plain memory copy
+    np_x, np_l, np_o = pin_x.view(torch.int16).numpy(), pin_l.numpy(), pin_o.view(torch.int16).numpy()
+    np_io = [(g_.x_host.view(torch.int16).numpy(), g_.logits_host.numpy(), g_.out_host.view(torch.int16).numpy())
+             for g_ in graphs] if use_graph else None
+
     def e2e_step(s):
         if use_graph:
-            # host in -> one graph launch (H2D copies, router, decode, D2H copy) -> host out
+            # host in -> one graph launch (staging kernel, routed decode, staging
+            # kernel) -> host out
             gr = graphs[s % L]
-            gr.x_host.copy_(pin_x[s])
-            gr.logits_host.copy_(pin_l[s])
-            pin_o[s].copy_(gr.replay_host())
+            xv, lv, ov = np_io[s % L]
+            np.copyto(xv, np_x[s])
+            np.copyto(lv, np_l[s])
+            gr.replay_host()
+            np.copyto(np_o[s], ov)
             return
         else:
             dx.copy_(pin_x[s], non_blocking=True)

@@ -51,6 +51,8 @@ SIGNATURES: dict[str, tuple] = {
     "ds_moe_decode_route": (c_int, [POINTER(DsMoeDesc), c_void_p, c_int, c_int64, c_void_p, c_void_p, c_int,
                                     c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "ds_qmm": (c_int, [POINTER(DsExpertBank), c_void_p, c_int, c_int64, c_void_p, c_void_p]),
+    "ds_host_device_pointer": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "ds_copy_ranges": (c_int, [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_size_t), c_void_p]),
     "ds_moe_align_capacity": (c_int, [c_int64, c_int, c_int, c_int, POINTER(c_int64), POINTER(c_int64)]),
     "ds_moe_align": (c_int, [c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_int64, c_void_p, c_int64,
                              c_void_p, c_void_p]),

@@ -534,12 +534,16 @@ class PeerDecodeGraph:
         with torch.cuda.graph(self.graph):
             self._step()
         if host_io:
+            # staging by one small kernel each way (moe.copy_ranges), not by
+            # copy-engine transfers: the inputs and output are a few KB
+            stage_in = [(self.x.data_ptr(), moe.host_device_pointer(self.x_host), moe._nbytes(self.x)),
+                        (self.logits.data_ptr(), moe.host_device_pointer(self.logits_host), moe._nbytes(self.logits))]
+            stage_out = [(moe.host_device_pointer(self.out_host), self.out.data_ptr(), moe._nbytes(self.out))]
             self.graph_host = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graph_host):
-                self.x.copy_(self.x_host, non_blocking=True)
-                self.logits.copy_(self.logits_host, non_blocking=True)
+                moe.copy_ranges(stage_in, dev)
                 self._step()
-                self.out_host.copy_(self.out, non_blocking=True)
+                moe.copy_ranges(stage_out, dev)
 
     def _step(self) -> None:
         self._route()

@@ -684,13 +684,47 @@ def _static_input(t: torch.Tensor | None, shape, dtype, device, name: str) -> to
     return t
 
 
+_WAIT_EVENTS: dict = {}
+
+
 def wait_stream(device) -> None:
     """Wait for the current stream by polling an event (a decode step is tens
-    of microseconds: a blocking synchronisation adds its own wake-up time)."""
-    ev = torch.cuda.Event()
+    of microseconds: a blocking synchronisation adds its own wake-up time).
+    One event per device is reused."""
+    device = torch.device(device)
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    ev = _WAIT_EVENTS.get(key)
+    if ev is None:
+        ev = _WAIT_EVENTS[key] = torch.cuda.Event()
     ev.record(torch.cuda.current_stream(device))
     while not ev.query():
         pass
+
+
+def host_device_pointer(t: torch.Tensor) -> int:
+    """Device address of a pinned host tensor's storage (``ds_host_device_pointer``)."""
+    if t.is_cuda or not t.is_pinned():
+        raise ValueError("host_device_pointer needs a pinned host tensor")
+    d = ctypes.c_void_p(0)
+    _abi.call("ds_host_device_pointer", ctypes.c_void_p(t.data_ptr()), ctypes.byref(d))
+    return int(d.value)
+
+
+def copy_ranges(ranges: list[tuple[int, int, int]], device) -> None:
+    """``ds_copy_ranges`` on the device's current stream: (dst, src, bytes)
+    device addresses (pinned host memory through ``host_device_pointer``),
+    up to four ranges in one launch.  A host-fed decode step stages its
+    inputs and output with it instead of copy-engine transfers, whose
+    per-copy latency dominates moves of a few kilobytes."""
+    n = len(ranges)
+    dst = (ctypes.c_void_p * n)(*[r[0] for r in ranges])
+    src = (ctypes.c_void_p * n)(*[r[1] for r in ranges])
+    nb = (ctypes.c_size_t * n)(*[r[2] for r in ranges])
+    _abi.call("ds_copy_ranges", n, dst, src, nb, stream_handle(torch.device(device)))
+
+
+def _nbytes(t: torch.Tensor) -> int:
+    return t.numel() * t.element_size()
 
 
 class DecodeGraph:
@@ -731,12 +765,16 @@ class DecodeGraph:
         with torch.cuda.graph(self.graph):
             self._step()
         if host_io:
+            # staging by one small kernel each way (copy_ranges), not by
+            # copy-engine transfers: the inputs and output are a few KB
+            stage_in = [(self.x.data_ptr(), host_device_pointer(self.x_host), _nbytes(self.x)),
+                        (self.logits.data_ptr(), host_device_pointer(self.logits_host), _nbytes(self.logits))]
+            stage_out = [(host_device_pointer(self.out_host), self.out.data_ptr(), _nbytes(self.out))]
             self.graph_host = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graph_host):
-                self.x.copy_(self.x_host, non_blocking=True)
-                self.logits.copy_(self.logits_host, non_blocking=True)
+                copy_ranges(stage_in, device)
                 self._step()
-                self.out_host.copy_(self.out, non_blocking=True)
+                copy_ranges(stage_out, device)
 
     def _step(self) -> None:
         moe_decode_routed(self.x, self.weights, self.logits, self.top_k, out=self.out, route_out=(self.w, self.ids),

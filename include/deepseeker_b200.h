@@ -222,6 +222,22 @@ int ds_moe_decode_route(const DsMoeDesc* desc, const void* x, int x_dtype, int64
  *   out : [rows, N] f32.  K <= 6144 (eight x rows staged in shared memory). */
 int ds_qmm(const DsExpertBank* w, const void* x, int x_dtype, int64_t rows, float* out, void* stream);
 
+/* ---- host-fed decode steps: staging without the copy engines ------------ */
+
+/* Device address of pinned host memory (cudaHostGetDevicePointer).  DS_EINVAL
+ * when the memory is not pinned and mapped.  No reference counterpart: the
+ * reference's MLX arrays live in unified memory. */
+int ds_host_device_pointer(const void* host, void** device);
+
+/* Copies n (1..4) byte ranges dst[k] <- src[k] in one kernel launch on
+ * `stream`.  Pointers are device addresses (device memory, or pinned host
+ * memory through ds_host_device_pointer), 16-byte aligned; bytes[k] is a
+ * multiple of 16.  A host-fed decode step stages its inputs in and its
+ * output out with it: a copy-engine transfer of a few kilobytes costs
+ * several microseconds of latency on the step's critical path, this one
+ * launch about as much as one.  No reference counterpart (see above). */
+int ds_copy_ranges(int n, void* const* dst, const void* const* src, const size_t* bytes, void* stream);
+
 /* ---- sort-and-pad of routed pairs by expert ---------------------------- */
 
 /* Output capacities ds_moe_align needs for topk_ids [m, k] over n_experts:
