@@ -38,6 +38,8 @@ import sys
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 
 
@@ -257,7 +259,6 @@ def time_reference(steps: int, warmup: int, budget_s: float | None = None) -> tu
 # ------------------------------------------------------------------ our arm
 
 def run_ours(args) -> dict:
-    import numpy as np
     if args.config == "c4":
         return run_grouped(args)
     if args.config == "c5":
@@ -952,7 +953,6 @@ def run_grouped(args) -> dict:
 
 
 def run_decode(args) -> dict:
-    import numpy as np
     import torch
 
     from deepseeker import moe, synthetic
