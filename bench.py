@@ -582,7 +582,7 @@ def run_stack(args) -> dict:
         out_buf = body()                          # eager once: workspaces, attributes
         torch.cuda.synchronize(dev)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with moe.graph_capture(graph):
             out_buf = body()
     elif world == 1:
         # one graph: for every layer, routing + the decode kernels over
@@ -612,7 +612,7 @@ def run_stack(args) -> dict:
         out_buf = body()                          # eager once: attributes, caches
         torch.cuda.synchronize(dev)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with moe.graph_capture(graph):
             out_buf = body()
     elif peer:
         comm = ep.PeerComm(b, H, K_TOP, timeout_ms=30000)
@@ -622,7 +622,7 @@ def run_stack(args) -> dict:
             pgs.append(ep.PeerDecodeGraph(pl, x=stage_x if l == 0 else pgs[-1].out, logits=stage_l[l]))
         torch.cuda.synchronize(dev)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with moe.graph_capture(graph):
             for pg in pgs:
                 pg._step()
         out_buf = pgs[-1].out
@@ -1184,7 +1184,8 @@ def run_decode(args) -> dict:
                                     " + t5_h + t5_gemm(down) + t5_combine" if fmt == "fp4" else
                                     "route_topk + ds_moe_decode: q3_gate_up + q3_down + q3_combine"),
                          "bytes_per_launch": step_bytes, "peak_kind": kind},
-            "e2e": {"value": round(world * tokens * args.steps / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+            "e2e": {"value": round(world * tokens * e2e_steps / (e2e_ms * 1e-3), 2) if e2e_steps else None,
+                    "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * (H * 2 + E * 4), "d2h_bytes_per_step": tokens * H * 2},
             # the layer's decode kernels per step (FP4: the prep kernel routes;
             # q3: the router launch first)

@@ -527,11 +527,10 @@ class PeerDecodeGraph:
         self.w = torch.empty(b, k, dtype=torch.float32, device=dev)
         self.ids = torch.empty(b, k, dtype=torch.int32, device=dev)
         self.out = torch.empty(b, H, dtype=torch.bfloat16, device=dev)
-        self._route = lambda: moe.route_softmax_topk(self.logits, k, out=(self.w, self.ids))
         self._step()                      # eager once on every rank (the exchange pairs up)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+        with moe.graph_capture(self.graph):
             self._step()
         if host_io:
             # staging by one small kernel each way (moe.copy_ranges), not by
@@ -540,13 +539,15 @@ class PeerDecodeGraph:
                         (self.logits.data_ptr(), moe.host_device_pointer(self.logits_host), moe._nbytes(self.logits))]
             stage_out = [(moe.host_device_pointer(self.out_host), self.out.data_ptr(), moe._nbytes(self.out))]
             self.graph_host = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.graph_host):
+            with moe.graph_capture(self.graph_host):
                 moe.copy_ranges(stage_in, dev)
                 self._step()
                 moe.copy_ranges(stage_out, dev)
 
     def _step(self) -> None:
-        self._route()
+        from . import moe
+
+        moe.route_softmax_topk(self.logits, self.layer.top_k, out=(self.w, self.ids))
         self.layer(self.x, self.ids, self.w, out=self.out)
 
     def replay(self) -> torch.Tensor:

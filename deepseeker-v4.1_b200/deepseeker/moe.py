@@ -24,7 +24,9 @@ Semantics kept from the reference:
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import gc
 from dataclasses import dataclass, field
 
 import torch
@@ -687,6 +689,23 @@ def _static_input(t: torch.Tensor | None, shape, dtype, device, name: str) -> to
 _WAIT_EVENTS: dict = {}
 
 
+@contextlib.contextmanager
+def graph_capture(graph: torch.cuda.CUDAGraph):
+    """``torch.cuda.graph(graph)`` with unreachable Python objects collected
+    first and the cycle collector paused during the capture: a collection
+    inside the capture could finalize an unreachable object that owns a CUDA
+    graph or event, and those calls invalidate a capture."""
+    gc.collect()
+    was_enabled = gc.isenabled()
+    gc.disable()
+    try:
+        with torch.cuda.graph(graph):
+            yield
+    finally:
+        if was_enabled:
+            gc.enable()
+
+
 def wait_stream(device) -> None:
     """Wait for the current stream by polling an event (a decode step is tens
     of microseconds: a blocking synchronisation adds its own wake-up time).
@@ -762,7 +781,7 @@ class DecodeGraph:
         self._step()                      # first call outside the capture: module load, attributes, caches
         torch.cuda.synchronize(device)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+        with graph_capture(self.graph):
             self._step()
         if host_io:
             # staging by one small kernel each way (copy_ranges), not by
@@ -771,7 +790,7 @@ class DecodeGraph:
                         (self.logits.data_ptr(), host_device_pointer(self.logits_host), _nbytes(self.logits))]
             stage_out = [(host_device_pointer(self.out_host), self.out.data_ptr(), _nbytes(self.out))]
             self.graph_host = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.graph_host):
+            with graph_capture(self.graph_host):
                 copy_ranges(stage_in, device)
                 self._step()
                 copy_ranges(stage_out, device)
@@ -824,7 +843,7 @@ class GraphChain:
             self.logits = torch.zeros((n,) + tuple(l0.shape), dtype=l0.dtype, device=l0.device)
         torch.cuda.synchronize(x0.device)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+        with graph_capture(self.graph):
             for i, layer in enumerate(self.layers):
                 if not in_place:
                     layer.x.copy_(self.x[i])
