@@ -324,11 +324,19 @@ def moe_decode_routed(x: torch.Tensor, weights: MoEWeights, logits: torch.Tensor
     kernels the routing is computed inside the decode's first kernel, one
     launch fewer per layer.  kind: "softmax" (route_scale unused),
     "sqrtsoftplus" (scores + bias, the reference's route_topk) or "scores".
+    ``out`` may be a pinned host tensor: the layer then writes its output
+    rows straight into it through its device mapping (read it after the
+    stream has been waited for).
     """
     if kind not in ROUTE_KINDS:
         raise ValueError(f"kind must be one of {sorted(ROUTE_KINDS)}")
     logits = require_cuda(logits, "logits", torch.float32)
+    out_addr = None
+    if out is not None and not out.is_cuda:
+        out_addr = host_device_pointer(out)          # ValueError unless pinned and mapped
     x, T, d, ws, out, xdt = _decode_call(x, weights, top_k, out, workspace, out_f32)
+    if out_addr is None:
+        out_addr = out.data_ptr()
     if logits.shape != (T, weights.n_experts) or not logits.is_contiguous():
         raise ValueError(f"logits must be a contiguous [T, {weights.n_experts}] f32 tensor")
     if bias is not None:
@@ -344,8 +352,8 @@ def moe_decode_routed(x: torch.Tensor, weights: MoEWeights, logits: torch.Tensor
         w = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
         ids = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
     _abi.call("ds_moe_decode_route", ctypes.byref(d), ptr(x), xdt, T, ptr(logits), ptr(bias), ROUTE_KINDS[kind],
-              ctypes.c_float(route_scale), ptr(ids), ptr(w), ptr(out), ptr(ws), ws.numel() * ws.element_size(),
-              stream_handle(x.device))
+              ctypes.c_float(route_scale), ptr(ids), ptr(w), ctypes.c_void_p(out_addr), ptr(ws),
+              ws.numel() * ws.element_size(), stream_handle(x.device))
     return out, (w, ids)
 
 
@@ -784,16 +792,16 @@ class DecodeGraph:
         with graph_capture(self.graph):
             self._step()
         if host_io:
-            # staging by one small kernel each way (copy_ranges), not by
-            # copy-engine transfers: the inputs and output are a few KB
+            # inputs staged by one small kernel (copy_ranges), not by
+            # copy-engine transfers (they are a few KB); the layer writes its
+            # output rows straight into out_host through its device mapping
             stage_in = [(self.x.data_ptr(), host_device_pointer(self.x_host), _nbytes(self.x)),
                         (self.logits.data_ptr(), host_device_pointer(self.logits_host), _nbytes(self.logits))]
-            stage_out = [(host_device_pointer(self.out_host), self.out.data_ptr(), _nbytes(self.out))]
             self.graph_host = torch.cuda.CUDAGraph()
             with graph_capture(self.graph_host):
                 copy_ranges(stage_in, device)
-                self._step()
-                copy_ranges(stage_out, device)
+                moe_decode_routed(self.x, self.weights, self.logits, self.top_k, out=self.out_host,
+                                  route_out=(self.w, self.ids), workspace=self.workspace)
 
     def _step(self) -> None:
         moe_decode_routed(self.x, self.weights, self.logits, self.top_k, out=self.out, route_out=(self.w, self.ids),

@@ -65,16 +65,34 @@ def test_graph_chain_rejects_foreign_buffers(cuda):
                        logits=torch.zeros(1, 1, 16, device=cuda))
 
 
-def test_graph_host_io_matches_eager(cuda):
-    """host_io: pinned host in, one graph launch (copies inside), pinned host out."""
-    layer = synthetic.make_layer("fp4", 4096, 2048, 64, seed=35, shared_inter=2048, device=cuda).prepare_tc()
-    g = moe.DecodeGraph(layer, 1, 8, host_io=True)
+@pytest.mark.parametrize("fmt,atoms,T", [("fp4", True, 1), ("fp4", True, 3), ("fp4", False, 1), ("q3", False, 2)])
+def test_graph_host_io_matches_eager(fmt, atoms, T, cuda):
+    """host_io: pinned host in (staging kernel), one graph launch, the layer's
+    output rows written straight into pinned host memory; every decode path
+    (tcgen05, single-token register dequant, q3) gives the device path's bits."""
+    layer = synthetic.make_layer(fmt, 4096, 2048, 64, seed=35, shared_inter=2048, device=cuda)
+    if atoms:
+        layer.prepare_tc()
+    g = moe.DecodeGraph(layer, T, 8, host_io=True)
     for step in range(3):
-        x = torch.randn(1, 4096).to(torch.bfloat16)
-        logits = torch.randn(1, 64)
+        x = torch.randn(T, 4096).to(torch.bfloat16)
+        logits = torch.randn(T, 64)
         g.x_host.copy_(x)
         g.logits_host.copy_(logits)
         got = g.replay_host().clone()
         w, ids = moe.route_softmax_topk(logits.to(cuda), 8)
         ref = moe.moe_decode(x.to(cuda), layer, ids, w).cpu()
         assert torch.equal(got, ref), step
+
+
+def test_routed_call_writes_pinned_host_output(cuda):
+    layer = synthetic.make_layer("fp4", 4096, 2048, 64, seed=36, shared_inter=2048, device=cuda).prepare_tc()
+    x = torch.randn(2, 4096, device=cuda).to(torch.bfloat16)
+    logits = torch.randn(2, 64, device=cuda)
+    ref, _ = moe.moe_decode_routed(x, layer, logits, 8)
+    host = torch.zeros(2, 4096, dtype=torch.bfloat16).pin_memory()
+    out, _ = moe.moe_decode_routed(x, layer, logits, 8, out=host)
+    moe.wait_stream(cuda)
+    assert out is host and torch.equal(host, ref.cpu())
+    with pytest.raises(ValueError):                 # pageable memory has no device mapping
+        moe.moe_decode_routed(x, layer, logits, 8, out=torch.zeros(2, 4096, dtype=torch.bfloat16))
