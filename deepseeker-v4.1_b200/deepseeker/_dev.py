@@ -39,7 +39,10 @@ def to_device(a, device: torch.device | None = None, dtype: torch.dtype | None =
     if isinstance(a, (bytes, bytearray, memoryview)):
         a = np.frombuffer(a, dtype=np.uint8)
     if isinstance(a, np.ndarray):
-        t = torch.from_numpy(np.ascontiguousarray(a))
+        a = np.ascontiguousarray(a)
+        if not a.flags.writeable:    # torch wants writable storage; the data is copied to the device anyway
+            a = a.copy()
+        t = torch.from_numpy(a)
     else:
         t = a
     if dtype is not None and t.dtype != dtype:
